@@ -1,0 +1,284 @@
+/*
+ * sam3cuda.h - C ABI of libsam3cuda: the SAM3 image-encoder hot path on
+ * NVIDIA B200 (sm_100a).
+ *
+ * The path: uint8-palette (256-entry LUT per output channel) weights expanded
+ * on chip into fp16 tensor-core GEMMs (QKV, attention out-projection, MLP
+ * fc1/fc2) with fused epilogues (bias, 2D axial RoPE, exact GELU, residual),
+ * global softmax attention, LayerNorm, patch embedding and the L2/L1 token
+ * pruning top-k + gather.
+ *
+ * Conventions
+ *  - Every entry point returns sam3_status_t; nothing aborts or throws.
+ *    A failing call leaves a message readable with sam3_last_error(ctx).
+ *  - fp16 tensors are IEEE binary16 passed as uint16_t (Swift: Float16 /
+ *    UInt16). Tensors are row-major; token rows are [batch*seq, dim].
+ *  - Device pointers are caller-owned (sam3_alloc or any CUDA allocation on the
+ *    context's device). Operators are asynchronous on the context's stream;
+ *    sam3_sync() waits and reports device-side errors.
+ *  - One context per (host thread, GPU). Calls on one context must be
+ *    serialised by the caller; different contexts are independent.
+ *
+ * Reference interfaces (paths relative to OrdoSAM3Sensor/Sources/Sam3Sensor/)
+ * are cited beside each entry point it replaces.
+ */
+#ifndef SAM3CUDA_H
+#define SAM3CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+  SAM3_OK = 0,
+  SAM3_ERR_INVALID_ARG = 1, /* null pointer, bad enum, misaligned pointer  */
+  SAM3_ERR_SHAPE = 2,       /* shape unsupported or inconsistent          */
+  SAM3_ERR_OOM = 3,         /* device or pinned-host allocation failed     */
+  SAM3_ERR_CUDA = 4,        /* CUDA runtime/driver error                   */
+  SAM3_ERR_TIMEOUT = 5,     /* a kernel's bounded wait expired             */
+  SAM3_ERR_UNSUPPORTED = 6  /* device is not sm_100 or feature missing     */
+} sam3_status_t;
+
+/* Epilogue selectors of sam3_linear_palette. */
+typedef enum {
+  SAM3_EPI_BIAS = 0,          /* y = acc + b                                 */
+  SAM3_EPI_BIAS_GELU = 1,     /* y = gelu_erf(acc + b)                       */
+  SAM3_EPI_BIAS_RESIDUAL = 2, /* y = residual + acc + b (y may == residual)  */
+  SAM3_EPI_BIAS_ROPE_QKV = 3  /* y = rope(acc + b) on the q and k thirds     */
+} sam3_epilogue_t;
+
+typedef enum { SAM3_SCORE_L2 = 0, SAM3_SCORE_L1 = 1 } sam3_score_norm_t;
+typedef enum { SAM3_ORDER_INDEX = 0, SAM3_ORDER_SCORE = 1 } sam3_keep_order_t;
+
+typedef struct sam3_ctx sam3_ctx_t;
+
+/* Encoder configuration. Reference: SAM3EncoderConfig.swift:6-64 and the
+ * WeightMapper.swift:23-38 constants; the defaults follow the benchmark spec
+ * (all-global 32 blocks, prune to 50% after block 16 by L2 norm, index order). */
+typedef struct {
+  int32_t embed_dim;         /* 1024 */
+  int32_t num_heads;         /* 16 (head_dim must be 64) */
+  int32_t mlp_hidden;        /* 4096 */
+  int32_t num_blocks;        /* 32 */
+  int32_t patch;             /* 14 */
+  int32_t image_size;        /* 1008 (square) */
+  int32_t prune_after_block; /* 16; 0 disables pruning */
+  int32_t keep_tokens;       /* 2592 */
+  int32_t score_norm;        /* sam3_score_norm_t */
+  int32_t keep_order;        /* sam3_keep_order_t */
+  float ln_eps;              /* 1e-6 */
+  float rope_theta;          /* 10000 */
+  int32_t max_batch;         /* images per sam3_encoder_forward call */
+} sam3_encoder_config_t;
+
+/* One palettized linear layer, device pointers: idx uint8 [n, k] (row-major,
+ * PyTorch [out, in]), palette fp16 [n, 256], bias fp16 [n] (may be NULL).
+ * W[r, c] = palette[r, idx[r, c]]; Y = X * W^T + b. */
+typedef struct {
+  const uint8_t* idx;
+  const uint16_t* palette;
+  const uint16_t* bias;
+  int32_t n, k;
+} sam3_palette_linear_t;
+
+/* Weights of one pre-LN ViT block (device pointers). Reference:
+ * TransformerBlock.loadWeights, ViTEncoder.swift:693-721. */
+typedef struct {
+  const uint16_t* ln1_gamma; /* [dim] (NULL = ones)  */
+  const uint16_t* ln1_beta;  /* [dim] (NULL = zeros) */
+  sam3_palette_linear_t qkv; /* n = 3*dim, k = dim   */
+  sam3_palette_linear_t proj;/* n = dim,   k = dim   */
+  const uint16_t* ln2_gamma;
+  const uint16_t* ln2_beta;
+  sam3_palette_linear_t fc1; /* n = hidden, k = dim  */
+  sam3_palette_linear_t fc2; /* n = dim, k = hidden  */
+} sam3_block_weights_t;
+
+/* Whole-encoder weights. patch_w fp16 [dim, 3, patch, patch], patch_b [dim],
+ * blocks: array of num_blocks block weights (host array of device pointers). */
+typedef struct {
+  const uint16_t* patch_w;
+  const uint16_t* patch_b;
+  const sam3_block_weights_t* blocks;
+  int32_t num_blocks;
+} sam3_encoder_weights_t;
+
+/* ---- context ------------------------------------------------------------ */
+/* Fill *cfg with the benchmark defaults listed above. */
+sam3_status_t sam3_config_default(sam3_encoder_config_t* cfg);
+
+/* Create a context on `device`; cfg may be NULL (defaults). Replaces the
+ * per-module MTLDevice/queue set-up of ViTEncoder.init (ViTEncoder.swift:
+ * 1056-1180) and the process-global CompiledGraphCache/BufferAllocator
+ * (OptimizationInfrastructure.swift:20-332): the context owns one stream and a
+ * workspace arena sized for cfg->max_batch, allocated up front. */
+sam3_status_t sam3_ctx_create(int device, const sam3_encoder_config_t* cfg,
+                              sam3_ctx_t** out);
+sam3_status_t sam3_ctx_destroy(sam3_ctx_t* ctx);
+/* Use a caller-provided cudaStream_t (NULL = the context's own stream). */
+sam3_status_t sam3_ctx_set_stream(sam3_ctx_t* ctx, void* cuda_stream);
+void* sam3_ctx_stream(sam3_ctx_t* ctx);
+/* Last error message of this context ("" when none). Never NULL. */
+const char* sam3_last_error(const sam3_ctx_t* ctx);
+/* Wait for the context's stream; reports device errors and kernel timeouts. */
+sam3_status_t sam3_sync(sam3_ctx_t* ctx);
+/* Count of this library's kernel launches since context creation. */
+uint64_t sam3_launch_count(const sam3_ctx_t* ctx);
+
+/* ---- memory --------------------------------------------------------------- */
+sam3_status_t sam3_alloc(sam3_ctx_t* ctx, size_t bytes, void** dptr);
+sam3_status_t sam3_free(sam3_ctx_t* ctx, void* dptr);
+sam3_status_t sam3_host_alloc(sam3_ctx_t* ctx, size_t bytes, void** hptr);
+sam3_status_t sam3_host_free(sam3_ctx_t* ctx, void* hptr);
+sam3_status_t sam3_upload(sam3_ctx_t* ctx, void* dst, const void* src, size_t bytes);
+sam3_status_t sam3_download(sam3_ctx_t* ctx, void* dst, const void* src, size_t bytes);
+
+/* ---- operators (asynchronous on the context stream) ----------------------- */
+
+/* w_out fp16 [n, k] = palette[r, idx[r, c]] (bit-exact). Reference:
+ * dequantize_int8 / dequantize_int8_optimized, Metal/Dequantize.metal:17-32,
+ * 71-93 (one shared palette there; one palette per output row here). */
+sam3_status_t sam3_dequant_palette(sam3_ctx_t* ctx, const sam3_palette_linear_t* w,
+                                   uint16_t* w_out);
+
+/* y fp16 [m, n] = epilogue(x [m, k] * dequant(w)^T + b), dequantization fused
+ * into the tcgen05 GEMM (no dequantized weight reaches HBM). Requires
+ * k % 64 == 0, n % 128 == 0, 16-byte aligned pointers.
+ * residual: fp16 [m, n] for SAM3_EPI_BIAS_RESIDUAL (may equal y).
+ * rope: f32 [rope_rows, 32, 2] for SAM3_EPI_BIAS_ROPE_QKV (head_dim 64,
+ *   n == 3 * heads * 64); GEMM row r uses rope row (r % rope_rows).
+ * Reference: the matrixMultiplication + bias calls of MPSAttentionLayer
+ * (MPSAttention.swift:113-117, 179-183), MLP.forward (ViTEncoder.swift:
+ * 979-997), the RoPE graph (MPSAttention.swift:137-163) and add_residual_half
+ * (Metal/Common.metal:13-22, dispatched at ViTEncoder.swift:723-746). */
+sam3_status_t sam3_linear_palette(sam3_ctx_t* ctx, const uint16_t* x, int32_t m,
+                                  const sam3_palette_linear_t* w, int32_t epilogue,
+                                  const uint16_t* residual, const float* rope,
+                                  int32_t rope_rows, uint16_t* y);
+
+/* y [m, d] = (x - mean) / sqrt(var + eps) * gamma + beta, biased variance.
+ * Reference: LayerNorm.forward, ViTEncoder.swift:795-887. */
+sam3_status_t sam3_layernorm(sam3_ctx_t* ctx, const uint16_t* x, int32_t m, int32_t d,
+                             const uint16_t* gamma, const uint16_t* beta, float eps,
+                             uint16_t* y);
+
+/* table f32 [grid_h*grid_w, head_dim/2, 2] of (cos, sin); pairs [0, hd/4) use
+ * the column index, pairs [hd/4, hd/2) the row index, freq_i = theta^(-4i/hd).
+ * Reference: compute_rope_freqs_2d, Metal/RoPE.metal:22-52; RoPE.init /
+ * getFrequencies, RoPE.swift:27-120. */
+sam3_status_t sam3_rope_table(sam3_ctx_t* ctx, int32_t grid_h, int32_t grid_w,
+                              int32_t head_dim, float theta, float* table);
+
+/* In-place RoPE on packed qkv rows [m, 3*heads*head_dim] (q and k thirds).
+ * Reference: apply_rope_2d_batch, Metal/RoPE.metal:111-153. */
+sam3_status_t sam3_rope_apply(sam3_ctx_t* ctx, uint16_t* qkv, int32_t m, int32_t heads,
+                              int32_t head_dim, const float* table, int32_t rope_rows);
+
+/* o [batch*seq, heads*64] = softmax(q k^T * scale) v per image and head, from
+ * packed rows qkv [batch*seq, 3*heads*64]. Global (unmasked) attention.
+ * Reference: scaledDotProductAttention, MPSAttention.swift:165-176;
+ * AttentionKernels.referenceSoftmax, AttentionKernels.swift:48-68. */
+sam3_status_t sam3_attention(sam3_ctx_t* ctx, const uint16_t* qkv, int32_t batch,
+                             int32_t seq, int32_t heads, int32_t head_dim, float scale,
+                             uint16_t* o);
+
+/* Token scores f32 [rows] = L2 norm or L1 (sum |x|) of each row.
+ * Reference: TokenPruner.swift:54-56. */
+sam3_status_t sam3_token_scores(sam3_ctx_t* ctx, const uint16_t* x, int32_t rows,
+                                int32_t d, int32_t norm, float* scores);
+
+/* Prune each image of x [batch*seq, d] to its `keep` highest-scoring tokens
+ * (ties to the lower index), in ascending index order (SAM3_ORDER_INDEX) or by
+ * descending score (SAM3_ORDER_SCORE). Outputs: feats fp16 [batch*keep, d],
+ * rope_out f32 [batch*keep, rope_cols] gathered from rope_in row
+ * ((b*seq + token) % rope_rows) (rope_in/rope_out may be NULL), idx int32
+ * [batch, keep] (token index within its image). seq <= 16384.
+ * Reference: TokenPruner.prune, TokenPruner.swift:32-126. */
+sam3_status_t sam3_prune(sam3_ctx_t* ctx, const uint16_t* x, int32_t batch, int32_t seq,
+                         int32_t d, int32_t keep, int32_t norm, int32_t order,
+                         const float* rope_in, int32_t rope_rows, int32_t rope_cols,
+                         uint16_t* feats, float* rope_out, int32_t* idx);
+
+/* Patch embedding: NHWC fp16 image [batch, h, w, 3] -> tokens [batch*gh*gw, dim]
+ * (row-major h*gw + w), conv weights fp16 [dim, 3, patch, patch], bias [dim].
+ * Reference: PatchEmbedding.forward, ViTEncoder.swift:218-263, and the flatten
+ * kernel texture_to_buffer_flat_half, Metal/ViTUtils.metal:53-76. */
+sam3_status_t sam3_patch_embed(sam3_ctx_t* ctx, const uint16_t* image, int32_t batch,
+                               int32_t height, int32_t width, const uint16_t* patch_w,
+                               const uint16_t* patch_b, int32_t patch, int32_t dim,
+                               uint16_t* out);
+
+/* x [batch*seq, dim] -> x + attn(LN1(x)) (in place). Reference: LN1 +
+ * MPSAttentionLayer.forward + residual of TransformerBlock.forward,
+ * ViTEncoder.swift:388-411; MPSAttention.swift:85-244. */
+sam3_status_t sam3_attention_block(sam3_ctx_t* ctx, uint16_t* x, int32_t batch,
+                                   int32_t seq, const sam3_block_weights_t* w,
+                                   const float* rope, int32_t rope_rows);
+
+/* x [m, dim] -> x + MLP(LN2(x)) (in place). Reference: LN2 + MLP.forward +
+ * residual, ViTEncoder.swift:412-430, 953-1050. */
+sam3_status_t sam3_mlp_block(sam3_ctx_t* ctx, uint16_t* x, int32_t m,
+                             const sam3_block_weights_t* w);
+
+/* One pre-LN ViT block in place on x [batch*seq, dim]; rope f32
+ * [rope_rows, 32, 2], GEMM row r uses rope row r % rope_rows. Reference:
+ * TransformerBlock.forward, ViTEncoder.swift:368-431 (fused form :433-691). */
+sam3_status_t sam3_vit_block(sam3_ctx_t* ctx, uint16_t* x, int32_t batch, int32_t seq,
+                             const sam3_block_weights_t* w, const float* rope,
+                             int32_t rope_rows);
+
+/* Full encoder on device buffers: image fp16 NHWC [batch, S, S, 3] ->
+ * feats fp16 [batch, keep, dim] (or [batch, seq, dim] without pruning) and
+ * idx int32 [batch, keep] (token index of each kept row). batch <= max_batch.
+ * Reference: ViTEncoder.forward(image:commandBuffer:), ViTEncoder.swift:
+ * 1235-1481. */
+sam3_status_t sam3_encoder_forward(sam3_ctx_t* ctx, const uint16_t* image, int32_t batch,
+                                   const sam3_encoder_weights_t* w, uint16_t* feats,
+                                   int32_t* idx);
+
+/* Same, from and to HOST buffers (pinned or pageable): copies the images in,
+ * runs the encoder and copies feats/idx out, then waits. Reference:
+ * SAM3MetalPipeline.encode(image:), SAM3MetalPipeline.swift:67-82. */
+sam3_status_t sam3_encoder_forward_host(sam3_ctx_t* ctx, const uint16_t* host_image,
+                                        int32_t batch, const sam3_encoder_weights_t* w,
+                                        uint16_t* host_feats, int32_t* host_idx);
+
+/* ---- device-side stage timing ---------------------------------------------
+ * When enabled, the context brackets each of its kernel launches with CUDA
+ * events on its stream and accumulates, per kernel class, the launch count,
+ * the device time and the algorithmic work (GEMM and attention FLOPs, bytes of
+ * the memory-bound kernels). Reference: the SAM3_STAGE_TIMING stage timer of
+ * ViTEncoder.forward (ViTEncoder.swift:1236-1237,1438-1450; Sam3Log.swift:
+ * 9-25), which timed CPU encode time; this one times the device. */
+typedef enum {
+  SAM3_PROF_GEMM = 0,      /* palette-dequant GEMMs (QKV, proj, fc1, fc2)   */
+  SAM3_PROF_ATTENTION = 1, /* softmax attention                             */
+  SAM3_PROF_LAYERNORM = 2,
+  SAM3_PROF_PRUNE = 3,     /* scores + select + gather                      */
+  SAM3_PROF_PATCH = 4,     /* im2col + weight pad + dense patch GEMM        */
+  SAM3_PROF_OTHER = 5,     /* RoPE table/apply, dequant, iota               */
+  SAM3_PROF_CLASSES = 6
+} sam3_prof_class_t;
+
+typedef struct {
+  uint64_t launches[SAM3_PROF_CLASSES];
+  double milliseconds[SAM3_PROF_CLASSES]; /* summed device time of launches */
+  double flops[SAM3_PROF_CLASSES];        /* 2*m*n*k (GEMM), 4*B*H*S^2*d    */
+  double bytes[SAM3_PROF_CLASSES];        /* algorithmic HBM bytes          */
+} sam3_profile_t;
+
+/* Turn timing on (resets the counters) or off. */
+sam3_status_t sam3_profile_enable(sam3_ctx_t* ctx, int32_t enable);
+/* Wait for the stream and return the counters accumulated since enabling. */
+sam3_status_t sam3_profile_read(sam3_ctx_t* ctx, sam3_profile_t* out);
+
+/* Rows kept per image by the encoder under the context's config. */
+int32_t sam3_encoder_out_tokens(const sam3_ctx_t* ctx);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* SAM3CUDA_H */

@@ -1,0 +1,220 @@
+// encoder.cu - ViT block and encoder drivers over the operators.
+//
+// Reference: TransformerBlock.forward (ViTEncoder.swift:368-431; fused op
+// order :433-691) and ViTEncoder.forward (ViTEncoder.swift:1235-1481): patch
+// embedding, the block loop with the token-pruning step inside it
+// (:1339-1396; here after `prune_after_block` blocks, all blocks global), the
+// RoPE rows of the kept tokens gathered alongside their features
+// (TokenPruner.swift:65-69). Per block: LN1 -> QKV GEMM (+bias, +RoPE
+// epilogue) -> attention -> out-proj GEMM (+bias, +residual, in place) -> LN2
+// -> fc1 GEMM (+bias, +GELU) -> fc2 GEMM (+bias, +residual, in place).
+#include <algorithm>
+
+#include "common.cuh"
+#include "internal.h"
+
+namespace sam3 {
+sam3_status_t ensure_workspace(sam3_ctx_t* ctx);
+
+namespace {
+
+__global__ void iota_kernel(int32_t* idx, int per, long long total) {
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < total) idx[i] = (int32_t)(i % per);
+}
+
+sam3_status_t check_block_weights(sam3_ctx_t* ctx, const sam3_block_weights_t* w) {
+  if (!w) return set_error(ctx, SAM3_ERR_INVALID_ARG, "block: null weights");
+  const int D = ctx->cfg.embed_dim, F = ctx->cfg.mlp_hidden;
+  if (w->qkv.n != 3 * D || w->qkv.k != D || w->proj.n != D || w->proj.k != D ||
+      w->fc1.n != F || w->fc1.k != D || w->fc2.n != D || w->fc2.k != F)
+    return set_error(ctx, SAM3_ERR_SHAPE, "block: weight shapes do not match the config");
+  return SAM3_OK;
+}
+
+sam3_status_t attention_block(sam3_ctx_t* ctx, uint16_t* x, int batch, int seq,
+                              const sam3_block_weights_t* w, const float* rope, int rope_rows) {
+  const int D = ctx->cfg.embed_dim, H = ctx->cfg.num_heads;
+  const int m = batch * seq;
+  sam3_status_t st;
+  if ((st = layernorm(ctx, x, m, D, w->ln1_gamma, w->ln1_beta, ctx->cfg.ln_eps, ctx->ln)) != SAM3_OK)
+    return st;
+  if ((st = gemm_palette(ctx, ctx->ln, m, D, w->qkv.idx, w->qkv.palette, w->qkv.bias, 3 * D,
+                         SAM3_EPI_BIAS_ROPE_QKV, nullptr, rope, rope_rows, ctx->qkv)) != SAM3_OK)
+    return st;
+  if ((st = attention(ctx, ctx->qkv, batch, seq, H, 64, 0.125f, ctx->attn)) != SAM3_OK) return st;
+  return gemm_palette(ctx, ctx->attn, m, D, w->proj.idx, w->proj.palette, w->proj.bias, D,
+                      SAM3_EPI_BIAS_RESIDUAL, x, nullptr, 1, x);
+}
+
+sam3_status_t mlp_block(sam3_ctx_t* ctx, uint16_t* x, int m, const sam3_block_weights_t* w) {
+  const int D = ctx->cfg.embed_dim, F = ctx->cfg.mlp_hidden;
+  sam3_status_t st;
+  if ((st = layernorm(ctx, x, m, D, w->ln2_gamma, w->ln2_beta, ctx->cfg.ln_eps, ctx->ln)) != SAM3_OK)
+    return st;
+  if ((st = gemm_palette(ctx, ctx->ln, m, D, w->fc1.idx, w->fc1.palette, w->fc1.bias, F,
+                         SAM3_EPI_BIAS_GELU, nullptr, nullptr, 1, ctx->hidden)) != SAM3_OK)
+    return st;
+  return gemm_palette(ctx, ctx->hidden, m, F, w->fc2.idx, w->fc2.palette, w->fc2.bias, D,
+                      SAM3_EPI_BIAS_RESIDUAL, x, nullptr, 1, x);
+}
+
+sam3_status_t check_rows(sam3_ctx_t* ctx, long long rows) {
+  if (rows <= 0) return set_error(ctx, SAM3_ERR_SHAPE, "block: empty input");
+  if ((size_t)rows > ctx->block_rows)
+    return set_error(ctx, SAM3_ERR_SHAPE, "block: %lld rows exceed the context capacity %zu "
+                     "(raise max_batch)", rows, ctx->block_rows);
+  return SAM3_OK;
+}
+
+// Runs the encoder on a device image; returns the final residual stream
+// (pointer into the workspace) and its rows per image; writes kept indices.
+sam3_status_t encoder_run(sam3_ctx_t* ctx, const uint16_t* image, int batch,
+                          const sam3_encoder_weights_t* w, int32_t* idx, const uint16_t** out,
+                          int* rows_out) {
+  const sam3_encoder_config_t& c = ctx->cfg;
+  if (!image || !w || !idx) return set_error(ctx, SAM3_ERR_INVALID_ARG, "encoder: null pointer");
+  if (batch <= 0 || batch > c.max_batch)
+    return set_error(ctx, SAM3_ERR_SHAPE, "encoder: batch %d outside [1, max_batch=%d]", batch,
+                     c.max_batch);
+  if (w->num_blocks != c.num_blocks || (c.num_blocks > 0 && !w->blocks) || !w->patch_w)
+    return set_error(ctx, SAM3_ERR_SHAPE, "encoder: weights do not match the config");
+  sam3_status_t st;
+  for (int i = 0; i < c.num_blocks; ++i)
+    if ((st = check_block_weights(ctx, &w->blocks[i])) != SAM3_OK) return st;
+  const int grid = c.image_size / c.patch;
+  const int S = grid * grid, D = c.embed_dim;
+  const bool pruned = c.prune_after_block > 0 && c.prune_after_block <= c.num_blocks &&
+                      c.keep_tokens < S;
+  const int keep = pruned ? c.keep_tokens : S;
+  if (!ctx->rope_ready) {
+    if ((st = rope_table(ctx, grid, grid, 64, c.rope_theta, ctx->rope)) != SAM3_OK) return st;
+    ctx->rope_ready = 1;
+  }
+  if ((st = patch_embed(ctx, image, batch, c.image_size, c.image_size, w->patch_w, w->patch_b,
+                        c.patch, D, ctx->x, ctx->cols, ctx->patch_wp)) != SAM3_OK)
+    return st;
+  uint16_t* cur = ctx->x;
+  int rows = S;
+  const float* rope = ctx->rope;
+  int rope_rows = S;
+  for (int blk = 0; blk <= c.num_blocks; ++blk) {
+    if (pruned && blk == c.prune_after_block) {
+      if ((st = prune(ctx, cur, batch, S, D, keep, c.score_norm, c.keep_order, ctx->rope, S, 64,
+                      ctx->xp, ctx->rope_pruned, idx, ctx->scores)) != SAM3_OK)
+        return st;
+      cur = ctx->xp;
+      rows = keep;
+      rope = ctx->rope_pruned;
+      rope_rows = batch * keep;
+    }
+    if (blk == c.num_blocks) break;
+    if ((st = attention_block(ctx, cur, batch, rows, &w->blocks[blk], rope, rope_rows)) != SAM3_OK)
+      return st;
+    if ((st = mlp_block(ctx, cur, batch * rows, &w->blocks[blk])) != SAM3_OK) return st;
+  }
+  if (!pruned) {
+    const long long total = (long long)batch * S;
+    ProfScope prof(ctx, SAM3_PROF_OTHER, 0.0, 4.0 * total);
+    iota_kernel<<<(int)((total + 255) / 256), 256, 0, ctx->stream>>>(idx, S, total);
+    if ((st = check_launch(ctx, "iota_kernel")) != SAM3_OK) return st;
+  }
+  *out = cur;
+  *rows_out = rows;
+  return SAM3_OK;
+}
+
+}  // namespace
+}  // namespace sam3
+
+using namespace sam3;
+
+extern "C" {
+
+sam3_status_t sam3_attention_block(sam3_ctx_t* ctx, uint16_t* x, int32_t batch, int32_t seq,
+                                   const sam3_block_weights_t* w, const float* rope,
+                                   int32_t rope_rows) {
+  SAM3_CHECK_CTX(ctx);
+  cudaSetDevice(ctx->device);
+  sam3_status_t st = check_block_weights(ctx, w);
+  if (st != SAM3_OK) return st;
+  if ((st = check_rows(ctx, (long long)batch * seq)) != SAM3_OK) return st;
+  if (!x || !rope) return set_error(ctx, SAM3_ERR_INVALID_ARG, "attention_block: null pointer");
+  return attention_block(ctx, x, batch, seq, w, rope, rope_rows);
+}
+
+sam3_status_t sam3_mlp_block(sam3_ctx_t* ctx, uint16_t* x, int32_t m,
+                             const sam3_block_weights_t* w) {
+  SAM3_CHECK_CTX(ctx);
+  cudaSetDevice(ctx->device);
+  sam3_status_t st = check_block_weights(ctx, w);
+  if (st != SAM3_OK) return st;
+  if ((st = check_rows(ctx, m)) != SAM3_OK) return st;
+  if (!x) return set_error(ctx, SAM3_ERR_INVALID_ARG, "mlp_block: null pointer");
+  return mlp_block(ctx, x, m, w);
+}
+
+sam3_status_t sam3_vit_block(sam3_ctx_t* ctx, uint16_t* x, int32_t batch, int32_t seq,
+                             const sam3_block_weights_t* w, const float* rope, int32_t rope_rows) {
+  sam3_status_t st = sam3_attention_block(ctx, x, batch, seq, w, rope, rope_rows);
+  if (st != SAM3_OK) return st;
+  return mlp_block(ctx, x, batch * seq, w);
+}
+
+int32_t sam3_encoder_out_tokens(const sam3_ctx_t* ctx) {
+  if (!ctx) return 0;
+  const sam3_encoder_config_t& c = ctx->cfg;
+  const int grid = c.image_size / c.patch;
+  const int S = grid * grid;
+  const bool pruned =
+      c.prune_after_block > 0 && c.prune_after_block <= c.num_blocks && c.keep_tokens < S;
+  return pruned ? c.keep_tokens : S;
+}
+
+sam3_status_t sam3_encoder_forward(sam3_ctx_t* ctx, const uint16_t* image, int32_t batch,
+                                   const sam3_encoder_weights_t* w, uint16_t* feats,
+                                   int32_t* idx) {
+  SAM3_CHECK_CTX(ctx);
+  if (!feats) return set_error(ctx, SAM3_ERR_INVALID_ARG, "encoder: null feats");
+  cudaSetDevice(ctx->device);
+  const uint16_t* out = nullptr;
+  int rows = 0;
+  sam3_status_t st = encoder_run(ctx, image, batch, w, idx, &out, &rows);
+  if (st != SAM3_OK) return st;
+  const size_t bytes = (size_t)batch * rows * ctx->cfg.embed_dim * 2;
+  return check_cuda(ctx, cudaMemcpyAsync(feats, out, bytes, cudaMemcpyDeviceToDevice, ctx->stream),
+                    "encoder feats copy");
+}
+
+sam3_status_t sam3_encoder_forward_host(sam3_ctx_t* ctx, const uint16_t* host_image,
+                                        int32_t batch, const sam3_encoder_weights_t* w,
+                                        uint16_t* host_feats, int32_t* host_idx) {
+  SAM3_CHECK_CTX(ctx);
+  if (!host_image || !host_feats || !host_idx)
+    return set_error(ctx, SAM3_ERR_INVALID_ARG, "encoder_host: null pointer");
+  if (batch <= 0 || batch > ctx->cfg.max_batch)
+    return set_error(ctx, SAM3_ERR_SHAPE, "encoder_host: batch %d outside [1, %d]", batch,
+                     ctx->cfg.max_batch);
+  cudaSetDevice(ctx->device);
+  const sam3_encoder_config_t& c = ctx->cfg;
+  const size_t img_bytes = (size_t)batch * c.image_size * c.image_size * 3 * 2;
+  sam3_status_t st = check_cuda(
+      ctx, cudaMemcpyAsync(ctx->image, host_image, img_bytes, cudaMemcpyHostToDevice, ctx->stream),
+      "encoder_host image upload");
+  if (st != SAM3_OK) return st;
+  const uint16_t* out = nullptr;
+  int rows = 0;
+  if ((st = encoder_run(ctx, ctx->image, batch, w, ctx->idx, &out, &rows)) != SAM3_OK) return st;
+  const size_t fbytes = (size_t)batch * rows * c.embed_dim * 2;
+  if ((st = check_cuda(ctx, cudaMemcpyAsync(host_feats, out, fbytes, cudaMemcpyDeviceToHost,
+                                            ctx->stream),
+                       "encoder_host feats download")) != SAM3_OK)
+    return st;
+  if ((st = check_cuda(ctx, cudaMemcpyAsync(host_idx, ctx->idx, (size_t)batch * rows * 4,
+                                            cudaMemcpyDeviceToHost, ctx->stream),
+                       "encoder_host idx download")) != SAM3_OK)
+    return st;
+  return sam3_sync(ctx);
+}
+
+}  // extern "C"

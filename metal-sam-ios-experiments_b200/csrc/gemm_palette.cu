@@ -1,0 +1,560 @@
+// gemm_palette.cu - uint8-palette dequantization fused into an sm_100a
+// tcgen05 GEMM:  Y[m, n] = epilogue( X[m, :] . W[n, :] + b[n] ),
+// W[n, k] = P[n, idx[n, k]] with one 256-entry fp16 palette per output row.
+//
+// Reference path replaced: the dense-fp16 MPSGraph matrixMultiplication calls
+// of MPSAttention.swift:113-117,179-183 and ViTEncoder.swift:979-997, fed by
+// the never-dispatched LUT expansion of Metal/Dequantize.metal:17-93. Here the
+// LUT expansion happens in shared memory right before the tensor cores read
+// the tile: no dequantized weight is ever written to HBM.
+//
+// Kernel structure (one persistent CTA per SM, 320 threads):
+//   warp 0      TMA producer: X tile [128 x 64] fp16 (128B swizzle) and the
+//               uint8 index tile [128 x 64] (64B swizzle) per k-block stage.
+//   warp 1      TMEM allocator + single-thread tcgen05.mma issuer
+//               (M=128, N=128, K=16 per instruction, fp32 accumulators in two
+//               128-column TMEM buffers so the epilogue overlaps the next tile).
+//   warps 2-5   palette expanders: thread r owns weight row r of the tile;
+//               its palette sits in shared memory transposed as 32-bit words
+//               word[e & 127][r] = P[r][e & 127] | P[r][(e & 127) + 128] << 16,
+//               so lane r always reads bank r (conflict-free lookups), and the
+//               fp16 row is written straight into the 128B-swizzled K-major
+//               operand layout the UMMA descriptor expects.
+//   warps 6-9   epilogue: tcgen05.ld 32 columns at a time, bias / exact GELU /
+//               2D-RoPE on the q,k thirds / residual add, fp16 store.
+// A dense-fp16-weight variant (TMA-loaded B, used by the patch embedding)
+// shares the kernel.
+#include "common.cuh"
+#include "internal.h"
+
+namespace sam3 {
+namespace {
+
+constexpr int BM = 128, BN = 128, BK = 64, STAGES = 4;
+constexpr int NUM_THREADS = 320;
+constexpr int A_STAGE = BM * BK * 2;  // 16 KB
+constexpr int B_STAGE = BN * BK * 2;  // 16 KB
+constexpr int I_STAGE = BN * BK;      // 8 KB
+constexpr int PAL_BYTES = BN * 512;   // 64 KB
+constexpr int OFF_A = 0;
+constexpr int OFF_B = OFF_A + STAGES * A_STAGE;
+constexpr int OFF_I = OFF_B + STAGES * B_STAGE;
+constexpr int OFF_P = OFF_I + STAGES * I_STAGE;
+constexpr int OFF_BAR = OFF_P + PAL_BYTES;
+constexpr int NUM_BARS = 3 * STAGES + 6;
+constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;
+constexpr int SMEM_BYTES = OFF_MISC + 16 + 1024;  // + slack for 1024-B alignment
+constexpr uint32_t TMEM_COLS = 2 * BN;
+constexpr uint32_t IDESC = umma_idesc_f16(BM, BN);
+static_assert(SMEM_BYTES <= 232448, "shared memory budget");
+
+enum BMode { kPalette = 0, kDense = 1 };
+
+struct GemmArgs {
+  const __half* bias;
+  const __half* residual;
+  const float* rope;
+  const __half* palette;
+  __half* y;
+  int* err;
+  int m, n, k;
+  int epi;
+  int rope_rows;
+  int qk_cols;
+  int m_tiles, total_tiles;
+};
+
+__device__ __forceinline__ void add_half8(float* f, uint4 v) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const float2 p = unpack_half2(w[q]);
+    f[2 * q] += p.x;
+    f[2 * q + 1] += p.y;
+  }
+}
+
+// Epilogue for 32 consecutive accumulator columns of one output row.
+__device__ __forceinline__ void epilogue_chunk(const GemmArgs& a, int row, int col0,
+                                               const uint32_t (&v)[32]) {
+  float f[32];
+#pragma unroll
+  for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(v[j]);
+  if (a.bias) {
+    const uint4* bp = reinterpret_cast<const uint4*>(a.bias + col0);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) add_half8(f + 8 * q, __ldg(bp + q));
+  }
+  if (a.epi == SAM3_EPI_BIAS_GELU) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) f[j] = gelu_erf(f[j]);
+  } else if (a.epi == SAM3_EPI_BIAS_ROPE_QKV && col0 < a.qk_cols) {
+    // 32 columns = 16 interleaved (even, odd) pairs of one 64-wide head;
+    // table row holds 32 (cos, sin) pairs, pair j at float offset 2j.
+    const float4* t = reinterpret_cast<const float4*>(
+        a.rope + (size_t)(row % a.rope_rows) * 64 + (col0 & 63));
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const float4 cs = __ldg(t + q);
+      float x0 = f[4 * q], x1 = f[4 * q + 1];
+      f[4 * q] = x0 * cs.x - x1 * cs.y;
+      f[4 * q + 1] = x0 * cs.y + x1 * cs.x;
+      x0 = f[4 * q + 2];
+      x1 = f[4 * q + 3];
+      f[4 * q + 2] = x0 * cs.z - x1 * cs.w;
+      f[4 * q + 3] = x0 * cs.w + x1 * cs.z;
+    }
+  }
+  if (row >= a.m) return;
+  const size_t off = (size_t)row * a.n + col0;
+  if (a.epi == SAM3_EPI_BIAS_RESIDUAL) {
+    const uint4* rp = reinterpret_cast<const uint4*>(a.residual + off);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) add_half8(f + 8 * q, rp[q]);
+  }
+  uint4* yp = reinterpret_cast<uint4*>(a.y + off);
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    uint4 o;
+    o.x = pack_half2(f[8 * q + 0], f[8 * q + 1]);
+    o.y = pack_half2(f[8 * q + 2], f[8 * q + 3]);
+    o.z = pack_half2(f[8 * q + 4], f[8 * q + 5]);
+    o.w = pack_half2(f[8 * q + 6], f[8 * q + 7]);
+    yp[q] = o;
+  }
+}
+
+// Expand 16 palette indices (one 16-byte idx chunk) of weight row r into 16
+// fp16 values = 8 packed words. pal points at word[0][r]; word[e][r] is at
+// pal[e * 128].
+__device__ __forceinline__ void expand16(uint4 v, const uint32_t* pal, uint32_t (&out)[8]) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const uint32_t u = w[q];
+    const uint32_t p0 = pal[(u & 0x7Fu) << 7];
+    const uint32_t p1 = pal[((u >> 8) & 0x7Fu) << 7];
+    const uint32_t p2 = pal[((u >> 16) & 0x7Fu) << 7];
+    const uint32_t p3 = pal[((u >> 24) & 0x7Fu) << 7];
+    // bit 7 of each index selects the high half-word (entries 128..255).
+    const uint32_t t = (u >> 6) & 0x02020202u;
+    const uint32_t sel01 = 0x5410u | ((t & 0x0202u) * 0x11u);
+    const uint32_t sel23 = 0x5410u | (((t >> 16) & 0x0202u) * 0x11u);
+    out[2 * q] = __byte_perm(p0, p1, sel01);
+    out[2 * q + 1] = __byte_perm(p2, p3, sel23);
+  }
+}
+
+template <int MODE>
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    gemm_palette_kernel(const __grid_constant__ CUtensorMap tmap_a,
+                        const __grid_constant__ CUtensorMap tmap_b, const GemmArgs args) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  const uint32_t sbase = smem_u32(smem);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  const uint32_t bar_full = sbase + OFF_BAR;
+  const uint32_t bar_full_b = bar_full + 8 * STAGES;
+  const uint32_t bar_empty = bar_full_b + 8 * STAGES;
+  const uint32_t bar_tfull = bar_empty + 8 * STAGES;
+  const uint32_t bar_tempty = bar_tfull + 16;
+  const uint32_t bar_drain = bar_tempty + 16;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + OFF_MISC);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + OFF_MISC + 4);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(bar_full + 8 * s, 1);
+      mbar_init(bar_full_b + 8 * s, 128);
+      mbar_init(bar_empty + 8 * s, 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(bar_tfull + 8 * a, 1);
+      mbar_init(bar_tempty + 8 * a, 128);
+    }
+    mbar_init(bar_drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    prefetch_tmap(&tmap_a);
+    prefetch_tmap(&tmap_b);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int G = gridDim.x;
+  const int t_begin = (int)((long long)blockIdx.x * args.total_tiles / G);
+  const int t_end = (int)((long long)(blockIdx.x + 1) * args.total_tiles / G);
+  const int kblocks = args.k / BK;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------- producer
+    if (lane == 0) {
+      int s = 0;
+      uint32_t ph = 0;
+      uint32_t issued = 0, issued_par = 0;
+      const uint32_t bytes = A_STAGE + (MODE == kPalette ? I_STAGE : B_STAGE);
+      for (int t = t_begin; t < t_end; ++t) {
+        const int m0 = (t % args.m_tiles) * BM, n0 = (t / args.m_tiles) * BN;
+        bool ok = true;
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait(bar_empty + 8 * s, ph ^ 1, abort_flag, args.err,
+                         kDevErrTimeoutProducer)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(bar_full + 8 * s, bytes);
+          tma_load_2d(sbase + OFF_A + s * A_STAGE, &tmap_a, bar_full + 8 * s, kb * BK, m0);
+          if (MODE == kPalette)
+            tma_load_2d(sbase + OFF_I + s * I_STAGE, &tmap_b, bar_full + 8 * s, kb * BK, n0);
+          else
+            tma_load_2d(sbase + OFF_B + s * B_STAGE, &tmap_b, bar_full + 8 * s, kb * BK, n0);
+          issued |= 1u << s;
+          issued_par = (issued_par & ~(1u << s)) | (ph << s);
+          if (++s == STAGES) {
+            s = 0;
+            ph ^= 1;
+          }
+        }
+        if (!ok) break;
+      }
+      if (*abort_flag) {
+        // Let every copy this thread issued land before the CTA can exit.
+        for (int q = 0; q < STAGES; ++q)
+          if (issued & (1u << q)) mbar_wait_drain(bar_full + 8 * q, (issued_par >> q) & 1u);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      int s = 0;
+      uint32_t ph = 0;
+      int it = 0;
+      bool issued_any = false;
+      for (int t = t_begin; t < t_end; ++t, ++it) {
+        const int acc = it & 1;
+        const uint32_t use = (uint32_t)(it >> 1) & 1u;
+        if (!mbar_wait(bar_tempty + 8 * acc, use ^ 1, abort_flag, args.err, kDevErrTimeoutMma))
+          break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+        bool ok = true;
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait(bar_full + 8 * s, ph, abort_flag, args.err, kDevErrTimeoutMma) ||
+              (MODE == kPalette &&
+               !mbar_wait(bar_full_b + 8 * s, ph, abort_flag, args.err, kDevErrTimeoutMma))) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = sbase + OFF_A + s * A_STAGE;
+          const uint32_t b_addr = sbase + OFF_B + s * B_STAGE;
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk)
+            umma_f16_ss(d_tmem, umma_desc_sw128(a_addr + kk * 32),
+                        umma_desc_sw128(b_addr + kk * 32), IDESC, (kb | kk) != 0);
+          umma_commit(bar_empty + 8 * s);
+          issued_any = true;
+          if (++s == STAGES) {
+            s = 0;
+            ph ^= 1;
+          }
+        }
+        if (!ok) break;
+        umma_commit(bar_tfull + 8 * acc);
+      }
+      if (*abort_flag && issued_any) {
+        umma_commit(bar_drain);
+        mbar_wait_drain(bar_drain, 0);
+      }
+    }
+  } else if (warp < 6) {
+    // ------------------------------------------------------------- palette expanders
+    // Thread r owns weight row r of the tile: it stages that row's palette,
+    // reads only that row's indices and writes only that row of the B tile,
+    // so the expanders never need to synchronise with each other.
+    if (MODE == kPalette) {
+      const int r = threadIdx.x - 64;
+      uint32_t* pal = reinterpret_cast<uint32_t*>(smem + OFF_P) + r;  // word[e][r] at pal[e*128]
+      int s = 0;
+      uint32_t ph = 0;
+      int cur_n = -1;
+      bool ok = true;
+      for (int t = t_begin; t < t_end && ok; ++t) {
+        const int n_tile = t / args.m_tiles;
+        if (n_tile != cur_n) {
+          const uint4* prow =
+              reinterpret_cast<const uint4*>(args.palette + (size_t)(n_tile * BN + r) * 256);
+#pragma unroll 4
+          for (int j = 0; j < 16; ++j) {
+            const uint4 lo = __ldg(prow + j), hi = __ldg(prow + 16 + j);
+            const uint32_t l[4] = {lo.x, lo.y, lo.z, lo.w}, h[4] = {hi.x, hi.y, hi.z, hi.w};
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              const int e = 8 * j + 2 * q;
+              pal[e * 128] = __byte_perm(l[q], h[q], 0x5410u);
+              pal[(e + 1) * 128] = __byte_perm(l[q], h[q], 0x7632u);
+            }
+          }
+          cur_n = n_tile;
+        }
+        for (int kb = 0; kb < kblocks; ++kb) {
+          ok = __all_sync(0xffffffffu, mbar_wait(bar_full + 8 * s, ph, abort_flag, args.err,
+                                                 kDevErrTimeoutDequant));
+          if (!ok) break;
+          const uint8_t* itile = smem + OFF_I + s * I_STAGE + r * 64;
+          uint8_t* brow = smem + OFF_B + s * B_STAGE + r * 128;
+          const int sw64 = (r >> 1) & 3;
+          const int sw128 = r & 7;
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const uint4 v = *reinterpret_cast<const uint4*>(itile + ((q ^ sw64) << 4));
+            uint32_t o[8];
+            expand16(v, pal, o);
+            *reinterpret_cast<uint4*>(brow + (((2 * q) ^ sw128) << 4)) =
+                make_uint4(o[0], o[1], o[2], o[3]);
+            *reinterpret_cast<uint4*>(brow + (((2 * q + 1) ^ sw128) << 4)) =
+                make_uint4(o[4], o[5], o[6], o[7]);
+          }
+          fence_proxy_async_smem();  // generic-proxy writes -> visible to the tensor core
+          mbar_arrive(bar_full_b + 8 * s);
+          if (++s == STAGES) {
+            s = 0;
+            ph ^= 1;
+          }
+        }
+      }
+    }
+  } else {
+    // ------------------------------------------------------------- epilogue
+    const int quad = warp & 3;  // TMEM lanes [32*quad, 32*quad + 32) belong to this warp
+    int it = 0;
+    for (int t = t_begin; t < t_end; ++t, ++it) {
+      const int acc = it & 1;
+      const uint32_t use = (uint32_t)(it >> 1) & 1u;
+      const bool ok = __all_sync(0xffffffffu, mbar_wait(bar_tfull + 8 * acc, use, abort_flag,
+                                                        args.err, kDevErrTimeoutEpilogue));
+      if (!ok) break;
+      tc_fence_after();
+      const int m0 = (t % args.m_tiles) * BM, n0 = (t / args.m_tiles) * BN;
+      const int row = m0 + quad * 32 + lane;
+      const uint32_t taddr = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * BN);
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(taddr + (uint32_t)(c * 32), v);
+        tmem_wait_ld();
+        epilogue_chunk(args, row, n0 + c * 32, v);
+      }
+      tc_fence_before();
+      mbar_arrive(bar_tempty + 8 * acc);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+// Stand-alone LUT expansion, the bit-exact check of the in-GEMM expansion and
+// the B200 form of dequantize_int8_optimized (Metal/Dequantize.metal:71-93):
+// 8 weight rows per CTA, their palettes staged in shared memory, 16-byte
+// index loads and 2 x 16-byte fp16 stores per thread.
+__global__ void __launch_bounds__(256) dequant_kernel(const uint8_t* __restrict__ idx,
+                                                      const __half* __restrict__ pal,
+                                                      __half* __restrict__ w, int n, int k) {
+  __shared__ __align__(16) uint16_t spal[8][256];
+  const int row0 = blockIdx.x * 8;
+  {
+    const int r = threadIdx.x >> 5, c = threadIdx.x & 31;  // 8 rows x 32 uint4
+    if (row0 + r < n)
+      reinterpret_cast<uint4*>(spal[r])[c] =
+          __ldg(reinterpret_cast<const uint4*>(pal + (size_t)(row0 + r) * 256) + c);
+  }
+  __syncthreads();
+  const int cpr = k / 16;  // 16-index chunks per row
+  for (int c = threadIdx.x; c < 8 * cpr; c += blockDim.x) {
+    const int r = c / cpr, q = c % cpr;
+    if (row0 + r >= n) break;
+    const uint4 v = __ldg(reinterpret_cast<const uint4*>(idx + (size_t)(row0 + r) * k) + q);
+    const uint32_t wv[4] = {v.x, v.y, v.z, v.w};
+    uint32_t o[8];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const uint32_t u = wv[j];
+      o[2 * j] = (uint32_t)spal[r][u & 0xFF] | ((uint32_t)spal[r][(u >> 8) & 0xFF] << 16);
+      o[2 * j + 1] = (uint32_t)spal[r][(u >> 16) & 0xFF] | ((uint32_t)spal[r][u >> 24] << 16);
+    }
+    uint4* dst = reinterpret_cast<uint4*>(w + (size_t)(row0 + r) * k) + 2 * q;
+    dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
+    dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
+  }
+}
+
+sam3_status_t make_map_2d(sam3_ctx_t* ctx, CUtensorMap* map, CUtensorMapDataType dt,
+                          int elem_bytes, const void* base, uint64_t inner, uint64_t outer,
+                          uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle sw) {
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {inner * (uint64_t)elem_bytes};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t es[2] = {1, 1};
+  CUresult r = encode_tiled()(map, dt, 2, const_cast<void*>(base), dims, strides, box, es,
+                              CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return set_error(ctx, SAM3_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return SAM3_OK;
+}
+
+template <int MODE>
+sam3_status_t launch(sam3_ctx_t* ctx, const CUtensorMap& ma, const CUtensorMap& mb,
+                     const GemmArgs& args) {
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaError_t e = cudaFuncSetAttribute(gemm_palette_kernel<MODE>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    if (e != cudaSuccess) return check_cuda(ctx, e, "gemm smem attribute");
+    attr_set = true;
+  }
+  const int grid = args.total_tiles < ctx->num_sms ? args.total_tiles : ctx->num_sms;
+  gemm_palette_kernel<MODE><<<grid, NUM_THREADS, SMEM_BYTES, ctx->stream>>>(ma, mb, args);
+  return check_launch(ctx, "gemm_palette_kernel");
+}
+
+sam3_status_t validate(sam3_ctx_t* ctx, const void* x, int m, int k, int n, const void* y) {
+  if (!x || !y) return set_error(ctx, SAM3_ERR_INVALID_ARG, "linear: null x or y");
+  if (m <= 0 || n <= 0 || k <= 0)
+    return set_error(ctx, SAM3_ERR_SHAPE, "linear: empty shape m=%d n=%d k=%d", m, n, k);
+  if (k % BK || n % BN)
+    return set_error(ctx, SAM3_ERR_SHAPE, "linear: need k %% 64 == 0 and n %% 128 == 0 (k=%d n=%d)",
+                     k, n);
+  if (!aligned16(x) || !aligned16(y))
+    return set_error(ctx, SAM3_ERR_INVALID_ARG, "linear: x and y must be 16-byte aligned");
+  return SAM3_OK;
+}
+
+}  // namespace
+
+sam3_status_t gemm_palette(sam3_ctx_t* ctx, const uint16_t* x, int m, int k, const uint8_t* idx,
+                           const uint16_t* palette, const uint16_t* bias, int n, int epi,
+                           const uint16_t* residual, const float* rope, int rope_rows,
+                           uint16_t* y) {
+  sam3_status_t st = validate(ctx, x, m, k, n, y);
+  if (st != SAM3_OK) return st;
+  if (!idx || !palette) return set_error(ctx, SAM3_ERR_INVALID_ARG, "linear: null idx/palette");
+  if (!aligned16(idx) || !aligned16(palette) || (bias && !aligned16(bias)))
+    return set_error(ctx, SAM3_ERR_INVALID_ARG, "linear: weights must be 16-byte aligned");
+  if (epi < SAM3_EPI_BIAS || epi > SAM3_EPI_BIAS_ROPE_QKV)
+    return set_error(ctx, SAM3_ERR_INVALID_ARG, "linear: bad epilogue %d", epi);
+  if (epi == SAM3_EPI_BIAS_RESIDUAL && (!residual || !aligned16(residual)))
+    return set_error(ctx, SAM3_ERR_INVALID_ARG, "linear: residual epilogue needs aligned residual");
+  int qk_cols = 0;
+  if (epi == SAM3_EPI_BIAS_ROPE_QKV) {
+    if (!rope || rope_rows <= 0 || !aligned16(rope))
+      return set_error(ctx, SAM3_ERR_INVALID_ARG, "linear: RoPE epilogue needs a table");
+    if (n % (3 * 64))
+      return set_error(ctx, SAM3_ERR_SHAPE, "linear: RoPE epilogue needs n = 3*heads*64");
+    qk_cols = 2 * (n / 3);
+  }
+  CUtensorMap ma, mb;
+  if ((st = make_map_2d(ctx, &ma, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, x, (uint64_t)k, (uint64_t)m,
+                        BK, BM, CU_TENSOR_MAP_SWIZZLE_128B)) != SAM3_OK)
+    return st;
+  if ((st = make_map_2d(ctx, &mb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, idx, (uint64_t)k, (uint64_t)n,
+                        BK, BN, CU_TENSOR_MAP_SWIZZLE_64B)) != SAM3_OK)
+    return st;
+  GemmArgs a;
+  a.bias = reinterpret_cast<const __half*>(bias);
+  a.residual = reinterpret_cast<const __half*>(residual);
+  a.rope = rope;
+  a.palette = reinterpret_cast<const __half*>(palette);
+  a.y = reinterpret_cast<__half*>(y);
+  a.err = ctx->dev_err;
+  a.m = m;
+  a.n = n;
+  a.k = k;
+  a.epi = epi;
+  a.rope_rows = rope_rows > 0 ? rope_rows : 1;
+  a.qk_cols = qk_cols;
+  a.m_tiles = (m + BM - 1) / BM;
+  a.total_tiles = a.m_tiles * (n / BN);
+  const double bytes = 2.0 * m * k + 1.0 * n * k + 512.0 * n + 2.0 * m * n *
+                       (epi == SAM3_EPI_BIAS_RESIDUAL ? 2 : 1);
+  ProfScope prof(ctx, SAM3_PROF_GEMM, 2.0 * m * n * k, bytes);
+  return launch<kPalette>(ctx, ma, mb, a);
+}
+
+sam3_status_t gemm_dense(sam3_ctx_t* ctx, const uint16_t* x, int m, int k, const uint16_t* w,
+                         const uint16_t* bias, int n, uint16_t* y) {
+  sam3_status_t st = validate(ctx, x, m, k, n, y);
+  if (st != SAM3_OK) return st;
+  if (!w || !aligned16(w) || (bias && !aligned16(bias)))
+    return set_error(ctx, SAM3_ERR_INVALID_ARG, "dense linear: bad weight pointer");
+  CUtensorMap ma, mb;
+  if ((st = make_map_2d(ctx, &ma, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, x, (uint64_t)k, (uint64_t)m,
+                        BK, BM, CU_TENSOR_MAP_SWIZZLE_128B)) != SAM3_OK)
+    return st;
+  if ((st = make_map_2d(ctx, &mb, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, w, (uint64_t)k, (uint64_t)n,
+                        BK, BN, CU_TENSOR_MAP_SWIZZLE_128B)) != SAM3_OK)
+    return st;
+  GemmArgs a{};
+  a.bias = reinterpret_cast<const __half*>(bias);
+  a.y = reinterpret_cast<__half*>(y);
+  a.err = ctx->dev_err;
+  a.m = m;
+  a.n = n;
+  a.k = k;
+  a.epi = SAM3_EPI_BIAS;
+  a.rope_rows = 1;
+  a.m_tiles = (m + BM - 1) / BM;
+  a.total_tiles = a.m_tiles * (n / BN);
+  ProfScope prof(ctx, SAM3_PROF_PATCH, 2.0 * m * n * k, 2.0 * (m * k + n * k + m * n));
+  return launch<kDense>(ctx, ma, mb, a);
+}
+
+}  // namespace sam3
+
+using namespace sam3;
+
+extern "C" {
+
+sam3_status_t sam3_linear_palette(sam3_ctx_t* ctx, const uint16_t* x, int32_t m,
+                                  const sam3_palette_linear_t* w, int32_t epilogue,
+                                  const uint16_t* residual, const float* rope, int32_t rope_rows,
+                                  uint16_t* y) {
+  SAM3_CHECK_CTX(ctx);
+  if (!w) return set_error(ctx, SAM3_ERR_INVALID_ARG, "linear: null weights");
+  cudaSetDevice(ctx->device);
+  return gemm_palette(ctx, x, m, w->k, w->idx, w->palette, w->bias, w->n, epilogue, residual,
+                      rope, rope_rows, y);
+}
+
+sam3_status_t sam3_dequant_palette(sam3_ctx_t* ctx, const sam3_palette_linear_t* w,
+                                   uint16_t* w_out) {
+  SAM3_CHECK_CTX(ctx);
+  if (!w || !w->idx || !w->palette || !w_out)
+    return set_error(ctx, SAM3_ERR_INVALID_ARG, "dequant: null pointer");
+  if (w->n <= 0 || w->k <= 0 || w->k % 16)
+    return set_error(ctx, SAM3_ERR_SHAPE, "dequant: need k %% 16 == 0 (n=%d k=%d)", w->n, w->k);
+  if (!aligned16(w->idx) || !aligned16(w->palette) || !aligned16(w_out))
+    return set_error(ctx, SAM3_ERR_INVALID_ARG, "dequant: pointers must be 16-byte aligned");
+  cudaSetDevice(ctx->device);
+  ProfScope prof(ctx, SAM3_PROF_OTHER, 0.0, 3.0 * w->n * w->k + 512.0 * w->n);
+  dequant_kernel<<<(w->n + 7) / 8, 256, 0, ctx->stream>>>(
+      w->idx, reinterpret_cast<const __half*>(w->palette), reinterpret_cast<__half*>(w_out), w->n,
+      w->k);
+  return check_launch(ctx, "dequant_kernel");
+}
+
+}  // extern "C"

@@ -1,0 +1,109 @@
+// internal.h - context object and internal launchers shared by the .cu files
+// of libsam3cuda. Not part of the public ABI (include/sam3cuda.h is).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <string>
+#include <vector>
+
+#include "../../include/sam3cuda.h"
+
+struct sam3_ctx {
+  int device = 0;
+  int num_sms = 148;
+  cudaStream_t own_stream = nullptr;
+  cudaStream_t stream = nullptr;  // the stream operators run on
+  sam3_encoder_config_t cfg{};
+  std::string last_error;
+  int* dev_err = nullptr;  // device error word written by bounded waits
+  uint64_t launches = 0;
+
+  // Workspace arena (allocated at create, sized for cfg.max_batch images).
+  char* ws = nullptr;
+  size_t ws_bytes = 0;
+  size_t ws_used = 0;
+  // Encoder scratch carved from the arena.
+  uint16_t* x = nullptr;        // [B*S, D] residual stream
+  uint16_t* xp = nullptr;       // [B*keep, D] residual stream after pruning
+  uint16_t* ln = nullptr;       // [B*S, D]
+  uint16_t* qkv = nullptr;      // [B*S, 3D]
+  uint16_t* attn = nullptr;     // [B*S, D]
+  uint16_t* hidden = nullptr;   // [B*S, F]
+  uint16_t* cols = nullptr;     // [B*S, Kp] im2col of the patch embedding
+  uint16_t* patch_wp = nullptr; // [D, Kp] padded patch weights
+  float* scores = nullptr;      // [B*S]
+  float* rope = nullptr;        // [S, 32, 2]
+  float* rope_pruned = nullptr; // [B*keep, 32, 2]
+  int32_t* idx = nullptr;       // [B*keep]
+  uint16_t* image = nullptr;    // [B, H, W, 3] staging for the host API
+  uint16_t* feats = nullptr;    // [B*keep, D] staging for the host API
+  int rope_ready = 0;
+  // Block-level scratch used by sam3_vit_block & co. outside the encoder.
+  size_t block_rows = 0;        // rows the block scratch can hold
+
+  // Device-side stage timing (sam3_profile_enable / sam3_profile_read).
+  struct ProfRecord {
+    int cls;
+    double flops, bytes;
+    cudaEvent_t start, stop;
+  };
+  bool profiling = false;
+  std::vector<ProfRecord> prof_pending;
+  std::vector<cudaEvent_t> event_pool;
+  sam3_profile_t prof{};
+};
+
+namespace sam3 {
+
+sam3_status_t set_error(sam3_ctx_t* ctx, sam3_status_t code, const char* fmt, ...);
+sam3_status_t check_launch(sam3_ctx_t* ctx, const char* what);
+sam3_status_t check_cuda(sam3_ctx_t* ctx, cudaError_t e, const char* what);
+sam3_status_t ensure_workspace(sam3_ctx_t* ctx);
+bool aligned16(const void* p);
+
+// cuTensorMapEncodeTiled obtained through the runtime's driver entry point.
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+EncodeTiledFn encode_tiled();
+
+// Launchers (validate, then enqueue on ctx->stream).
+sam3_status_t gemm_palette(sam3_ctx_t* ctx, const uint16_t* x, int m, int k,
+                           const uint8_t* idx, const uint16_t* palette, const uint16_t* bias,
+                           int n, int epi, const uint16_t* residual, const float* rope,
+                           int rope_rows, uint16_t* y);
+sam3_status_t gemm_dense(sam3_ctx_t* ctx, const uint16_t* x, int m, int k, const uint16_t* w,
+                         const uint16_t* bias, int n, uint16_t* y);
+sam3_status_t layernorm(sam3_ctx_t* ctx, const uint16_t* x, int m, int d, const uint16_t* g,
+                        const uint16_t* b, float eps, uint16_t* y);
+sam3_status_t attention(sam3_ctx_t* ctx, const uint16_t* qkv, int batch, int seq, int heads,
+                        int head_dim, float scale, uint16_t* o);
+sam3_status_t rope_table(sam3_ctx_t* ctx, int gh, int gw, int hd, float theta, float* t);
+sam3_status_t prune(sam3_ctx_t* ctx, const uint16_t* x, int batch, int seq, int d, int keep,
+                    int norm, int order, const float* rope_in, int rope_rows, int rope_cols,
+                    uint16_t* feats, float* rope_out, int32_t* idx, float* scores_scratch);
+sam3_status_t patch_embed(sam3_ctx_t* ctx, const uint16_t* image, int batch, int h, int w,
+                          const uint16_t* pw, const uint16_t* pb, int patch, int dim,
+                          uint16_t* out, uint16_t* cols_scratch, uint16_t* wpad_scratch);
+
+// Brackets one launch with CUDA events when the context is profiling.
+class ProfScope {
+ public:
+  ProfScope(sam3_ctx_t* ctx, int cls, double flops, double bytes);
+  ~ProfScope();
+
+ private:
+  sam3_ctx_t* ctx_;
+  int idx_ = -1;
+};
+
+}  // namespace sam3
+
+#define SAM3_CHECK_CTX(ctx) \
+  do {                      \
+    if (!(ctx)) return SAM3_ERR_INVALID_ARG; \
+  } while (0)

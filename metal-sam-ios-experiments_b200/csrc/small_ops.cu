@@ -1,0 +1,545 @@
+// small_ops.cu - the HBM-bound operators of the path: LayerNorm, the RoPE
+// table and stand-alone RoPE, token scores, token pruning (radix select +
+// stable compaction + gather) and the patch-embedding im2col.
+#include <algorithm>
+
+#include "common.cuh"
+#include "internal.h"
+
+namespace sam3 {
+namespace {
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// ---------------------------------------------------------------- LayerNorm
+// One warp per row; lane owns 8-element chunks lane*8 + j*256 (coalesced
+// 512-byte warp accesses). Two-pass mean/variance in fp32 registers.
+// Reference: LayerNorm.forward, ViTEncoder.swift:795-887 (graph.normalize
+// with biased variance, epsilon 1e-6).
+template <int NCH>
+__global__ void __launch_bounds__(256) layernorm_kernel(const __half* __restrict__ x, int m,
+                                                        const __half* __restrict__ g,
+                                                        const __half* __restrict__ b, float eps,
+                                                        __half* __restrict__ y) {
+  constexpr int D = NCH * 256;
+  const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= m) return;
+  const uint4* xr = reinterpret_cast<const uint4*>(x + (size_t)row * D);
+  float v[NCH][8];
+  float s = 0.f;
+#pragma unroll
+  for (int j = 0; j < NCH; ++j) {
+    const uint4 u = __ldg(xr + lane + 32 * j);
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const float2 p = unpack_half2(w[q]);
+      v[j][2 * q] = p.x;
+      v[j][2 * q + 1] = p.y;
+      s += p.x + p.y;
+    }
+  }
+  const float mean = warp_sum(s) * (1.0f / D);
+  float var = 0.f;
+#pragma unroll
+  for (int j = 0; j < NCH; ++j)
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const float t = v[j][e] - mean;
+      var += t * t;
+    }
+  const float rstd = 1.0f / sqrtf(warp_sum(var) * (1.0f / D) + eps);
+  uint4* yr = reinterpret_cast<uint4*>(y + (size_t)row * D);
+#pragma unroll
+  for (int j = 0; j < NCH; ++j) {
+    const int c0 = (lane + 32 * j) * 8;
+    float gg[8], bb[8];
+    if (g) {
+      const uint4 u = __ldg(reinterpret_cast<const uint4*>(g + c0));
+      const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float2 p = unpack_half2(w[q]);
+        gg[2 * q] = p.x;
+        gg[2 * q + 1] = p.y;
+      }
+    } else {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) gg[e] = 1.f;
+    }
+    if (b) {
+      const uint4 u = __ldg(reinterpret_cast<const uint4*>(b + c0));
+      const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float2 p = unpack_half2(w[q]);
+        bb[2 * q] = p.x;
+        bb[2 * q + 1] = p.y;
+      }
+    } else {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) bb[e] = 0.f;
+    }
+    uint4 o;
+    uint32_t* ow = &o.x;
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+      ow[q] = pack_half2((v[j][2 * q] - mean) * rstd * gg[2 * q] + bb[2 * q],
+                         (v[j][2 * q + 1] - mean) * rstd * gg[2 * q + 1] + bb[2 * q + 1]);
+    yr[lane + 32 * j] = o;
+  }
+}
+
+// ---------------------------------------------------------------- RoPE
+// Reference: compute_rope_freqs_2d, Metal/RoPE.metal:22-52.
+__global__ void rope_table_kernel(float* __restrict__ t, int gh, int gw, int hd, float theta) {
+  const int quarter = hd / 4;
+  const int p = blockIdx.x * blockDim.y + threadIdx.y;
+  const int i = threadIdx.x;
+  if (p >= gh * gw || i >= quarter) return;
+  const int h = p / gw, w = p % gw;
+  const float freq = 1.0f / powf(theta, (float)(2 * i) / (float)(2 * quarter));
+  const float ax = (float)w * freq, ay = (float)h * freq;
+  float2* row = reinterpret_cast<float2*>(t + (size_t)p * hd);
+  row[i] = make_float2(cosf(ax), sinf(ax));
+  row[quarter + i] = make_float2(cosf(ay), sinf(ay));
+}
+
+// Reference: apply_rope_2d_batch, Metal/RoPE.metal:111-153 (packed QKV row,
+// q and k rotated, v untouched).
+__global__ void rope_apply_kernel(__half2* __restrict__ qkv, int m, int dim, int hd,
+                                  const float2* __restrict__ t, int rows) {
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (long long)m * dim) return;
+  const int row = (int)(i / dim), pr = (int)(i % dim);
+  const int col = 2 * pr;  // column inside the q|k region
+  const int j = (col % hd) / 2;
+  const float2 cs = t[(size_t)(row % rows) * (hd / 2) + j];
+  __half2* p = qkv + ((size_t)row * 3 * dim + col) / 2;
+  const float2 v = __half22float2(*p);
+  *p = __floats2half2_rn(v.x * cs.x - v.y * cs.y, v.x * cs.y + v.y * cs.x);
+}
+
+// ---------------------------------------------------------------- pruning
+// Score per token. Reference: TokenPruner.swift:54-56 (L1 = sum |x|); the
+// benchmark spec uses the L2 norm.
+__global__ void __launch_bounds__(256) token_score_kernel(const __half* __restrict__ x, int rows,
+                                                          int d, int norm,
+                                                          float* __restrict__ scores) {
+  const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const uint4* xr = reinterpret_cast<const uint4*>(x + (size_t)row * d);
+  float s = 0.f;
+  for (int c = lane; c < d / 8; c += 32) {
+    const uint4 u = __ldg(xr + c);
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const float2 p = unpack_half2(w[q]);
+      s += norm == SAM3_SCORE_L1 ? fabsf(p.x) + fabsf(p.y) : p.x * p.x + p.y * p.y;
+    }
+  }
+  s = warp_sum(s);
+  if (lane == 0) scores[row] = norm == SAM3_SCORE_L1 ? s : sqrtf(s);
+}
+
+__device__ __forceinline__ uint32_t order_key(float f) {
+  const uint32_t b = __float_as_uint(f);
+  return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+
+// Block-wide exclusive scan of per-thread counts (1024 threads).
+__device__ __forceinline__ int block_exclusive_scan(int v, int* warp_sums, int* total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int inc = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int t = __shfl_up_sync(0xffffffffu, inc, o);
+    if (lane >= o) inc += t;
+  }
+  if (lane == 31) warp_sums[warp] = inc;
+  __syncthreads();
+  if (warp == 0) {
+    int w = warp_sums[lane];
+    int wi = w;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int t = __shfl_up_sync(0xffffffffu, wi, o);
+      if (lane >= o) wi += t;
+    }
+    warp_sums[lane] = wi - w;
+    if (lane == 31) *total = wi;
+  }
+  __syncthreads();
+  const int r = warp_sums[warp] + inc - v;
+  __syncthreads();
+  return r;
+}
+
+// One CTA (1024 threads) per image: 4 passes of 8-bit radix selection find
+// the keep-th largest score key T and how many ties at T to take; ties go to
+// the lower token index; a stable compaction emits the kept indices in
+// ascending order, or a bitonic sort orders them by (score desc, index asc).
+// Reference: the topK of TokenPruner.swift:59-60 (MPSGraph, ties undefined).
+__global__ void __launch_bounds__(1024) prune_select_kernel(const float* __restrict__ scores,
+                                                            int seq, int keep, int order,
+                                                            int32_t* __restrict__ idx_out) {
+  extern __shared__ __align__(16) uint8_t sm[];
+  uint32_t* keys = reinterpret_cast<uint32_t*>(sm);
+  __shared__ int hist[256];
+  __shared__ int warp_sums[32];
+  __shared__ int s_total;
+  __shared__ uint32_t s_prefix;
+  __shared__ int s_needed;
+  const int b = blockIdx.x;
+  const float* sc = scores + (size_t)b * seq;
+  for (int i = threadIdx.x; i < seq; i += blockDim.x) keys[i] = order_key(sc[i]);
+  if (threadIdx.x == 0) {
+    s_prefix = 0;
+    s_needed = keep;
+  }
+  __syncthreads();
+  uint32_t mask = 0;
+  for (int pass = 0; pass < 4; ++pass) {
+    const int shift = 24 - 8 * pass;
+    for (int i = threadIdx.x; i < 256; i += blockDim.x) hist[i] = 0;
+    __syncthreads();
+    const uint32_t prefix = s_prefix;
+    for (int i = threadIdx.x; i < seq; i += blockDim.x)
+      if ((keys[i] & mask) == prefix) atomicAdd(&hist[(keys[i] >> shift) & 255u], 1);
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      int cum = 0, need = s_needed;
+      for (int dgt = 255; dgt >= 0; --dgt) {
+        if (cum + hist[dgt] >= need) {
+          s_prefix = prefix | ((uint32_t)dgt << shift);
+          s_needed = need - cum;
+          break;
+        }
+        cum += hist[dgt];
+      }
+    }
+    mask |= 255u << shift;
+    __syncthreads();
+  }
+  const uint32_t T = s_prefix;
+  const int ties = s_needed;  // how many tokens with key == T to keep
+
+  // Contiguous chunk per thread keeps index order inside the scans.
+  const int per = (seq + blockDim.x - 1) / blockDim.x;
+  const int lo = threadIdx.x * per, hi = min(seq, lo + per);
+  int n_eq = 0;
+  for (int i = lo; i < hi; ++i) n_eq += keys[i] == T;
+  const int eq0 = block_exclusive_scan(n_eq, warp_sums, &s_total);  // ties before my chunk
+  int eq_rank = eq0, n_sel = 0;
+  for (int i = lo; i < hi; ++i) {
+    const uint32_t k = keys[i];
+    if (k > T) ++n_sel;
+    else if (k == T) n_sel += (eq_rank++ < ties);
+  }
+  int pos = block_exclusive_scan(n_sel, warp_sums, &s_total);
+  eq_rank = eq0;
+  int32_t* out = idx_out + (size_t)b * keep;
+  if (order == SAM3_ORDER_INDEX) {
+    for (int i = lo; i < hi; ++i) {
+      const uint32_t k = keys[i];
+      bool take = k > T;
+      if (k == T) take = eq_rank++ < ties;
+      if (take) out[pos++] = i;
+    }
+    return;
+  }
+  // SAM3_ORDER_SCORE: bitonic sort of (~key << 32 | index) ascending.
+  int p2 = 1;
+  while (p2 < keep) p2 <<= 1;
+  unsigned long long* sk = reinterpret_cast<unsigned long long*>(sm + (((size_t)seq * 4 + 15) & ~15));
+  for (int i = threadIdx.x; i < p2; i += blockDim.x) sk[i] = ~0ull;
+  __syncthreads();
+  for (int i = lo; i < hi; ++i) {
+    const uint32_t k = keys[i];
+    bool take = k > T;
+    if (k == T) take = eq_rank++ < ties;
+    if (take) sk[pos++] = ((unsigned long long)(~k) << 32) | (uint32_t)i;
+  }
+  __syncthreads();
+  for (int size = 2; size <= p2; size <<= 1)
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      for (int i = threadIdx.x; i < p2; i += blockDim.x) {
+        const int j = i ^ stride;
+        if (j > i) {
+          const bool up = (i & size) == 0;
+          const unsigned long long a = sk[i], c = sk[j];
+          if ((a > c) == up) {
+            sk[i] = c;
+            sk[j] = a;
+          }
+        }
+      }
+      __syncthreads();
+    }
+  for (int i = threadIdx.x; i < keep; i += blockDim.x) out[i] = (int32_t)(sk[i] & 0xffffffffu);
+}
+
+// Gather kept rows (features fp16, RoPE rows f32). One warp per output row.
+__global__ void __launch_bounds__(256) prune_gather_kernel(
+    const __half* __restrict__ x, int seq, int d, int keep, const int32_t* __restrict__ idx,
+    const float* __restrict__ rope_in, int rope_rows, int rope_cols, __half* __restrict__ feats,
+    float* __restrict__ rope_out, int total) {
+  const int r = blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (r >= total) return;
+  const int b = r / keep;
+  const long long src = (long long)b * seq + idx[r];
+  const uint4* s = reinterpret_cast<const uint4*>(x + src * d);
+  uint4* dst = reinterpret_cast<uint4*>(feats + (size_t)r * d);
+  for (int c = lane; c < d / 8; c += 32) dst[c] = __ldg(s + c);
+  if (rope_in && rope_out) {
+    const float* rs = rope_in + (size_t)(src % rope_rows) * rope_cols;
+    float* rd = rope_out + (size_t)r * rope_cols;
+    for (int c = lane; c < rope_cols; c += 32) rd[c] = __ldg(rs + c);
+  }
+}
+
+// ---------------------------------------------------------------- patch embedding
+// im2col of an NHWC fp16 image into [tokens, kp] rows (k = c*P*P + ky*P + kx,
+// the PyTorch conv-weight order), zero-padded from 3*P*P up to kp.
+__global__ void im2col_kernel(const __half* __restrict__ img, int batch, int h, int w, int patch,
+                              int kp, __half* __restrict__ cols) {
+  const int gw = w / patch, gh = h / patch;
+  const long long total = (long long)batch * gh * gw * kp;
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= total) return;
+  const int k = (int)(i % kp);
+  const long long t = i / kp;
+  const int pp = patch * patch;
+  __half v = __float2half(0.f);
+  if (k < 3 * pp) {
+    const int c = k / pp, ky = (k % pp) / patch, kx = k % patch;
+    const int b = (int)(t / ((long long)gh * gw));
+    const int p = (int)(t % ((long long)gh * gw));
+    const int yy = (p / gw) * patch + ky, xx = (p % gw) * patch + kx;
+    v = img[(((size_t)b * h + yy) * w + xx) * 3 + c];
+  }
+  cols[i] = v;
+}
+
+__global__ void pad_weight_kernel(const __half* __restrict__ w, int n, int k, int kp,
+                                  __half* __restrict__ wp) {
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (long long)n * kp) return;
+  const int c = (int)(i % kp);
+  const long long r = i / kp;
+  wp[i] = c < k ? w[r * k + c] : __float2half(0.f);
+}
+
+int blocks_for(long long n, int t) { return (int)((n + t - 1) / t); }
+
+}  // namespace
+
+sam3_status_t layernorm(sam3_ctx_t* ctx, const uint16_t* x, int m, int d, const uint16_t* g,
+                        const uint16_t* b, float eps, uint16_t* y) {
+  if (!x || !y) return set_error(ctx, SAM3_ERR_INVALID_ARG, "layernorm: null pointer");
+  if (m <= 0 || d <= 0) return set_error(ctx, SAM3_ERR_SHAPE, "layernorm: empty shape");
+  if (!aligned16(x) || !aligned16(y) || (g && !aligned16(g)) || (b && !aligned16(b)))
+    return set_error(ctx, SAM3_ERR_INVALID_ARG, "layernorm: pointers must be 16-byte aligned");
+  const __half* hx = reinterpret_cast<const __half*>(x);
+  const __half* hg = reinterpret_cast<const __half*>(g);
+  const __half* hb = reinterpret_cast<const __half*>(b);
+  __half* hy = reinterpret_cast<__half*>(y);
+  const int grid = blocks_for(m, 8);
+  ProfScope prof(ctx, SAM3_PROF_LAYERNORM, 0.0, 4.0 * m * d);
+  switch (d) {
+    case 256: layernorm_kernel<1><<<grid, 256, 0, ctx->stream>>>(hx, m, hg, hb, eps, hy); break;
+    case 512: layernorm_kernel<2><<<grid, 256, 0, ctx->stream>>>(hx, m, hg, hb, eps, hy); break;
+    case 768: layernorm_kernel<3><<<grid, 256, 0, ctx->stream>>>(hx, m, hg, hb, eps, hy); break;
+    case 1024: layernorm_kernel<4><<<grid, 256, 0, ctx->stream>>>(hx, m, hg, hb, eps, hy); break;
+    case 1280: layernorm_kernel<5><<<grid, 256, 0, ctx->stream>>>(hx, m, hg, hb, eps, hy); break;
+    case 1536: layernorm_kernel<6><<<grid, 256, 0, ctx->stream>>>(hx, m, hg, hb, eps, hy); break;
+    case 2048: layernorm_kernel<8><<<grid, 256, 0, ctx->stream>>>(hx, m, hg, hb, eps, hy); break;
+    default:
+      return set_error(ctx, SAM3_ERR_SHAPE, "layernorm: d=%d unsupported (256..2048, step 256)", d);
+  }
+  return check_launch(ctx, "layernorm_kernel");
+}
+
+sam3_status_t rope_table(sam3_ctx_t* ctx, int gh, int gw, int hd, float theta, float* t) {
+  if (!t) return set_error(ctx, SAM3_ERR_INVALID_ARG, "rope_table: null table");
+  if (gh <= 0 || gw <= 0 || hd <= 0 || hd % 4 || hd > 256)
+    return set_error(ctx, SAM3_ERR_SHAPE, "rope_table: bad grid/head_dim");
+  const int quarter = hd / 4;
+  const int per = std::max(1, 256 / quarter);
+  ProfScope prof(ctx, SAM3_PROF_OTHER, 0.0, 4.0 * gh * gw * hd);
+  rope_table_kernel<<<blocks_for((long long)gh * gw, per), dim3(quarter, per), 0, ctx->stream>>>(
+      t, gh, gw, hd, theta);
+  return check_launch(ctx, "rope_table_kernel");
+}
+
+sam3_status_t prune(sam3_ctx_t* ctx, const uint16_t* x, int batch, int seq, int d, int keep,
+                    int norm, int order, const float* rope_in, int rope_rows, int rope_cols,
+                    uint16_t* feats, float* rope_out, int32_t* idx, float* scores) {
+  if (!x || !feats || !idx || !scores)
+    return set_error(ctx, SAM3_ERR_INVALID_ARG, "prune: null pointer");
+  if (batch <= 0 || seq <= 0 || d <= 0 || d % 8 || keep <= 0 || keep > seq || seq > 16384)
+    return set_error(ctx, SAM3_ERR_SHAPE, "prune: bad shape batch=%d seq=%d d=%d keep=%d", batch,
+                     seq, d, keep);
+  if (norm != SAM3_SCORE_L2 && norm != SAM3_SCORE_L1)
+    return set_error(ctx, SAM3_ERR_INVALID_ARG, "prune: bad norm");
+  if (order != SAM3_ORDER_INDEX && order != SAM3_ORDER_SCORE)
+    return set_error(ctx, SAM3_ERR_INVALID_ARG, "prune: bad order");
+  if (order == SAM3_ORDER_SCORE && keep > 8192)
+    return set_error(ctx, SAM3_ERR_SHAPE, "prune: score order supports keep <= 8192");
+  if ((rope_in == nullptr) != (rope_out == nullptr) || (rope_in && (rope_rows <= 0 || rope_cols <= 0)))
+    return set_error(ctx, SAM3_ERR_INVALID_ARG, "prune: rope_in/rope_out mismatch");
+  if (!aligned16(x) || !aligned16(feats))
+    return set_error(ctx, SAM3_ERR_INVALID_ARG, "prune: x/feats must be 16-byte aligned");
+  const long long rows = (long long)batch * seq;
+  sam3_status_t st;
+  {
+    ProfScope prof(ctx, SAM3_PROF_PRUNE, 0.0, 2.0 * rows * d + 4.0 * rows);
+    token_score_kernel<<<blocks_for(rows, 8), 256, 0, ctx->stream>>>(
+        reinterpret_cast<const __half*>(x), (int)rows, d, norm, scores);
+    st = check_launch(ctx, "token_score_kernel");
+  }
+  if (st != SAM3_OK) return st;
+  size_t smem = ((size_t)seq * 4 + 15) & ~(size_t)15;
+  if (order == SAM3_ORDER_SCORE) {
+    int p2 = 1;
+    while (p2 < keep) p2 <<= 1;
+    smem += (size_t)p2 * 8;
+  }
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(prune_select_kernel,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return check_cuda(ctx, e, "prune smem attribute");
+  }
+  {
+    ProfScope prof(ctx, SAM3_PROF_PRUNE, 0.0, 4.0 * rows + 4.0 * batch * keep);
+    prune_select_kernel<<<batch, 1024, smem, ctx->stream>>>(scores, seq, keep, order, idx);
+    if ((st = check_launch(ctx, "prune_select_kernel")) != SAM3_OK) return st;
+  }
+  const int total = batch * keep;
+  ProfScope prof(ctx, SAM3_PROF_PRUNE, 0.0,
+                 4.0 * total * d + (rope_in ? 8.0 * total * rope_cols : 0.0) + 4.0 * total);
+  prune_gather_kernel<<<blocks_for(total, 8), 256, 0, ctx->stream>>>(
+      reinterpret_cast<const __half*>(x), seq, d, keep, idx, rope_in, rope_rows > 0 ? rope_rows : 1,
+      rope_cols, reinterpret_cast<__half*>(feats), rope_out, total);
+  return check_launch(ctx, "prune_gather_kernel");
+}
+
+sam3_status_t patch_embed(sam3_ctx_t* ctx, const uint16_t* image, int batch, int h, int w,
+                          const uint16_t* pw, const uint16_t* pb, int patch, int dim,
+                          uint16_t* out, uint16_t* cols, uint16_t* wpad) {
+  if (!image || !pw || !out || !cols || !wpad)
+    return set_error(ctx, SAM3_ERR_INVALID_ARG, "patch_embed: null pointer");
+  if (batch <= 0 || patch <= 0 || h % patch || w % patch || dim % 128)
+    return set_error(ctx, SAM3_ERR_SHAPE, "patch_embed: bad shape");
+  const int k = 3 * patch * patch;
+  const int kp = (k + 63) / 64 * 64;
+  const long long tokens = (long long)batch * (h / patch) * (w / patch);
+  sam3_status_t st;
+  {
+    ProfScope prof(ctx, SAM3_PROF_PATCH, 0.0, 2.0 * tokens * k + 2.0 * tokens * kp);
+  im2col_kernel<<<blocks_for(tokens * kp, 256), 256, 0, ctx->stream>>>(
+      reinterpret_cast<const __half*>(image), batch, h, w, patch, kp,
+      reinterpret_cast<__half*>(cols));
+  st = check_launch(ctx, "im2col_kernel");
+  if (st != SAM3_OK) return st;
+  }
+  {
+    ProfScope prof(ctx, SAM3_PROF_PATCH, 0.0, 2.0 * dim * k + 2.0 * dim * kp);
+  pad_weight_kernel<<<blocks_for((long long)dim * kp, 256), 256, 0, ctx->stream>>>(
+      reinterpret_cast<const __half*>(pw), dim, k, kp, reinterpret_cast<__half*>(wpad));
+  if ((st = check_launch(ctx, "pad_weight_kernel")) != SAM3_OK) return st;
+  }
+  return gemm_dense(ctx, cols, (int)tokens, kp, wpad, pb, dim, out);
+}
+
+}  // namespace sam3
+
+using namespace sam3;
+
+extern "C" {
+
+sam3_status_t sam3_layernorm(sam3_ctx_t* ctx, const uint16_t* x, int32_t m, int32_t d,
+                             const uint16_t* gamma, const uint16_t* beta, float eps, uint16_t* y) {
+  SAM3_CHECK_CTX(ctx);
+  cudaSetDevice(ctx->device);
+  return layernorm(ctx, x, m, d, gamma, beta, eps, y);
+}
+
+sam3_status_t sam3_rope_table(sam3_ctx_t* ctx, int32_t gh, int32_t gw, int32_t hd, float theta,
+                              float* table) {
+  SAM3_CHECK_CTX(ctx);
+  cudaSetDevice(ctx->device);
+  return rope_table(ctx, gh, gw, hd, theta, table);
+}
+
+sam3_status_t sam3_rope_apply(sam3_ctx_t* ctx, uint16_t* qkv, int32_t m, int32_t heads,
+                              int32_t hd, const float* table, int32_t rope_rows) {
+  SAM3_CHECK_CTX(ctx);
+  if (!qkv || !table) return set_error(ctx, SAM3_ERR_INVALID_ARG, "rope_apply: null pointer");
+  if (m <= 0 || heads <= 0 || hd <= 0 || hd % 2 || rope_rows <= 0)
+    return set_error(ctx, SAM3_ERR_SHAPE, "rope_apply: bad shape");
+  if (reinterpret_cast<uintptr_t>(qkv) & 3u)
+    return set_error(ctx, SAM3_ERR_INVALID_ARG, "rope_apply: qkv must be 4-byte aligned");
+  cudaSetDevice(ctx->device);
+  const int dim = heads * hd;
+  ProfScope prof(ctx, SAM3_PROF_OTHER, 0.0, 8.0 * m * dim + 8.0 * m * hd / 2);
+  rope_apply_kernel<<<blocks_for((long long)m * dim, 256), 256, 0, ctx->stream>>>(
+      reinterpret_cast<__half2*>(qkv), m, dim, hd, reinterpret_cast<const float2*>(table),
+      rope_rows);
+  return check_launch(ctx, "rope_apply_kernel");
+}
+
+sam3_status_t sam3_token_scores(sam3_ctx_t* ctx, const uint16_t* x, int32_t rows, int32_t d,
+                                int32_t norm, float* scores) {
+  SAM3_CHECK_CTX(ctx);
+  if (!x || !scores) return set_error(ctx, SAM3_ERR_INVALID_ARG, "token_scores: null pointer");
+  if (rows <= 0 || d <= 0 || d % 8) return set_error(ctx, SAM3_ERR_SHAPE, "token_scores: bad shape");
+  if (norm != SAM3_SCORE_L2 && norm != SAM3_SCORE_L1)
+    return set_error(ctx, SAM3_ERR_INVALID_ARG, "token_scores: bad norm");
+  if (!aligned16(x)) return set_error(ctx, SAM3_ERR_INVALID_ARG, "token_scores: x alignment");
+  cudaSetDevice(ctx->device);
+  ProfScope prof(ctx, SAM3_PROF_PRUNE, 0.0, 2.0 * rows * d + 4.0 * rows);
+  token_score_kernel<<<blocks_for(rows, 8), 256, 0, ctx->stream>>>(
+      reinterpret_cast<const __half*>(x), rows, d, norm, scores);
+  return check_launch(ctx, "token_score_kernel");
+}
+
+sam3_status_t sam3_prune(sam3_ctx_t* ctx, const uint16_t* x, int32_t batch, int32_t seq, int32_t d,
+                         int32_t keep, int32_t norm, int32_t order, const float* rope_in,
+                         int32_t rope_rows, int32_t rope_cols, uint16_t* feats, float* rope_out,
+                         int32_t* idx) {
+  SAM3_CHECK_CTX(ctx);
+  cudaSetDevice(ctx->device);
+  if ((long long)batch * seq > (long long)ctx->block_rows) {
+    // scores scratch lives in the workspace; grow it outside any hot loop
+    return set_error(ctx, SAM3_ERR_SHAPE, "prune: batch*seq=%lld exceeds context capacity %zu",
+                     (long long)batch * seq, ctx->block_rows);
+  }
+  return prune(ctx, x, batch, seq, d, keep, norm, order, rope_in, rope_rows, rope_cols, feats,
+               rope_out, idx, ctx->scores);
+}
+
+sam3_status_t sam3_patch_embed(sam3_ctx_t* ctx, const uint16_t* image, int32_t batch, int32_t h,
+                               int32_t w, const uint16_t* pw, const uint16_t* pb, int32_t patch,
+                               int32_t dim, uint16_t* out) {
+  SAM3_CHECK_CTX(ctx);
+  cudaSetDevice(ctx->device);
+  const int k = 3 * patch * patch, kp = (k + 63) / 64 * 64;
+  const size_t tokens = (size_t)batch * (h / (patch > 0 ? patch : 1)) * (w / (patch > 0 ? patch : 1));
+  const sam3_encoder_config_t& c = ctx->cfg;
+  const size_t cap_cols = ctx->block_rows * (size_t)((3 * c.patch * c.patch + 63) / 64 * 64);
+  if (patch <= 0 || tokens * kp > cap_cols || (size_t)dim * kp > (size_t)c.embed_dim *
+                                                                     ((3 * c.patch * c.patch + 63) / 64 * 64))
+    return set_error(ctx, SAM3_ERR_SHAPE, "patch_embed: shape exceeds context workspace");
+  return patch_embed(ctx, image, batch, h, w, pw, pb, patch, dim, out, ctx->cols, ctx->patch_wp);
+}
+
+}  // extern "C"

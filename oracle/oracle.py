@@ -1,0 +1,308 @@
+"""numpy front end for the CPU oracle (oracle/libsam3oracle.so).
+
+TEST INFRASTRUCTURE ONLY: imported by tests/, by ``__graft_entry__.smoke()``
+and by the CPU-baseline leg of ``bench.py``. The product library never loads
+it. PARITY UNPINNED against the reference itself (its Swift/Metal path cannot
+run here); pinned by known-answer tests and an independent float64
+restatement (tests/golden).
+
+fp16 tensors travel as ``np.float16`` arrays (bit-identical to uint16 views).
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import subprocess
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+_LIB_PATH = os.path.join(_HERE, "libsam3oracle.so")
+
+EPI_BIAS, EPI_BIAS_GELU, EPI_BIAS_RESIDUAL, EPI_BIAS_ROPE_QKV = 0, 1, 2, 3
+SCORE_L2, SCORE_L1 = 0, 1
+ORDER_INDEX, ORDER_SCORE = 0, 1
+
+_lib = None
+
+
+def build() -> str:
+    """Compile the oracle if the shared object is missing or stale."""
+    src = os.path.join(_HERE, "sam3_oracle.cpp")
+    if (not os.path.exists(_LIB_PATH)
+            or os.path.getmtime(_LIB_PATH) < os.path.getmtime(src)):
+        subprocess.check_call(["make", "-s", "-C", _HERE])
+    return _LIB_PATH
+
+
+def lib() -> C.CDLL:
+    global _lib
+    if _lib is None:
+        if not os.path.exists(_LIB_PATH):
+            build()
+        _lib = C.CDLL(_LIB_PATH)
+        _declare(_lib)
+    return _lib
+
+
+class PaletteLinear(C.Structure):
+    _fields_ = [("idx", C.c_void_p), ("palette", C.c_void_p), ("bias", C.c_void_p),
+                ("n", C.c_int32), ("k", C.c_int32)]
+
+
+class BlockWeights(C.Structure):
+    _fields_ = [("ln1_gamma", C.c_void_p), ("ln1_beta", C.c_void_p),
+                ("qkv", PaletteLinear), ("proj", PaletteLinear),
+                ("ln2_gamma", C.c_void_p), ("ln2_beta", C.c_void_p),
+                ("fc1", PaletteLinear), ("fc2", PaletteLinear)]
+
+
+def _declare(L):
+    P, I64, I, F, U64 = C.c_void_p, C.c_int64, C.c_int, C.c_float, C.c_uint64
+    sig = {
+        "so_gen_normal_f16": [U64, U64, I64, F, F, P],
+        "so_gen_uniform_f16": [U64, U64, I64, F, F, P],
+        "so_gen_uniform_u8": [U64, U64, I64, P],
+        "so_gen_palette": [U64, U64, I64, F, P],
+        "so_dequant": [P, P, I64, I64, P],
+        "so_linear": [P, I64, P, P, P, I64, I64, I, P, P, I64, I, I, P],
+        "so_linear_dense": [P, I64, P, P, I64, I64, P],
+        "so_layernorm": [P, I64, I64, P, P, F, P],
+        "so_rope_table": [I, I, I, F, P],
+        "so_rope_apply": [P, I64, I, I, P, I64],
+        "so_attention": [P, I, I64, I, I, F, P],
+        "so_token_scores": [P, I64, I64, I, P],
+        "so_select_topk": [P, I, I64, I64, I, P],
+        "so_prune": [P, I, I64, I64, I64, I, I, P, I64, I, P, P, P],
+        "so_patch_embed": [P, I, I, I, P, P, I, I, P],
+        "so_vit_block": [P, I, I64, I, I, F, P, P, I64],
+        "so_encoder_forward": [P, I, I, I, I, I, I, I, I64, I, I, F, F, P, P, P, P, P],
+    }
+    for name, args in sig.items():
+        fn = getattr(L, name)
+        fn.argtypes = args
+        fn.restype = None
+    L.so_num_threads.restype = C.c_int
+    L.so_half_to_float.argtypes = [C.c_uint16]
+    L.so_half_to_float.restype = C.c_float
+    L.so_float_to_half.argtypes = [C.c_float]
+    L.so_float_to_half.restype = C.c_uint16
+
+
+def _p(a):
+    return None if a is None else a.ctypes.data_as(C.c_void_p)
+
+
+def _c(a, dtype):
+    a = np.ascontiguousarray(a, dtype=dtype)
+    return a
+
+
+def num_threads() -> int:
+    return lib().so_num_threads()
+
+
+# ---- generators ---------------------------------------------------------------
+def gen_normal(seed, stream, shape, mean=0.0, std=1.0):
+    out = np.empty(shape, np.float16)
+    lib().so_gen_normal_f16(seed, stream, out.size, mean, std, _p(out))
+    return out
+
+
+def gen_uniform(seed, stream, shape, lo=-1.0, hi=1.0):
+    out = np.empty(shape, np.float16)
+    lib().so_gen_uniform_f16(seed, stream, out.size, lo, hi, _p(out))
+    return out
+
+
+def gen_u8(seed, stream, shape):
+    out = np.empty(shape, np.uint8)
+    lib().so_gen_uniform_u8(seed, stream, out.size, _p(out))
+    return out
+
+
+def gen_palette(seed, stream, rows, std=0.02):
+    out = np.empty((rows, 256), np.float16)
+    lib().so_gen_palette(seed, stream, rows, std, _p(out))
+    return out
+
+
+# ---- operators ----------------------------------------------------------------
+def dequant(idx, palette):
+    idx = _c(idx, np.uint8)
+    palette = _c(palette, np.float16)
+    n, k = idx.shape
+    out = np.empty((n, k), np.float16)
+    lib().so_dequant(_p(idx), _p(palette), n, k, _p(out))
+    return out
+
+
+def linear(x, idx, palette, bias, epilogue=EPI_BIAS, residual=None, rope=None,
+           rope_period=1, heads=16, head_dim=64):
+    x = _c(x, np.float16)
+    idx = _c(idx, np.uint8)
+    palette = _c(palette, np.float16)
+    bias = None if bias is None else _c(bias, np.float16)
+    residual = None if residual is None else _c(residual, np.float16)
+    rope = None if rope is None else _c(rope, np.float32)
+    m, k = x.shape
+    n = idx.shape[0]
+    y = np.empty((m, n), np.float16)
+    lib().so_linear(_p(x), m, _p(idx), _p(palette), _p(bias), n, k, epilogue,
+                    _p(residual), _p(rope), rope_period, heads, head_dim, _p(y))
+    return y
+
+
+def linear_dense(x, w, bias):
+    x = _c(x, np.float16)
+    w = _c(w, np.float16)
+    bias = None if bias is None else _c(bias, np.float16)
+    m, k = x.shape
+    n = w.shape[0]
+    y = np.empty((m, n), np.float16)
+    lib().so_linear_dense(_p(x), m, _p(w), _p(bias), n, k, _p(y))
+    return y
+
+
+def layernorm(x, gamma=None, beta=None, eps=1e-6):
+    x = _c(x, np.float16)
+    m, d = x.shape
+    g = None if gamma is None else _c(gamma, np.float16)
+    b = None if beta is None else _c(beta, np.float16)
+    y = np.empty_like(x)
+    lib().so_layernorm(_p(x), m, d, _p(g), _p(b), eps, _p(y))
+    return y
+
+
+def rope_table(grid_h, grid_w, head_dim=64, theta=10000.0):
+    t = np.empty((grid_h * grid_w, head_dim // 2, 2), np.float32)
+    lib().so_rope_table(grid_h, grid_w, head_dim, theta, _p(t))
+    return t
+
+
+def rope_apply(qkv, heads, head_dim, table, rope_period):
+    qkv = np.array(qkv, dtype=np.float16, copy=True, order="C")
+    table = _c(table, np.float32)
+    lib().so_rope_apply(_p(qkv), qkv.shape[0], heads, head_dim, _p(table), rope_period)
+    return qkv
+
+
+def attention(qkv, batch, seq, heads, head_dim, scale=None):
+    qkv = _c(qkv, np.float16)
+    if scale is None:
+        scale = 1.0 / np.sqrt(head_dim)
+    o = np.empty((batch * seq, heads * head_dim), np.float16)
+    lib().so_attention(_p(qkv), batch, seq, heads, head_dim, float(scale), _p(o))
+    return o
+
+
+def token_scores(x, norm=SCORE_L2):
+    x = _c(x, np.float16)
+    s = np.empty(x.shape[0], np.float32)
+    lib().so_token_scores(_p(x), x.shape[0], x.shape[1], norm, _p(s))
+    return s
+
+
+def select_topk(scores, batch, seq, keep, order=ORDER_INDEX):
+    scores = _c(scores, np.float32)
+    idx = np.empty((batch, keep), np.int32)
+    lib().so_select_topk(_p(scores), batch, seq, keep, order, _p(idx))
+    return idx
+
+
+def prune(x, batch, seq, keep, norm=SCORE_L2, order=ORDER_INDEX, rope=None,
+          rope_period=None):
+    x = _c(x, np.float16)
+    d = x.shape[1]
+    feats = np.empty((batch * keep, d), np.float16)
+    idx = np.empty((batch, keep), np.int32)
+    rope_out = None
+    cols = 0
+    if rope is not None:
+        rope = _c(rope, np.float32)
+        cols = int(np.prod(rope.shape[1:]))
+        rope_out = np.empty((batch * keep,) + tuple(rope.shape[1:]), np.float32)
+        if rope_period is None:
+            rope_period = rope.shape[0]
+    lib().so_prune(_p(x), batch, seq, d, keep, norm, order, _p(rope),
+                   rope_period or 1, cols, _p(feats), _p(rope_out), _p(idx))
+    return feats, rope_out, idx
+
+
+def patch_embed(image, w, bias, patch=14):
+    image = _c(image, np.float16)
+    w = _c(w, np.float16)
+    bias = _c(bias, np.float16)
+    b, h, wd, _ = image.shape
+    dim = w.shape[0]
+    out = np.empty((b * (h // patch) * (wd // patch), dim), np.float16)
+    lib().so_patch_embed(_p(image), b, h, wd, _p(w), _p(bias), patch, dim, _p(out))
+    return out
+
+
+# ---- weights ----------------------------------------------------------------------
+class SyntheticBlock:
+    """Seeded palettized block weights with the benchmark distributions:
+    idx ~ U{0..255}, palette ~ N(0, 0.02) sorted ascending per row,
+    bias ~ N(0, 0.01), LN gamma = 1, beta = 0."""
+
+    def __init__(self, seed, layer, dim=1024, hidden=4096):
+        def lin(name, n, k, tag):
+            s = 1000 * layer + tag
+            return {"idx": gen_u8(seed, s + 1, (n, k)),
+                    "palette": gen_palette(seed, s + 2, n, 0.02),
+                    "bias": gen_normal(seed, s + 3, (n,), 0.0, 0.01)}
+        self.dim, self.hidden = dim, hidden
+        self.ln1_gamma = np.ones(dim, np.float16)
+        self.ln1_beta = np.zeros(dim, np.float16)
+        self.ln2_gamma = np.ones(dim, np.float16)
+        self.ln2_beta = np.zeros(dim, np.float16)
+        self.qkv = lin("qkv", 3 * dim, dim, 10)
+        self.proj = lin("proj", dim, dim, 20)
+        self.fc1 = lin("fc1", hidden, dim, 30)
+        self.fc2 = lin("fc2", dim, hidden, 40)
+
+    def linears(self):
+        return {"qkv": self.qkv, "proj": self.proj, "fc1": self.fc1, "fc2": self.fc2}
+
+    def as_struct(self) -> BlockWeights:
+        def pl(d):
+            return PaletteLinear(_p(d["idx"]).value, _p(d["palette"]).value,
+                                 _p(d["bias"]).value, d["idx"].shape[0], d["idx"].shape[1])
+        return BlockWeights(_p(self.ln1_gamma).value, _p(self.ln1_beta).value,
+                            pl(self.qkv), pl(self.proj),
+                            _p(self.ln2_gamma).value, _p(self.ln2_beta).value,
+                            pl(self.fc1), pl(self.fc2))
+
+
+def vit_block(x, batch, seq, heads, block: SyntheticBlock, rope, rope_period,
+              ln_eps=1e-6):
+    x = np.array(x, dtype=np.float16, copy=True, order="C")
+    rope = _c(rope, np.float32)
+    w = block.as_struct()
+    lib().so_vit_block(_p(x), batch, seq, x.shape[1], heads, ln_eps, C.byref(w),
+                       _p(rope), rope_period)
+    return x
+
+
+def encoder_forward(image, blocks, patch_w, patch_b, heads=16, patch=14,
+                    prune_after=16, keep=None, norm=SCORE_L2, order=ORDER_INDEX,
+                    ln_eps=1e-6, theta=10000.0):
+    image = _c(image, np.float16)
+    b, size, _, _ = image.shape
+    grid = size // patch
+    seq = grid * grid
+    dim = patch_w.shape[0]
+    if keep is None:
+        keep = seq // 2
+    pruned = 0 < prune_after <= len(blocks) and keep < seq
+    rows = keep if pruned else seq
+    arr = (BlockWeights * len(blocks))(*[blk.as_struct() for blk in blocks])
+    feats = np.empty((b, rows, dim), np.float16)
+    idx = np.empty((b, rows), np.int32)
+    patch_w = _c(patch_w, np.float16)
+    patch_b = _c(patch_b, np.float16)
+    lib().so_encoder_forward(_p(image), b, size, patch, dim, heads, len(blocks),
+                             prune_after, keep, norm, order, ln_eps, theta,
+                             _p(patch_w), _p(patch_b), arr, _p(feats), _p(idx))
+    return feats, idx

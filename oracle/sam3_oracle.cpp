@@ -1,0 +1,510 @@
+// sam3_oracle.cpp - CPU restatement of the SAM3 palettized ViT-encoder path.
+//
+// TEST INFRASTRUCTURE ONLY (the checker; never part of libsam3cuda).
+// PARITY UNPINNED against the reference itself (Swift/Metal/MPSGraph cannot run
+// here and the reference ships no golden vectors for this path); pinned by
+// known-answer tests from the reference formulas and by an independent float64
+// restatement (tests/golden/make_golden.py).
+//
+// Reference citations are relative to the reference project root
+// (OrdoSAM3Sensor/Sources/Sam3Sensor/...).
+#include "sam3_oracle.h"
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <numeric>
+#include <vector>
+
+#ifdef _OPENMP
+#include <omp.h>
+#endif
+
+namespace {
+
+typedef float v8f __attribute__((vector_size(32)));
+
+inline float h2f(uint16_t h) {
+  _Float16 v;
+  std::memcpy(&v, &h, 2);
+  return (float)v;
+}
+inline uint16_t f2h(float f) {
+  _Float16 v = (_Float16)f;  // IEEE round-to-nearest-even
+  uint16_t h;
+  std::memcpy(&h, &v, 2);
+  return h;
+}
+
+inline uint64_t splitmix64(uint64_t z) {
+  z += 0x9E3779B97F4A7C15ull;
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  return z ^ (z >> 31);
+}
+struct Rng {
+  uint64_t key;
+  Rng(uint64_t seed, uint64_t stream) : key(seed ^ splitmix64(stream)) {}
+  uint64_t u64(uint64_t i) const {
+    return splitmix64(key + i * 0xD1B54A32D192ED03ull);
+  }
+  double uniform(uint64_t i) const {  // [0, 1)
+    return (double)(u64(i) >> 11) * (1.0 / 9007199254740992.0);
+  }
+  double normal(uint64_t i) const {  // Box-Muller on counters 2i, 2i+1
+    double u1 = ((double)(u64(2 * i) >> 11) + 1.0) * (1.0 / 9007199254740992.0);
+    double u2 = (double)(u64(2 * i + 1) >> 11) * (1.0 / 9007199254740992.0);
+    return std::sqrt(-2.0 * std::log(u1)) * std::cos(6.283185307179586 * u2);
+  }
+};
+
+std::vector<float> to_float(const uint16_t* x, int64_t n) {
+  std::vector<float> f((size_t)n);
+#pragma omp parallel for schedule(static)
+  for (int64_t i = 0; i < n; ++i) f[(size_t)i] = h2f(x[i]);
+  return f;
+}
+
+inline float dot8(const float* a, const float* b, int64_t k) {
+  v8f acc = {0, 0, 0, 0, 0, 0, 0, 0};
+  int64_t i = 0;
+  for (; i + 8 <= k; i += 8) {
+    v8f va, vb;
+    std::memcpy(&va, a + i, 32);
+    std::memcpy(&vb, b + i, 32);
+    acc += va * vb;
+  }
+  float s = 0.f;
+  for (int l = 0; l < 8; ++l) s += acc[l];
+  for (; i < k; ++i) s += a[i] * b[i];
+  return s;
+}
+
+// C[i][j] = sum_k A[i][k] * B[j][k], float32 accumulation, blocked for cache.
+void gemm_nt(const float* A, int64_t m, const float* B, int64_t n, int64_t k,
+             float* C) {
+  const int64_t MB = 64, NB = 64;
+  const int64_t mblocks = (m + MB - 1) / MB, nblocks = (n + NB - 1) / NB;
+#pragma omp parallel for collapse(2) schedule(dynamic, 1)
+  for (int64_t bi = 0; bi < mblocks; ++bi) {
+    for (int64_t bj = 0; bj < nblocks; ++bj) {
+      const int64_t i0 = bi * MB, i1 = std::min(m, i0 + MB);
+      const int64_t j0 = bj * NB, j1 = std::min(n, j0 + NB);
+      int64_t i = i0;
+      for (; i + 4 <= i1; i += 4) {
+        int64_t j = j0;
+        for (; j + 4 <= j1; j += 4) {
+          v8f acc[4][4];
+          for (int a = 0; a < 4; ++a)
+            for (int b = 0; b < 4; ++b) acc[a][b] = (v8f){0, 0, 0, 0, 0, 0, 0, 0};
+          int64_t kk = 0;
+          for (; kk + 8 <= k; kk += 8) {
+            v8f va[4], vb[4];
+            for (int a = 0; a < 4; ++a) std::memcpy(&va[a], A + (i + a) * k + kk, 32);
+            for (int b = 0; b < 4; ++b) std::memcpy(&vb[b], B + (j + b) * k + kk, 32);
+            for (int a = 0; a < 4; ++a)
+              for (int b = 0; b < 4; ++b) acc[a][b] += va[a] * vb[b];
+          }
+          for (int a = 0; a < 4; ++a)
+            for (int b = 0; b < 4; ++b) {
+              float s = 0.f;
+              for (int l = 0; l < 8; ++l) s += acc[a][b][l];
+              for (int64_t t = kk; t < k; ++t) s += A[(i + a) * k + t] * B[(j + b) * k + t];
+              C[(i + a) * n + j + b] = s;
+            }
+        }
+        for (; j < j1; ++j)
+          for (int a = 0; a < 4; ++a) C[(i + a) * n + j] = dot8(A + (i + a) * k, B + j * k, k);
+      }
+      for (; i < i1; ++i)
+        for (int64_t j = j0; j < j1; ++j) C[i * n + j] = dot8(A + i * k, B + j * k, k);
+    }
+  }
+}
+
+inline float gelu_erf(float v) {
+  // Exact GELU: 0.5 x (1 + erf(x / sqrt 2)).
+  // Reference: ViTEncoder.swift:985-992 (MLP) and :582-589 (fused block).
+  return (float)(0.5 * (double)v * (1.0 + std::erf((double)v * 0.70710678118654752440)));
+}
+
+}  // namespace
+
+extern "C" {
+
+float so_half_to_float(uint16_t h) { return h2f(h); }
+uint16_t so_float_to_half(float f) { return f2h(f); }
+int so_num_threads(void) {
+#ifdef _OPENMP
+  return omp_get_max_threads();
+#else
+  return 1;
+#endif
+}
+
+void so_gen_normal_f16(uint64_t seed, uint64_t stream, int64_t n, float mean,
+                       float std, uint16_t* out) {
+  Rng r(seed, stream);
+#pragma omp parallel for schedule(static)
+  for (int64_t i = 0; i < n; ++i)
+    out[i] = f2h((float)(mean + std * r.normal((uint64_t)i)));
+}
+
+void so_gen_uniform_f16(uint64_t seed, uint64_t stream, int64_t n, float lo,
+                        float hi, uint16_t* out) {
+  Rng r(seed, stream);
+#pragma omp parallel for schedule(static)
+  for (int64_t i = 0; i < n; ++i)
+    out[i] = f2h((float)(lo + (hi - lo) * r.uniform((uint64_t)i)));
+}
+
+void so_gen_uniform_u8(uint64_t seed, uint64_t stream, int64_t n, uint8_t* out) {
+  Rng r(seed, stream);
+#pragma omp parallel for schedule(static)
+  for (int64_t i = 0; i < n; ++i) out[i] = (uint8_t)(r.u64((uint64_t)i) >> 56);
+}
+
+void so_gen_palette(uint64_t seed, uint64_t stream, int64_t rows, float std,
+                    uint16_t* out) {
+  Rng r(seed, stream);
+#pragma omp parallel for schedule(static)
+  for (int64_t row = 0; row < rows; ++row) {
+    float v[256];
+    for (int e = 0; e < 256; ++e)
+      v[e] = h2f(f2h((float)(std * r.normal((uint64_t)(row * 256 + e)))));
+    std::sort(v, v + 256);
+    for (int e = 0; e < 256; ++e) out[row * 256 + e] = f2h(v[e]);
+  }
+}
+
+// W[n,k] = P[n, idx[n,k]] - per-output-channel 256-entry LUT.
+// Reference: Metal/Dequantize.metal:17-32 (dequantize_int8; the reference
+// shares one palette per tensor, the per-row palette is the spec'd format).
+void so_dequant(const uint8_t* idx, const uint16_t* palette, int64_t n,
+                int64_t k, uint16_t* w_out) {
+#pragma omp parallel for schedule(static)
+  for (int64_t r = 0; r < n; ++r)
+    for (int64_t c = 0; c < k; ++c) w_out[r * k + c] = palette[r * 256 + idx[r * k + c]];
+}
+
+// Palettized linear with fused epilogues.
+// Reference: MPSAttention.swift:113-117 (QKV matmul + bias), :137-163 (RoPE
+// on q,k as interleaved pairs), :179-183 (proj + bias); ViTEncoder.swift:
+// 979-997 (fc1 + bias + erf-GELU, fc2 + bias), :409/:559 (residual add).
+void so_linear(const uint16_t* x, int64_t m, const uint8_t* idx,
+               const uint16_t* palette, const uint16_t* bias, int64_t n,
+               int64_t k, int epilogue, const uint16_t* residual,
+               const float* rope, int64_t rope_period, int heads,
+               int head_dim, uint16_t* y) {
+  std::vector<float> xf = to_float(x, m * k);
+  std::vector<float> wf((size_t)(n * k));
+#pragma omp parallel for schedule(static)
+  for (int64_t r = 0; r < n; ++r)
+    for (int64_t c = 0; c < k; ++c)
+      wf[(size_t)(r * k + c)] = h2f(palette[r * 256 + idx[r * k + c]]);
+  std::vector<float> acc((size_t)(m * n));
+  gemm_nt(xf.data(), m, wf.data(), n, k, acc.data());
+  const int64_t qk_cols = 2LL * heads * head_dim;
+  const int pairs = head_dim / 2;
+#pragma omp parallel for schedule(static)
+  for (int64_t i = 0; i < m; ++i) {
+    float* row = acc.data() + i * n;
+    for (int64_t j = 0; j < n; ++j) row[j] += bias ? h2f(bias[j]) : 0.f;
+    if (epilogue == SO_EPI_BIAS_GELU) {
+      for (int64_t j = 0; j < n; ++j) row[j] = gelu_erf(row[j]);
+    } else if (epilogue == SO_EPI_BIAS_RESIDUAL) {
+      for (int64_t j = 0; j < n; ++j) row[j] += h2f(residual[i * n + j]);
+    } else if (epilogue == SO_EPI_BIAS_ROPE_QKV) {
+      const float* t = rope + (i % rope_period) * (int64_t)head_dim;
+      for (int64_t j = 0; j < qk_cols; j += 2) {
+        const int p = (int)((j % head_dim) / 2);
+        const float c = t[2 * p], s = t[2 * p + 1];
+        const float a = row[j], b = row[j + 1];
+        row[j] = a * c - b * s;
+        row[j + 1] = a * s + b * c;
+      }
+      (void)pairs;
+    }
+    for (int64_t j = 0; j < n; ++j) y[i * n + j] = f2h(row[j]);
+  }
+}
+
+void so_linear_dense(const uint16_t* x, int64_t m, const uint16_t* w,
+                     const uint16_t* bias, int64_t n, int64_t k, uint16_t* y) {
+  std::vector<float> xf = to_float(x, m * k);
+  std::vector<float> wf = to_float(w, n * k);
+  std::vector<float> acc((size_t)(m * n));
+  gemm_nt(xf.data(), m, wf.data(), n, k, acc.data());
+#pragma omp parallel for schedule(static)
+  for (int64_t i = 0; i < m; ++i)
+    for (int64_t j = 0; j < n; ++j)
+      y[i * n + j] = f2h(acc[(size_t)(i * n + j)] + (bias ? h2f(bias[j]) : 0.f));
+}
+
+// LayerNorm, biased variance, y = (x - mean) / sqrt(var + eps) * g + b.
+// Reference: ViTEncoder.swift:822-831 (graph.mean / variance / normalize,
+// epsilon 1e-6) and :457-470 (the fused block's LN1 written out).
+void so_layernorm(const uint16_t* x, int64_t m, int64_t d,
+                  const uint16_t* gamma, const uint16_t* beta, float eps,
+                  uint16_t* y) {
+#pragma omp parallel for schedule(static)
+  for (int64_t i = 0; i < m; ++i) {
+    const uint16_t* xr = x + i * d;
+    double s = 0.0;
+    for (int64_t j = 0; j < d; ++j) s += h2f(xr[j]);
+    const double mean = s / (double)d;
+    double v = 0.0;
+    for (int64_t j = 0; j < d; ++j) {
+      const double t = h2f(xr[j]) - mean;
+      v += t * t;
+    }
+    const float rstd = (float)(1.0 / std::sqrt(v / (double)d + (double)eps));
+    const float meanf = (float)mean;
+    for (int64_t j = 0; j < d; ++j) {
+      const float g = gamma ? h2f(gamma[j]) : 1.f, b = beta ? h2f(beta[j]) : 0.f;
+      y[i * d + j] = f2h((h2f(xr[j]) - meanf) * rstd * g + b);
+    }
+  }
+}
+
+// 2D axial RoPE table. Reference: Metal/RoPE.metal:22-52 (compute_rope_freqs_2d):
+// quarter = head_dim/4 pairs per axis; freq_i = 1 / theta^(2i / (head_dim/2));
+// pairs [0, quarter) take the column index w, pairs [quarter, 2*quarter) take
+// the row index h; layout [tokens, head_dim/2, (cos, sin)] (RoPE.swift:64-67).
+void so_rope_table(int grid_h, int grid_w, int head_dim, float theta,
+                   float* table) {
+  const int quarter = head_dim / 4;
+  const int64_t tokens = (int64_t)grid_h * grid_w;
+  for (int64_t p = 0; p < tokens; ++p) {
+    const int h = (int)(p / grid_w), w = (int)(p % grid_w);
+    float* t = table + p * head_dim;
+    for (int i = 0; i < quarter; ++i) {
+      const float freq = (float)(1.0 / std::pow((double)theta, (double)(2 * i) / (double)(2 * quarter)));
+      const float ax = (float)w * freq, ay = (float)h * freq;
+      t[2 * i] = (float)std::cos((double)ax);
+      t[2 * i + 1] = (float)std::sin((double)ax);
+      t[2 * (quarter + i)] = (float)std::cos((double)ay);
+      t[2 * (quarter + i) + 1] = (float)std::sin((double)ay);
+    }
+  }
+}
+
+// Stand-alone RoPE on fp16 packed rows: (a, b) -> (a c - b s, a s + b c) on
+// interleaved pairs of q and k. Reference: MPSAttention.swift:137-160;
+// Metal/RoPE.metal:111-153 (apply_rope_2d_batch on the packed QKV row).
+void so_rope_apply(uint16_t* qkv, int64_t m, int heads, int head_dim,
+                   const float* table, int64_t rope_period) {
+  const int64_t dim = (int64_t)heads * head_dim;
+#pragma omp parallel for schedule(static)
+  for (int64_t i = 0; i < m; ++i) {
+    uint16_t* row = qkv + i * 3 * dim;
+    const float* t = table + (i % rope_period) * (int64_t)head_dim;
+    for (int64_t j = 0; j < 2 * dim; j += 2) {
+      const int p = (int)((j % head_dim) / 2);
+      const float c = t[2 * p], s = t[2 * p + 1];
+      const float a = h2f(row[j]), b = h2f(row[j + 1]);
+      row[j] = f2h(a * c - b * s);
+      row[j + 1] = f2h(a * s + b * c);
+    }
+  }
+}
+
+// Global softmax attention over packed rows [q | k | v], head-major columns.
+// Reference: MPSAttention.swift:121-176 (reshape [B,S,3,NH,DPH], SDPA with
+// scale 1/sqrt(d)); AttentionKernels.swift:48-68 (explicit softmax form).
+void so_attention(const uint16_t* qkv, int batch, int64_t seq, int heads,
+                  int head_dim, float scale, uint16_t* o) {
+  const int64_t dim = (int64_t)heads * head_dim;
+  for (int b = 0; b < batch; ++b) {
+    for (int h = 0; h < heads; ++h) {
+      std::vector<float> q((size_t)(seq * head_dim)), kk((size_t)(seq * head_dim)),
+          v((size_t)(seq * head_dim));
+#pragma omp parallel for schedule(static)
+      for (int64_t s = 0; s < seq; ++s) {
+        const uint16_t* row = qkv + (b * seq + s) * 3 * dim + (int64_t)h * head_dim;
+        for (int d = 0; d < head_dim; ++d) {
+          q[(size_t)(s * head_dim + d)] = h2f(row[d]);
+          kk[(size_t)(s * head_dim + d)] = h2f(row[dim + d]);
+          v[(size_t)(s * head_dim + d)] = h2f(row[2 * dim + d]);
+        }
+      }
+#pragma omp parallel
+      {
+        std::vector<float> p((size_t)seq), acc((size_t)head_dim);
+#pragma omp for schedule(static)
+        for (int64_t i = 0; i < seq; ++i) {
+          const float* qi = q.data() + i * head_dim;
+          float mx = -INFINITY;
+          for (int64_t j = 0; j < seq; ++j) {
+            p[(size_t)j] = dot8(qi, kk.data() + j * head_dim, head_dim) * scale;
+            mx = std::max(mx, p[(size_t)j]);
+          }
+          float l = 0.f;
+          for (int64_t j = 0; j < seq; ++j) {
+            p[(size_t)j] = std::exp(p[(size_t)j] - mx);
+            l += p[(size_t)j];
+          }
+          std::fill(acc.begin(), acc.end(), 0.f);
+          for (int64_t j = 0; j < seq; ++j) {
+            const float pj = p[(size_t)j];
+            const float* vj = v.data() + j * head_dim;
+            for (int d = 0; d < head_dim; ++d) acc[(size_t)d] += pj * vj[d];
+          }
+          const float inv = 1.f / l;
+          uint16_t* orow = o + (b * seq + i) * dim + (int64_t)h * head_dim;
+          for (int d = 0; d < head_dim; ++d) orow[d] = f2h(acc[(size_t)d] * inv);
+        }
+      }
+    }
+  }
+}
+
+// Token score: L2 norm (spec) or L1 = sum |x| (TokenPruner.swift:54-56).
+void so_token_scores(const uint16_t* x, int64_t rows, int64_t d, int norm,
+                     float* scores) {
+#pragma omp parallel for schedule(static)
+  for (int64_t i = 0; i < rows; ++i) {
+    double s = 0.0;
+    for (int64_t j = 0; j < d; ++j) {
+      const double t = h2f(x[i * d + j]);
+      s += norm == SO_SCORE_L1 ? std::fabs(t) : t * t;
+    }
+    scores[i] = (float)(norm == SO_SCORE_L1 ? s : std::sqrt(s));
+  }
+}
+
+// Top-k per image, key (-score, index): ties go to the lower index. Output in
+// ascending index order (spec: stable index order) or by descending score
+// (the order of MPSGraph topK, TokenPruner.swift:59-60).
+void so_select_topk(const float* scores, int batch, int64_t seq, int64_t keep,
+                    int order, int32_t* idx) {
+  for (int b = 0; b < batch; ++b) {
+    const float* s = scores + b * seq;
+    std::vector<int32_t> ord((size_t)seq);
+    std::iota(ord.begin(), ord.end(), 0);
+    auto cmp = [s](int32_t a, int32_t c) {
+      if (s[a] != s[c]) return s[a] > s[c];
+      return a < c;
+    };
+    std::partial_sort(ord.begin(), ord.begin() + keep, ord.end(), cmp);
+    ord.resize((size_t)keep);
+    if (order == SO_ORDER_INDEX) std::sort(ord.begin(), ord.end());
+    std::memcpy(idx + b * keep, ord.data(), (size_t)keep * 4);
+  }
+}
+
+// Score -> top-k -> gather of features and RoPE rows.
+// Reference: TokenPruner.swift:32-126 (abs/sum score, topK, gather features
+// [B,K,D] and RoPE rows [B,K,ropeDim], int32 indices).
+void so_prune(const uint16_t* x, int batch, int64_t seq, int64_t d,
+              int64_t keep, int norm, int order, const float* rope_in,
+              int64_t rope_period, int rope_cols, uint16_t* feats,
+              float* rope_out, int32_t* idx) {
+  std::vector<float> scores((size_t)(batch * seq));
+  so_token_scores(x, batch * seq, d, norm, scores.data());
+  so_select_topk(scores.data(), batch, seq, keep, order, idx);
+  for (int b = 0; b < batch; ++b)
+    for (int64_t i = 0; i < keep; ++i) {
+      const int64_t src = b * seq + idx[b * keep + i];
+      std::memcpy(feats + (b * keep + i) * d, x + src * d, (size_t)d * 2);
+      if (rope_in && rope_out)
+        std::memcpy(rope_out + (b * keep + i) * rope_cols,
+                    rope_in + (src % rope_period) * rope_cols, (size_t)rope_cols * 4);
+    }
+}
+
+// conv(patch x patch, stride patch) on an NHWC fp16 image, tokens row-major
+// h*gw + w. Reference: ViTEncoder.swift:218-263 (MPSCNN conv) and
+// Metal/ViTUtils.metal:53-76 (flatten to [S, D], index h*W + w).
+void so_patch_embed(const uint16_t* image, int batch, int height, int width,
+                    const uint16_t* w, const uint16_t* bias, int patch,
+                    int dim, uint16_t* out) {
+  const int gh = height / patch, gw = width / patch;
+  const int64_t kdim = 3LL * patch * patch;
+  const int64_t tokens = (int64_t)batch * gh * gw;
+  std::vector<uint16_t> cols((size_t)(tokens * kdim));
+#pragma omp parallel for schedule(static)
+  for (int64_t t = 0; t < tokens; ++t) {
+    const int b = (int)(t / ((int64_t)gh * gw));
+    const int p = (int)(t % ((int64_t)gh * gw));
+    const int py = p / gw, px = p % gw;
+    for (int c = 0; c < 3; ++c)
+      for (int ky = 0; ky < patch; ++ky)
+        for (int kx = 0; kx < patch; ++kx) {
+          const int64_t yy = (int64_t)py * patch + ky, xx = (int64_t)px * patch + kx;
+          cols[(size_t)(t * kdim + (c * patch + ky) * patch + kx)] =
+              image[(((int64_t)b * height + yy) * width + xx) * 3 + c];
+        }
+  }
+  so_linear_dense(cols.data(), tokens, w, bias, dim, kdim, out);
+}
+
+// One pre-LN ViT block. Reference op order: ViTEncoder.swift:457-615
+// (LN1 -> QKV+b -> RoPE(q,k) -> SDPA -> proj+b -> +x -> LN2 -> fc1+b -> GELU
+// -> fc2+b -> +residual); unfused equivalent at ViTEncoder.swift:388-430.
+void so_vit_block(uint16_t* x, int batch, int64_t seq, int dim, int heads,
+                  float ln_eps, const so_block_weights_t* w, const float* rope,
+                  int64_t rope_period) {
+  const int64_t m = (int64_t)batch * seq;
+  const int hd = dim / heads;
+  const int64_t hidden = w->fc1.n;
+  std::vector<uint16_t> ln((size_t)(m * dim)), qkv((size_t)(m * 3 * dim)),
+      att((size_t)(m * dim)), hbuf((size_t)(m * hidden));
+  so_layernorm(x, m, dim, w->ln1_gamma, w->ln1_beta, ln_eps, ln.data());
+  so_linear(ln.data(), m, w->qkv.idx, w->qkv.palette, w->qkv.bias, 3LL * dim, dim,
+            SO_EPI_BIAS_ROPE_QKV, nullptr, rope, rope_period, heads, hd, qkv.data());
+  so_attention(qkv.data(), batch, seq, heads, hd, 1.0f / std::sqrt((float)hd), att.data());
+  so_linear(att.data(), m, w->proj.idx, w->proj.palette, w->proj.bias, dim, dim,
+            SO_EPI_BIAS_RESIDUAL, x, nullptr, 1, heads, hd, x);
+  so_layernorm(x, m, dim, w->ln2_gamma, w->ln2_beta, ln_eps, ln.data());
+  so_linear(ln.data(), m, w->fc1.idx, w->fc1.palette, w->fc1.bias, hidden, dim,
+            SO_EPI_BIAS_GELU, nullptr, nullptr, 1, heads, hd, hbuf.data());
+  so_linear(hbuf.data(), m, w->fc2.idx, w->fc2.palette, w->fc2.bias, dim, hidden,
+            SO_EPI_BIAS_RESIDUAL, x, nullptr, 1, heads, hd, x);
+}
+
+// Encoder driver. Reference: ViTEncoder.swift:1235-1396 (patch embed, block
+// loop, prune inside the loop with gathered RoPE rows at :1344-1371). The
+// spec places the prune after `prune_after` blocks, all blocks global.
+void so_encoder_forward(const uint16_t* image, int batch, int image_size,
+                        int patch, int dim, int heads, int num_blocks,
+                        int prune_after, int64_t keep, int norm, int order,
+                        float ln_eps, float rope_theta,
+                        const uint16_t* patch_w, const uint16_t* patch_b,
+                        const so_block_weights_t* blocks, uint16_t* feats,
+                        int32_t* idx) {
+  const int grid = image_size / patch;
+  const int64_t seq = (int64_t)grid * grid;
+  const int hd = dim / heads;
+  std::vector<uint16_t> x((size_t)(batch * seq * dim));
+  so_patch_embed(image, batch, image_size, image_size, patch_w, patch_b, patch, dim, x.data());
+  std::vector<float> table((size_t)(seq * hd));
+  so_rope_table(grid, grid, hd, rope_theta, table.data());
+  const float* rope = table.data();
+  int64_t period = seq, cur = seq;
+  std::vector<uint16_t> px;
+  std::vector<float> prope;
+  bool pruned = false;
+  for (int blk = 0; blk <= num_blocks; ++blk) {
+    if (prune_after > 0 && blk == prune_after && keep < seq) {
+      px.resize((size_t)(batch * keep * dim));
+      prope.resize((size_t)(batch * keep * hd));
+      so_prune(x.data(), batch, seq, dim, keep, norm, order, table.data(), seq, hd,
+               px.data(), prope.data(), idx);
+      x.swap(px);
+      rope = prope.data();
+      period = batch * keep;
+      cur = keep;
+      pruned = true;
+    }
+    if (blk == num_blocks) break;
+    so_vit_block(x.data(), batch, cur, dim, heads, ln_eps, &blocks[blk], rope, period);
+  }
+  if (!pruned) {
+    for (int b = 0; b < batch; ++b)
+      for (int64_t i = 0; i < seq; ++i) idx[b * seq + i] = (int32_t)i;
+  }
+  std::memcpy(feats, x.data(), (size_t)(batch * cur * dim) * 2);
+}
+
+}  // extern "C"

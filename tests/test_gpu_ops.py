@@ -1,0 +1,434 @@
+"""Parity of libsam3cuda (called through its C ABI) with the CPU oracle.
+
+Tolerances (from the benchmark spec): dequantized weights bit-exact; pruning
+indices bit-exact wherever the score margin exceeds 1e-3; layer and encoder
+outputs within a normwise max relative error of 1e-2 in fp16
+(max |gpu - oracle| / max |oracle|), with tighter bounds asserted where the two
+sides differ only by fp32 summation order.
+"""
+import ctypes as C
+
+import numpy as np
+import pytest
+
+from util import f16_ulps, max_rel_err
+
+pytestmark = pytest.mark.gpu
+F16 = np.float16
+SPEC_TOL = 1e-2
+
+
+# ------------------------------------------------------------------ helpers
+def upload_linear(ctx, sam3, idx, pal, bias):
+    return sam3.palette_linear(ctx.upload(idx), ctx.upload(pal),
+                               None if bias is None else ctx.upload(bias),
+                               idx.shape[0], idx.shape[1])
+
+
+def upload_block(ctx, sam3, blk):
+    def pl(d):
+        return upload_linear(ctx, sam3, d["idx"], d["palette"], d["bias"])
+    return sam3.block_weights(ctx.upload(blk.ln1_gamma), ctx.upload(blk.ln1_beta), pl(blk.qkv),
+                              pl(blk.proj), ctx.upload(blk.ln2_gamma), ctx.upload(blk.ln2_beta),
+                              pl(blk.fc1), pl(blk.fc2))
+
+
+def run_linear(ctx, sam3, x, idx, pal, bias, epi, residual=None, rope=None, rope_rows=0):
+    m, n = x.shape[0], idx.shape[0]
+    w = upload_linear(ctx, sam3, idx, pal, bias)
+    dx = ctx.upload(x)
+    dy = ctx.alloc(m * n * 2)
+    dres = ctx.upload(residual) if residual is not None else None
+    drope = ctx.upload(rope.astype(np.float32)) if rope is not None else None
+    ctx.linear_palette(dx, m, w, epi, dy, dres, drope, rope_rows)
+    ctx.sync()
+    return ctx.download(dy, (m, n), F16)
+
+
+# ------------------------------------------------------------------ dequant
+def test_dequant_golden_bit_exact(ctx, sam3, golden):
+    idx, pal = golden["dq_idx"], golden["dq_pal"]
+    w = upload_linear(ctx, sam3, idx, pal, None)
+    out = ctx.alloc(idx.size * 2)
+    ctx.dequant_palette(w, out)
+    ctx.sync()
+    got = ctx.download(out, idx.shape, F16)
+    assert np.array_equal(got.view(np.uint16), golden["dq_w"].view(np.uint16))
+
+
+def test_dequant_qkv_shape_bit_exact(ctx, sam3, oracle):
+    idx = oracle.gen_u8(1, 1, (3072, 1024))
+    pal = oracle.gen_palette(1, 2, 3072)
+    w = upload_linear(ctx, sam3, idx, pal, None)
+    out = ctx.alloc(idx.size * 2)
+    ctx.dequant_palette(w, out)
+    ctx.sync()
+    got = ctx.download(out, idx.shape, F16)
+    assert np.array_equal(got.view(np.uint16), oracle.dequant(idx, pal).view(np.uint16))
+
+
+# ------------------------------------------------------------------ palettized linear
+@pytest.mark.parametrize("epi,key", [(0, "lin_y_bias"), (1, "lin_y_gelu"), (2, "lin_y_res"),
+                                     (3, "lin_y_rope")])
+def test_linear_epilogues_golden(ctx, sam3, golden, epi, key):
+    y = run_linear(ctx, sam3, golden["lin_x"], golden["lin_idx"], golden["lin_pal"],
+                   golden["lin_bias"], epi, residual=golden["lin_res"] if epi == 2 else None,
+                   rope=golden["lin_table"] if epi == 3 else None, rope_rows=24)
+    assert max_rel_err(y, golden[key]) < 2e-3
+    assert f16_ulps(y, golden[key]) <= 4
+
+
+def test_linear_c0_qkv_projection_full_size(ctx, sam3, oracle):
+    # X [5184,1024] ~ N(0,1); idx [3072,1024] ~ U{0..255}; palette N(0,0.02)
+    # sorted; bias N(0,0.01); Y = X . deq(W)^T + b.
+    x = oracle.gen_normal(5, 1, (5184, 1024))
+    idx = oracle.gen_u8(5, 2, (3072, 1024))
+    pal = oracle.gen_palette(5, 3, 3072)
+    bias = oracle.gen_normal(5, 4, (3072,), 0.0, 0.01)
+    y = run_linear(ctx, sam3, x, idx, pal, bias, sam3.EPI_BIAS)
+    ref = oracle.linear(x, idx, pal, bias)
+    assert max_rel_err(y, ref) < 2e-3
+    assert max_rel_err(y, ref) < SPEC_TOL
+
+
+@pytest.mark.parametrize("m", [1, 127, 129, 300])
+def test_linear_ragged_rows(ctx, sam3, oracle, m):
+    x = oracle.gen_normal(6, m, (m, 256))
+    idx = oracle.gen_u8(6, 2, (256, 256))
+    pal = oracle.gen_palette(6, 3, 256)
+    bias = oracle.gen_normal(6, 4, (256,), 0.0, 0.01)
+    res = oracle.gen_normal(6, 5, (m, 256))
+    y = run_linear(ctx, sam3, x, idx, pal, bias, sam3.EPI_BIAS_RESIDUAL, residual=res)
+    ref = oracle.linear(x, idx, pal, bias, epilogue=oracle.EPI_BIAS_RESIDUAL, residual=res)
+    assert max_rel_err(y, ref) < 2e-3
+
+
+def test_linear_many_tiles_gelu_and_rope(ctx, sam3, oracle):
+    # more tiles than SMs, several n-tiles per CTA (palette reloads), K=4096
+    m = 1000
+    x = oracle.gen_normal(7, 1, (m, 4096))
+    idx = oracle.gen_u8(7, 2, (1024, 4096))
+    pal = oracle.gen_palette(7, 3, 1024)
+    bias = oracle.gen_normal(7, 4, (1024,), 0.0, 0.01)
+    y = run_linear(ctx, sam3, x, idx, pal, bias, sam3.EPI_BIAS_GELU)
+    ref = oracle.linear(x, idx, pal, bias, epilogue=oracle.EPI_BIAS_GELU)
+    assert max_rel_err(y, ref) < 2e-3
+    table = oracle.rope_table(10, 10)
+    x2 = oracle.gen_normal(7, 5, (m, 1024))
+    idx2 = oracle.gen_u8(7, 6, (3072, 1024))
+    pal2 = oracle.gen_palette(7, 7, 3072)
+    b2 = oracle.gen_normal(7, 8, (3072,), 0.0, 0.01)
+    y2 = run_linear(ctx, sam3, x2, idx2, pal2, b2, sam3.EPI_BIAS_ROPE_QKV, rope=table,
+                    rope_rows=100)
+    ref2 = oracle.linear(x2, idx2, pal2, b2, epilogue=oracle.EPI_BIAS_ROPE_QKV, rope=table,
+                         rope_period=100, heads=16, head_dim=64)
+    assert max_rel_err(y2, ref2) < 2e-3
+
+
+def test_linear_in_place_residual(ctx, sam3, oracle):
+    x = oracle.gen_normal(8, 1, (256, 512))
+    idx = oracle.gen_u8(8, 2, (512, 512))
+    pal = oracle.gen_palette(8, 3, 512)
+    bias = oracle.gen_normal(8, 4, (512,), 0.0, 0.01)
+    w = upload_linear(ctx, sam3, idx, pal, bias)
+    dx = ctx.upload(x)
+    ctx.linear_palette(dx, 256, w, sam3.EPI_BIAS_RESIDUAL, dx, dx)  # y = x + x W^T + b
+    ctx.sync()
+    got = ctx.download(dx, (256, 512), F16)
+    ref = oracle.linear(x, idx, pal, bias, epilogue=oracle.EPI_BIAS_RESIDUAL, residual=x)
+    assert max_rel_err(got, ref) < 2e-3
+
+
+def test_linear_rejects_bad_shapes(ctx, sam3):
+    w = sam3.palette_linear(16, 16, None, 100, 64)  # n % 128 != 0
+    with pytest.raises(sam3.SAM3Error) as e:
+        ctx.linear_palette(16, 4, w, sam3.EPI_BIAS, 16)
+    assert e.value.status == sam3.ERR_SHAPE
+    w = sam3.palette_linear(16, 16, None, 128, 96)  # k % 64 != 0
+    with pytest.raises(sam3.SAM3Error):
+        ctx.linear_palette(16, 4, w, sam3.EPI_BIAS, 16)
+    w = sam3.palette_linear(16, 16, None, 128, 64)
+    with pytest.raises(sam3.SAM3Error) as e:
+        ctx.linear_palette(16, 4, w, 9, 16)
+    assert e.value.status == sam3.ERR_INVALID_ARG
+
+
+# ------------------------------------------------------------------ LayerNorm / RoPE
+def test_layernorm_golden_and_full(ctx, sam3, golden, oracle):
+    x, g, b = golden["ln_x"], golden["ln_g"], golden["ln_b"]
+    dx, dy = ctx.upload(x), ctx.alloc(x.nbytes)
+    ctx.layernorm(dx, 16, 256, ctx.upload(g), ctx.upload(b), 1e-6, dy)
+    ctx.sync()
+    assert f16_ulps(ctx.download(dy, x.shape, F16), golden["ln_y"]) <= 1
+    x = oracle.gen_normal(9, 1, (5184, 1024), 0.3, 2.0)
+    dx, dy = ctx.upload(x), ctx.alloc(x.nbytes)
+    ctx.layernorm(dx, 5184, 1024, None, None, 1e-6, dy)
+    ctx.sync()
+    assert f16_ulps(ctx.download(dy, x.shape, F16), oracle.layernorm(x)) <= 1
+
+
+def test_rope_table_matches_oracle(ctx, sam3, golden, oracle):
+    t = ctx.alloc(72 * 72 * 64 * 4)
+    ctx.rope_table(72, 72, 64, 10000.0, t)
+    ctx.sync()
+    got = ctx.download(t, (5184, 32, 2), np.float32)
+    assert np.abs(got - oracle.rope_table(72, 72)).max() < 1e-5
+    t2 = ctx.alloc(24 * 64 * 4)
+    ctx.rope_table(4, 6, 64, 10000.0, t2)
+    ctx.sync()
+    assert np.abs(ctx.download(t2, (24, 32, 2), np.float32) - golden["rope_table_4x6"]).max() < 1e-5
+
+
+def test_rope_apply_golden(ctx, sam3, golden):
+    q = golden["rope_qkv"]
+    dq = ctx.upload(q)
+    ctx.rope_apply(dq, 24, 2, 64, ctx.upload(golden["rope_table_4x6"]), 24)
+    ctx.sync()
+    assert f16_ulps(ctx.download(dq, q.shape, F16), golden["rope_out"]) <= 1
+
+
+# ------------------------------------------------------------------ attention
+def test_attention_golden_ragged(ctx, sam3, golden):
+    qkv = golden["att_qkv"]
+    o = ctx.alloc(2 * 37 * 128 * 2)
+    ctx.attention(ctx.upload(qkv), 2, 37, 2, 64, 0.125, o)
+    ctx.sync()
+    assert max_rel_err(ctx.download(o, (74, 128), F16), golden["att_o"]) < 2e-3
+
+
+def test_attention_zero_query_is_mean_of_v(ctx, sam3, oracle):
+    seq, heads = 300, 2
+    qkv = oracle.gen_normal(10, 1, (seq, 3 * heads * 64))
+    qkv[:, :heads * 64] = 0
+    o = ctx.alloc(seq * heads * 64 * 2)
+    ctx.attention(ctx.upload(qkv), 1, seq, heads, 64, 0.125, o)
+    ctx.sync()
+    got = ctx.download(o, (seq, heads * 64), F16).astype(np.float64)
+    v = qkv[:, 2 * heads * 64:].astype(np.float64)
+    assert np.abs(got - v.mean(0)).max() < 2e-3
+
+
+def test_attention_full_size_72x72_grid(ctx, sam3, oracle):
+    seq, heads = 5184, 16
+    qkv = oracle.gen_normal(11, 1, (seq, 3 * 1024))
+    o = ctx.alloc(seq * 1024 * 2)
+    ctx.attention(ctx.upload(qkv), 1, seq, heads, 64, 0.125, o)
+    ctx.sync()
+    got = ctx.download(o, (seq, 1024), F16)
+    ref = oracle.attention(qkv, 1, seq, heads, 64)
+    assert max_rel_err(got, ref) < 5e-3
+
+
+# ------------------------------------------------------------------ pruning
+@pytest.mark.parametrize("order", [0, 1])
+def test_prune_golden_with_ties(ctx, sam3, golden, order):
+    x = golden["pr_x"]
+    feats, idx = ctx.alloc(24 * 16 * 2), ctx.alloc(24 * 4)
+    ctx.prune(ctx.upload(x), 2, 24, 16, 12, sam3.SCORE_L2, order, feats, idx)
+    ctx.sync()
+    assert np.array_equal(ctx.download(idx, (2, 12), np.int32), golden[f"pr_idx_o{order}"])
+    assert np.array_equal(ctx.download(feats, (24, 16), F16).view(np.uint16),
+                          golden[f"pr_feats_o{order}"].view(np.uint16))
+
+
+def test_prune_l1(ctx, sam3, golden):
+    feats, idx = ctx.alloc(24 * 16 * 2), ctx.alloc(24 * 4)
+    ctx.prune(ctx.upload(golden["pr_x"]), 2, 24, 16, 12, sam3.SCORE_L1, 0, feats, idx)
+    ctx.sync()
+    assert np.array_equal(ctx.download(idx, (2, 12), np.int32), golden["pr_idx_l1"])
+
+
+def _margin_check(got_idx, scores, keep):
+    """Indices must agree exactly unless the keep-th / (keep+1)-th score gap is
+    <= 1e-3; inside that band only tokens within 1e-3 of the cut may differ."""
+    order = np.lexsort((np.arange(len(scores)), -scores.astype(np.float64)))
+    ref = np.sort(order[:keep])
+    s_sorted = scores[order]
+    gap = float(s_sorted[keep - 1] - s_sorted[keep])
+    if gap > 1e-3:
+        assert np.array_equal(np.sort(got_idx), ref)
+    else:
+        cut = 0.5 * float(s_sorted[keep - 1] + s_sorted[keep])
+        sure_in = set(np.nonzero(scores > cut + 1e-3)[0])
+        sure_out = set(np.nonzero(scores < cut - 1e-3)[0])
+        g = set(got_idx.tolist())
+        assert sure_in <= g and not (sure_out & g)
+
+
+def test_prune_full_size_index_order_with_rope(ctx_full, sam3, oracle):
+    ctx = ctx_full
+    seq, keep, d = 5184, 2592, 1024
+    x = oracle.gen_normal(12, 1, (seq, d))
+    table = oracle.rope_table(72, 72)
+    feats, idx = ctx.alloc(keep * d * 2), ctx.alloc(keep * 4)
+    rope_out = ctx.alloc(keep * 64 * 4)
+    ctx.prune(ctx.upload(x), 1, seq, d, keep, sam3.SCORE_L2, sam3.ORDER_INDEX, feats, idx,
+              rope_in=ctx.upload(table), rope_rows=seq, rope_cols=64, rope_out=rope_out)
+    ctx.sync()
+    gi = ctx.download(idx, (keep,), np.int32)
+    assert (np.diff(gi) > 0).all()
+    _margin_check(gi, oracle.token_scores(x), keep)
+    gf = ctx.download(feats, (keep, d), F16)
+    assert np.array_equal(gf.view(np.uint16), x[gi].view(np.uint16))
+    gr = ctx.download(rope_out, (keep, 32, 2), np.float32)
+    assert np.array_equal(gr, table[gi])
+
+
+def test_prune_score_order_matches_oracle(ctx_full, sam3, oracle):
+    ctx = ctx_full
+    seq, keep, d = 5184, 2592, 1024
+    x = oracle.gen_normal(13, 1, (seq, d))
+    feats, idx = ctx.alloc(keep * d * 2), ctx.alloc(keep * 4)
+    ctx.prune(ctx.upload(x), 1, seq, d, keep, sam3.SCORE_L2, sam3.ORDER_SCORE, feats, idx)
+    ctx.sync()
+    gi = ctx.download(idx, (keep,), np.int32)
+    s = oracle.token_scores(x)
+    assert (np.diff(s[gi].astype(np.float64)) <= 1e-3).all()  # non-increasing score
+    _margin_check(gi, s, keep)
+
+
+# ------------------------------------------------------------------ patch embedding
+def test_patch_embed_golden(ctx, sam3, golden):
+    img, w, b = golden["pe_img"], golden["pe_w"], golden["pe_b"]
+    out = ctx.alloc(4 * 128 * 2)
+    ctx.patch_embed(ctx.upload(img), 1, 28, 28, ctx.upload(w), ctx.upload(b), 14, 128, out)
+    ctx.sync()
+    assert f16_ulps(ctx.download(out, (4, 128), F16), golden["pe_out"]) <= 2
+
+
+def test_patch_embed_full_size(ctx_full, sam3, oracle):
+    ctx = ctx_full
+    img = oracle.gen_uniform(14, 1, (1, 1008, 1008, 3), -1.0, 1.0)
+    w = oracle.gen_normal(14, 2, (1024, 3, 14, 14), 0.0, 0.02)
+    b = oracle.gen_normal(14, 3, (1024,), 0.0, 0.02)
+    out = ctx.alloc(5184 * 1024 * 2)
+    ctx.patch_embed(ctx.upload(img), 1, 1008, 1008, ctx.upload(w), ctx.upload(b), 14, 1024, out)
+    ctx.sync()
+    got = ctx.download(out, (5184, 1024), F16)
+    assert max_rel_err(got, oracle.patch_embed(img, w, b, 14)) < 2e-3
+
+
+# ------------------------------------------------------------------ blocks
+def test_mlp_block_c1_full_size(ctx_full, sam3, oracle):
+    ctx = ctx_full
+    blk = oracle.SyntheticBlock(21, 0)
+    w = upload_block(ctx, sam3, blk)
+    x = oracle.gen_normal(21, 1, (5184, 1024))
+    dx = ctx.upload(x)
+    ctx.mlp_block(dx, 5184, w)
+    ctx.sync()
+    got = ctx.download(dx, x.shape, F16)
+    ln = oracle.layernorm(x)
+    h = oracle.linear(ln, **_lin(blk.fc1), epilogue=oracle.EPI_BIAS_GELU)
+    ref = oracle.linear(h, **_lin(blk.fc2), epilogue=oracle.EPI_BIAS_RESIDUAL, residual=x)
+    assert max_rel_err(got, ref) < SPEC_TOL
+
+
+def _lin(d):
+    return {"idx": d["idx"], "palette": d["palette"], "bias": d["bias"]}
+
+
+def test_attention_block_c2_full_size(ctx_full, sam3, oracle):
+    ctx = ctx_full
+    blk = oracle.SyntheticBlock(22, 0)
+    w = upload_block(ctx, sam3, blk)
+    table = oracle.rope_table(72, 72)
+    x = oracle.gen_normal(22, 1, (5184, 1024))
+    dx = ctx.upload(x)
+    ctx.attention_block(dx, 1, 5184, w, ctx.upload(table), 5184)
+    ctx.sync()
+    got = ctx.download(dx, x.shape, F16)
+    ln = oracle.layernorm(x)
+    qkv = oracle.linear(ln, **_lin(blk.qkv), epilogue=oracle.EPI_BIAS_ROPE_QKV, rope=table,
+                        rope_period=5184)
+    att = oracle.attention(qkv, 1, 5184, 16, 64)
+    ref = oracle.linear(att, **_lin(blk.proj), epilogue=oracle.EPI_BIAS_RESIDUAL, residual=x)
+    assert max_rel_err(got, ref) < SPEC_TOL
+
+
+def test_vit_block_small_batched(ctx, sam3, oracle):
+    blk = oracle.SyntheticBlock(23, 0, 256, 512)
+    w = upload_block(ctx, sam3, blk)
+    table = oracle.rope_table(8, 8)
+    x = oracle.gen_normal(23, 1, (2 * 64, 256))
+    dx = ctx.upload(x)
+    ctx.vit_block(dx, 2, 64, w, ctx.upload(table), 64)
+    ctx.sync()
+    got = ctx.download(dx, x.shape, F16)
+    ref = oracle.vit_block(x, 2, 64, 4, blk, table, 64)
+    assert max_rel_err(got, ref) < SPEC_TOL
+
+
+# ------------------------------------------------------------------ encoder
+def _small_encoder(oracle, seed=31, dim=256, heads=4, hidden=512, nblocks=2):
+    blocks = [oracle.SyntheticBlock(seed, i, dim, hidden) for i in range(nblocks)]
+    pw = oracle.gen_normal(seed, 900, (dim, 3, 14, 14), 0.0, 0.02)
+    pb = oracle.gen_normal(seed, 901, (dim,), 0.0, 0.02)
+    return blocks, pw, pb
+
+
+def _upload_encoder(ctx, sam3, blocks, pw, pb):
+    return sam3.encoder_weights(ctx.upload(pw), ctx.upload(pb),
+                                [upload_block(ctx, sam3, b) for b in blocks])
+
+
+def test_encoder_small_device_and_host_api(ctx, sam3, oracle):
+    blocks, pw, pb = _small_encoder(oracle)
+    w = _upload_encoder(ctx, sam3, blocks, pw, pb)
+    img = oracle.gen_uniform(31, 77, (2, 112, 112, 3), -1.0, 1.0)
+    ref_f, ref_i = oracle.encoder_forward(img, blocks, pw, pb, heads=4, prune_after=1, keep=32)
+    assert ctx.out_tokens == 32
+    feats, idx = ctx.alloc(2 * 32 * 256 * 2), ctx.alloc(2 * 32 * 4)
+    ctx.encoder_forward(ctx.upload(img), 2, w, feats, idx)
+    ctx.sync()
+    gi = ctx.download(idx, (2, 32), np.int32)
+    gf = ctx.download(feats, (2, 32, 256), F16)
+    assert np.array_equal(gi, ref_i)
+    assert max_rel_err(gf, ref_f) < SPEC_TOL
+    # host-buffer entry point gives the same bits as the device entry point
+    hf = np.empty((2, 32, 256), F16)
+    hi = np.empty((2, 32), np.int32)
+    ctx.encoder_forward_host(img, 2, w, hf, hi)
+    assert np.array_equal(hi, gi) and np.array_equal(hf.view(np.uint16), gf.view(np.uint16))
+
+
+def test_encoder_full_size_two_blocks_matches_oracle(sam3, oracle):
+    # 1008^2 image, full width (1024, 16 heads, 4096), two blocks with the
+    # prune (to 2592 tokens by L2 norm) between them.
+    with sam3.Context(0, num_blocks=2, prune_after_block=1, max_batch=1) as ctx:
+        blocks = [oracle.SyntheticBlock(41, i) for i in range(2)]
+        pw = oracle.gen_normal(41, 900, (1024, 3, 14, 14), 0.0, 0.02)
+        pb = oracle.gen_normal(41, 901, (1024,), 0.0, 0.02)
+        w = _upload_encoder(ctx, sam3, blocks, pw, pb)
+        img = oracle.gen_uniform(41, 77, (1, 1008, 1008, 3), -1.0, 1.0)
+        hf = np.empty((1, 2592, 1024), F16)
+        hi = np.empty((1, 2592), np.int32)
+        ctx.encoder_forward_host(img, 1, w, hf, hi)
+        ref_f, ref_i = oracle.encoder_forward(img, blocks, pw, pb, prune_after=1, keep=2592)
+        assert (np.diff(hi[0]) > 0).all()
+        same = hi[0] == ref_i[0]
+        assert same.mean() > 0.99
+        if same.all():
+            assert max_rel_err(hf, ref_f) < SPEC_TOL
+
+
+def test_encoder_full_32_blocks_properties(ctx_full, sam3, oracle):
+    # The 32-block 1008^2 encoder: valid sorted indices, finite features,
+    # determinism (same inputs -> bit-identical outputs on a second run).
+    ctx = ctx_full
+    rng = np.random.default_rng(5)
+    blocks = [oracle.SyntheticBlock(51, i) for i in range(32)]
+    pw = oracle.gen_normal(51, 900, (1024, 3, 14, 14), 0.0, 0.02)
+    pb = oracle.gen_normal(51, 901, (1024,), 0.0, 0.02)
+    w = _upload_encoder(ctx, sam3, blocks, pw, pb)
+    img = rng.uniform(-1, 1, size=(1, 1008, 1008, 3)).astype(F16)
+    out = []
+    for _ in range(2):
+        hf = np.empty((1, 2592, 1024), F16)
+        hi = np.empty((1, 2592), np.int32)
+        ctx.encoder_forward_host(img, 1, w, hf, hi)
+        out.append((hf, hi))
+    (f1, i1), (f2, i2) = out
+    assert (np.diff(i1[0]) > 0).all() and i1.min() >= 0 and i1.max() < 5184
+    assert np.isfinite(f1.astype(np.float32)).all()
+    assert np.array_equal(i1, i2) and np.array_equal(f1.view(np.uint16), f2.view(np.uint16))

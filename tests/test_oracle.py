@@ -1,0 +1,159 @@
+"""The CPU oracle against the golden vectors and known-answer tests (CPU only).
+
+The golden vectors are an independent float64 restatement of the reference
+formulas (tests/golden/make_golden.py); the KATs follow closed forms read off
+the reference sources (cited per test).
+"""
+import math
+
+import numpy as np
+import pytest
+
+from util import f16_ulps, max_rel_err
+
+F16 = np.float16
+
+
+def test_fp16_conversion_matches_numpy(oracle):
+    vals = np.array([0.0, -0.0, 1e-8, 6.1e-5, 0.1, 1.0 / 3, 65504.0, 70000.0, -2.5e-3],
+                    np.float32)
+    L = oracle.lib()
+    got = np.array([L.so_float_to_half(float(v)) for v in vals], np.uint16)
+    assert (got == vals.astype(F16).view(np.uint16)).all()
+    back = np.array([L.so_half_to_float(int(h)) for h in got], np.float32)
+    assert np.array_equal(back, got.view(F16).astype(np.float32), equal_nan=True)
+
+
+def test_generators_deterministic_and_distributed(oracle):
+    a = oracle.gen_normal(7, 3, (4096,), 0.0, 1.0)
+    b = oracle.gen_normal(7, 3, (4096,), 0.0, 1.0)
+    c = oracle.gen_normal(7, 4, (4096,), 0.0, 1.0)
+    assert np.array_equal(a.view(np.uint16), b.view(np.uint16))
+    assert not np.array_equal(a, c)
+    assert abs(float(a.astype(np.float64).mean())) < 0.06
+    assert abs(float(a.astype(np.float64).std()) - 1.0) < 0.05
+    u = oracle.gen_u8(7, 5, (1 << 16,))
+    assert u.min() == 0 and u.max() == 255
+    assert abs(np.bincount(u, minlength=256).std() / 256.0) < 0.2
+    p = oracle.gen_palette(7, 6, 32, 0.02)
+    assert (np.diff(p.astype(np.float32), axis=1) >= 0).all()
+    assert abs(float(p.astype(np.float64).std()) - 0.02) < 0.003
+    img = oracle.gen_uniform(7, 8, (10000,), -1.0, 1.0)
+    assert img.min() >= -1.0 and img.max() <= 1.0
+
+
+def test_dequant_golden(oracle, golden):
+    # Metal/Dequantize.metal:17-32: out[i] = palette[idx[i]] (bit-exact).
+    w = oracle.dequant(golden["dq_idx"], golden["dq_pal"])
+    assert np.array_equal(w.view(np.uint16), golden["dq_w"].view(np.uint16))
+    # identity-like palette row: P[i] = i - 128
+    assert np.array_equal(w[2].astype(np.float32), golden["dq_idx"][2].astype(np.float32) - 128)
+
+
+@pytest.mark.parametrize("epi,key", [(0, "lin_y_bias"), (1, "lin_y_gelu"), (2, "lin_y_res"),
+                                     (3, "lin_y_rope")])
+def test_linear_golden(oracle, golden, epi, key):
+    y = oracle.linear(golden["lin_x"], golden["lin_idx"], golden["lin_pal"], golden["lin_bias"],
+                      epilogue=epi, residual=golden["lin_res"] if epi == 2 else None,
+                      rope=golden["lin_table"].astype(np.float32) if epi == 3 else None,
+                      rope_period=24, heads=2, head_dim=64)
+    # float32 accumulation vs float64: at most one fp16 rounding step apart.
+    assert f16_ulps(y, golden[key]) <= 2
+    assert max_rel_err(y, golden[key]) < 2e-3
+
+
+def test_layernorm_golden(oracle, golden):
+    y = oracle.layernorm(golden["ln_x"], golden["ln_g"], golden["ln_b"], 1e-6)
+    assert f16_ulps(y, golden["ln_y"]) <= 1
+
+
+def test_rope_table_golden_and_kat(oracle, golden):
+    t = oracle.rope_table(4, 6)
+    assert np.abs(t - golden["rope_table_4x6"]).max() < 2e-6
+    # KATs from Metal/RoPE.metal:22-52. Token 0 = (h 0, w 0): identity rotation.
+    assert np.allclose(t[0, :, 0], 1.0) and np.allclose(t[0, :, 1], 0.0)
+    # token (h=1, w=2) = 1*6 + 2: pair 0 (x axis, freq 1) has angle 2; pair 16
+    # (y axis, freq 1) has angle 1; pair 1 has freq 10000^(-1/16).
+    p = 1 * 6 + 2
+    assert abs(t[p, 0, 0] - math.cos(2.0)) < 1e-6 and abs(t[p, 0, 1] - math.sin(2.0)) < 1e-6
+    assert abs(t[p, 16, 0] - math.cos(1.0)) < 1e-6
+    f1 = 10000.0 ** (-1.0 / 16.0)
+    assert abs(t[p, 1, 1] - math.sin(2.0 * f1)) < 1e-6
+    # every entry is a unit vector (the only property RoPETests.swift:108-113 checks)
+    assert np.allclose((t ** 2).sum(-1), 1.0, atol=1e-6)
+
+
+def test_rope_apply_golden(oracle, golden):
+    out = oracle.rope_apply(golden["rope_qkv"], 2, 64, golden["rope_table_4x6"], 24)
+    assert f16_ulps(out, golden["rope_out"]) <= 1
+    # v third untouched
+    assert np.array_equal(out[:, 256:].view(np.uint16), golden["rope_qkv"][:, 256:].view(np.uint16))
+
+
+def test_attention_golden(oracle, golden):
+    o = oracle.attention(golden["att_qkv"], 2, 37, 2, 64)
+    assert max_rel_err(o, golden["att_o"]) < 2e-3
+
+
+def test_attention_kat_zero_query_is_mean_of_v(oracle):
+    # q = 0 -> uniform softmax -> output = mean of V (AttentionKernels.swift:48-68).
+    seq, heads = 50, 2
+    qkv = oracle.gen_normal(3, 9, (seq, 3 * heads * 64))
+    qkv[:, :heads * 64] = 0
+    o = oracle.attention(qkv, 1, seq, heads, 64)
+    v = qkv[:, 2 * heads * 64:].astype(np.float64)
+    assert np.abs(o.astype(np.float64) - v.mean(0)).max() < 2e-3
+
+
+@pytest.mark.parametrize("order", [0, 1])
+def test_prune_golden_with_ties(oracle, golden, order):
+    feats, _, idx = oracle.prune(golden["pr_x"], 2, 24, 12, norm=0, order=order)
+    assert np.array_equal(idx, golden[f"pr_idx_o{order}"])
+    assert np.array_equal(feats.view(np.uint16), golden[f"pr_feats_o{order}"].view(np.uint16))
+
+
+def test_prune_l1_score(oracle, golden):
+    _, _, idx = oracle.prune(golden["pr_x"], 2, 24, 12, norm=1, order=0)
+    assert np.array_equal(idx, golden["pr_idx_l1"])
+
+
+def test_prune_gathers_rope_rows(oracle):
+    x = oracle.gen_normal(1, 2, (2 * 16, 32))
+    table = oracle.rope_table(4, 4)
+    feats, rope_out, idx = oracle.prune(x, 2, 16, 5, rope=table, rope_period=16)
+    for b in range(2):
+        for i in range(5):
+            assert np.array_equal(rope_out[b * 5 + i], table[idx[b, i]])
+
+
+def test_patch_embed_golden(oracle, golden):
+    out = oracle.patch_embed(golden["pe_img"], golden["pe_w"], golden["pe_b"], 14)
+    assert f16_ulps(out, golden["pe_out"]) <= 2
+
+
+def test_vit_block_golden(oracle, golden):
+    blk = oracle.SyntheticBlock.__new__(oracle.SyntheticBlock)
+    dim = 128
+    blk.ln1_gamma = blk.ln2_gamma = np.ones(dim, F16)
+    blk.ln1_beta = blk.ln2_beta = np.zeros(dim, F16)
+    for name in ("qkv", "proj", "fc1", "fc2"):
+        setattr(blk, name, {"idx": golden[f"blk_{name}_idx"], "palette": golden[f"blk_{name}_pal"],
+                            "bias": golden[f"blk_{name}_bias"]})
+    y = oracle.vit_block(golden["blk_x"], 1, 16, 2, blk, golden["blk_table"], 16)
+    assert max_rel_err(y, golden["blk_y"]) < 5e-3
+
+
+def test_encoder_small_end_to_end(oracle):
+    # 2 blocks, 8x8 grid, prune after block 1 to 32 tokens: shapes, index order,
+    # determinism (same seed -> bit-identical output).
+    dim, heads, hidden = 256, 4, 512
+    blocks = [oracle.SyntheticBlock(11, i, dim, hidden) for i in range(2)]
+    img = oracle.gen_uniform(11, 99, (1, 112, 112, 3), -1.0, 1.0)
+    pw = oracle.gen_normal(11, 98, (dim, 3, 14, 14), 0.0, 0.02)
+    pb = oracle.gen_normal(11, 97, (dim,), 0.0, 0.02)
+    f1, i1 = oracle.encoder_forward(img, blocks, pw, pb, heads=heads, prune_after=1, keep=32)
+    f2, i2 = oracle.encoder_forward(img, blocks, pw, pb, heads=heads, prune_after=1, keep=32)
+    assert f1.shape == (1, 32, dim) and i1.shape == (1, 32)
+    assert (np.diff(i1[0]) > 0).all() and i1.min() >= 0 and i1.max() < 64
+    assert np.array_equal(f1.view(np.uint16), f2.view(np.uint16)) and np.array_equal(i1, i2)
+    assert np.isfinite(f1.astype(np.float32)).all()
