@@ -394,7 +394,10 @@ def test_encoder_small_device_and_host_api(ctx, sam3, oracle):
 
 def test_encoder_full_size_two_blocks_matches_oracle(sam3, oracle):
     # 1008^2 image, full width (1024, 16 heads, 4096), two blocks with the
-    # prune (to 2592 tokens by L2 norm) between them.
+    # prune (to 2592 tokens by L2 norm) between them. Upstream fp16 rounding
+    # differs between the two sides, so the kept sets may differ only for
+    # tokens whose oracle score lies within a relative 1e-3 of the cut; the
+    # output rows of tokens both sides kept must agree within the fp16 spec.
     with sam3.Context(0, num_blocks=2, prune_after_block=1, max_batch=1) as ctx:
         blocks = [oracle.SyntheticBlock(41, i) for i in range(2)]
         pw = oracle.gen_normal(41, 900, (1024, 3, 14, 14), 0.0, 0.02)
@@ -404,12 +407,21 @@ def test_encoder_full_size_two_blocks_matches_oracle(sam3, oracle):
         hf = np.empty((1, 2592, 1024), F16)
         hi = np.empty((1, 2592), np.int32)
         ctx.encoder_forward_host(img, 1, w, hf, hi)
-        ref_f, ref_i = oracle.encoder_forward(img, blocks, pw, pb, prune_after=1, keep=2592)
-        assert (np.diff(hi[0]) > 0).all()
-        same = hi[0] == ref_i[0]
-        assert same.mean() > 0.99
-        if same.all():
-            assert max_rel_err(hf, ref_f) < SPEC_TOL
+    ref_f, ref_i = oracle.encoder_forward(img, blocks, pw, pb, prune_after=1, keep=2592)
+    x1 = oracle.vit_block(oracle.patch_embed(img, pw, pb, 14), 1, 5184, 16, blocks[0],
+                          oracle.rope_table(72, 72), 5184)
+    scores = oracle.token_scores(x1).astype(np.float64)
+    srt = np.sort(scores)[::-1]
+    cut = 0.5 * (srt[2591] + srt[2592])
+    assert (np.diff(hi[0]) > 0).all()
+    g, r = set(hi[0].tolist()), set(ref_i[0].tolist())
+    diff = np.array(sorted(g ^ r), dtype=np.int64)
+    if diff.size:
+        assert np.abs(scores[diff] - cut).max() <= 1e-3 * cut, (diff.size, np.abs(scores[diff] - cut).max())
+    common = np.array(sorted(g & r))
+    gpos = np.searchsorted(hi[0], common)
+    rpos = np.searchsorted(ref_i[0], common)
+    assert max_rel_err(hf[0][gpos], ref_f[0][rpos]) < SPEC_TOL
 
 
 def test_encoder_full_32_blocks_properties(ctx_full, sam3, oracle):
