@@ -16,6 +16,8 @@
 //    MPSAttentionLayer does (it forces sEff = seqLen, MPSAttention.swift:97-104).
 #pragma once
 
+#include <cuda_runtime.h>
+
 #include <stdexcept>
 #include <string>
 #include <tuple>
@@ -178,10 +180,9 @@ class TransformerBlock {
     (void)windowed;
     const size_t bytes = (size_t)seqLen * batch * dim_ * 2;
     auto* out = static_cast<uint16_t*>(allocate(ctx_, bytes, recycledBuffers, "block output"));
-    check(ctx_, sam3_sync(ctx_), "block sync");
-    check(ctx_, sam3_upload(ctx_, out, nullptr, 0) == SAM3_ERR_INVALID_ARG ? SAM3_OK : SAM3_OK,
-          "block");
-    copy_device(out, input, bytes);
+    cudaStream_t s = static_cast<cudaStream_t>(sam3_ctx_stream(ctx_));
+    if (cudaMemcpyAsync(out, input, bytes, cudaMemcpyDeviceToDevice, s) != cudaSuccess)
+      throw SAM3Error(SAM3_ERR_CUDA, "TransformerBlock: input copy failed");
     check(ctx_, sam3_vit_block(ctx_, out, batch, seqLen, &w_, ropeFreqs,
                                ropeRows > 0 ? ropeRows : seqLen),
           "TransformerBlock");
@@ -189,10 +190,63 @@ class TransformerBlock {
   }
 
  private:
-  void copy_device(void* dst, const void* src, size_t bytes);
   sam3_ctx_t* ctx_;
   int dim_, heads_, hidden_;
   sam3_block_weights_t w_{};
+};
+
+// TokenPruner.swift:11-197. prune() returns (features, RoPE rows, indices).
+// The reference scores with L1 and orders by score (MPSGraph topK); the
+// defaults here follow the benchmark spec (L2, ascending token index).
+class TokenPruner {
+ public:
+  TokenPruner(sam3_ctx_t* ctx, int keepK, int dim, int ropeDim = 64,
+              int norm = SAM3_SCORE_L2, int order = SAM3_ORDER_INDEX)
+      : ctx_(ctx), keep_(keepK), dim_(dim), rope_dim_(ropeDim), norm_(norm), order_(order) {}
+  std::tuple<uint16_t*, float*, int32_t*> prune(const uint16_t* input, const float* ropeFreqs,
+                                                int seqLen, int batch,
+                                                BufferList& recycledBuffers) {
+    auto* feats = static_cast<uint16_t*>(
+        allocate(ctx_, (size_t)batch * keep_ * dim_ * 2, recycledBuffers, "PrunedFeats"));
+    auto* rope = static_cast<float*>(
+        allocate(ctx_, (size_t)batch * keep_ * rope_dim_ * 4, recycledBuffers, "PrunedRoPE"));
+    auto* idx = static_cast<int32_t*>(
+        allocate(ctx_, (size_t)batch * keep_ * 4, recycledBuffers, "PruneIndices"));
+    check(ctx_, sam3_prune(ctx_, input, batch, seqLen, dim_, keep_, norm_, order_, ropeFreqs,
+                           seqLen, rope_dim_, feats, rope, idx),
+          "TokenPruner.prune");
+    return {feats, rope, idx};
+  }
+
+ private:
+  sam3_ctx_t* ctx_;
+  int keep_, dim_, rope_dim_, norm_, order_;
+};
+
+// ViTEncoder.swift:1056-1481: image -> pruned token features (+ indices).
+class ViTEncoder {
+ public:
+  ViTEncoder(sam3_ctx_t* ctx, const sam3_encoder_weights_t& w, int embedDim = 1024)
+      : ctx_(ctx), w_(w), dim_(embedDim) {}
+  // image: device fp16 NHWC [batch, S, S, 3]. Returns feats [batch, keep, dim];
+  // the kept token indices [batch, keep] go to *indices. Both buffers are
+  // appended to recycledBuffers.
+  uint16_t* forward(const uint16_t* image, int batch, BufferList& recycledBuffers,
+                    int32_t** indices = nullptr) {
+    const int keep = sam3_encoder_out_tokens(ctx_);
+    auto* idx = static_cast<int32_t*>(
+        allocate(ctx_, (size_t)batch * keep * 4, recycledBuffers, "encoder indices"));
+    auto* feats = static_cast<uint16_t*>(
+        allocate(ctx_, (size_t)batch * keep * dim_ * 2, recycledBuffers, "encoder features"));
+    check(ctx_, sam3_encoder_forward(ctx_, image, batch, &w_, feats, idx), "ViTEncoder.forward");
+    if (indices) *indices = idx;
+    return feats;
+  }
+
+ private:
+  sam3_ctx_t* ctx_;
+  sam3_encoder_weights_t w_;
+  int dim_;
 };
 
 }  // namespace sam3

@@ -1,0 +1,118 @@
+#!/usr/bin/env python
+"""Kernel micro-benchmarks for libsam3cuda (one operator, one shape).
+
+    python microbench.py gemm --m 41472 --n 4096 --k 1024 --epi gelu
+    python microbench.py attention --batch 8 --seq 5184
+    python microbench.py layernorm --m 41472
+
+Inputs are synthetic device tensors (torch is used only to allocate and fill
+them); each iteration calls the operator through the C ABI; timings are CUDA
+events on the library's stream around each launch (sam3_profile_*), after
+warm-up. Prints one JSON line per operator.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import sys
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, HERE)
+
+EPIS = {"bias": 0, "gelu": 1, "residual": 2, "rope": 3}
+
+
+def peaks():
+    try:
+        with open(os.path.join(os.path.dirname(HERE), "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["bf16_tflops"]), float(p["hbm_gbs"])
+    except Exception:
+        return 1590.0, 6650.0
+
+
+def main():
+    import torch
+    import sam3cuda as sam3
+
+    ap = argparse.ArgumentParser()
+    ap.add_argument("op", choices=("gemm", "attention", "layernorm", "dequant"))
+    ap.add_argument("--m", type=int, default=41472)
+    ap.add_argument("--n", type=int, default=4096)
+    ap.add_argument("--k", type=int, default=1024)
+    ap.add_argument("--epi", choices=tuple(EPIS), default="bias")
+    ap.add_argument("--batch", type=int, default=8)
+    ap.add_argument("--seq", type=int, default=5184)
+    ap.add_argument("--heads", type=int, default=16)
+    ap.add_argument("--iters", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    a = ap.parse_args()
+
+    dev = torch.device("cuda", 0)
+    ctx = sam3.Context(0, max_batch=1)
+    tf_peak, bw_peak = peaks()
+    g = torch.Generator(device=dev)
+    g.manual_seed(0)
+
+    def run(fn):
+        for _ in range(a.warmup):
+            fn()
+        ctx.sync()
+        ctx.profile_enable(True)
+        for _ in range(a.iters):
+            fn()
+        prof = ctx.profile_read()
+        ctx.profile_enable(False)
+        return prof
+
+    if a.op in ("gemm", "dequant"):
+        x = torch.randn((a.m, a.k), generator=g, device=dev).half()
+        idx = torch.randint(0, 256, (a.n, a.k), generator=g, device=dev, dtype=torch.uint8)
+        pal = (torch.randn((a.n, 256), generator=g, device=dev) * 0.02).half().sort(dim=1).values
+        bias = (torch.randn((a.n,), generator=g, device=dev) * 0.01).half()
+        y = torch.empty((a.m, a.n), dtype=torch.float16, device=dev)
+        w = sam3.palette_linear(idx, pal.contiguous(), bias, a.n, a.k)
+        if a.op == "dequant":
+            out = torch.empty((a.n, a.k), dtype=torch.float16, device=dev)
+            prof = run(lambda: ctx.dequant_palette(w, out))["other"]
+            ms = prof["ms"] / prof["launches"]
+            print(json.dumps({"op": "dequant", "n": a.n, "k": a.k, "us": ms * 1e3,
+                              "gbs": prof["bytes"] / prof["launches"] / (ms * 1e-3) / 1e9,
+                              "frac_hbm": prof["bytes"] / prof["launches"] / (ms * 1e-3) / 1e9 / bw_peak}))
+            return
+        epi = EPIS[a.epi]
+        res = torch.randn((a.m, a.n), generator=g, device=dev).half() if epi == 2 else None
+        rope = None
+        rows = 0
+        if epi == 3:
+            rows = a.seq
+            rope = torch.empty((rows, 32, 2), dtype=torch.float32, device=dev)
+            side = int(round(rows ** 0.5))
+            ctx.rope_table(side, rows // side, 64, 10000.0, rope)
+        prof = run(lambda: ctx.linear_palette(x, a.m, w, epi, y, res, rope, rows))["gemm"]
+        ms = prof["ms"] / prof["launches"]
+        tf = prof["flops"] / prof["launches"] / (ms * 1e-3) / 1e12
+        print(json.dumps({"op": "gemm", "m": a.m, "n": a.n, "k": a.k, "epi": a.epi, "us": ms * 1e3,
+                          "tflops": tf, "frac_burst_peak": tf / tf_peak}))
+    elif a.op == "attention":
+        qkv = torch.randn((a.batch * a.seq, 3 * a.heads * 64), generator=g, device=dev).half()
+        o = torch.empty((a.batch * a.seq, a.heads * 64), dtype=torch.float16, device=dev)
+        prof = run(lambda: ctx.attention(qkv, a.batch, a.seq, a.heads, 64, 0.125, o))["attention"]
+        ms = prof["ms"] / prof["launches"]
+        tf = prof["flops"] / prof["launches"] / (ms * 1e-3) / 1e12
+        print(json.dumps({"op": "attention", "batch": a.batch, "seq": a.seq, "heads": a.heads,
+                          "us": ms * 1e3, "tflops": tf, "frac_burst_peak": tf / tf_peak}))
+    else:
+        x = torch.randn((a.m, 1024), generator=g, device=dev).half()
+        y = torch.empty_like(x)
+        prof = run(lambda: ctx.layernorm(x, a.m, 1024, None, None, 1e-6, y))["layernorm"]
+        ms = prof["ms"] / prof["launches"]
+        gbs = prof["bytes"] / prof["launches"] / (ms * 1e-3) / 1e9
+        print(json.dumps({"op": "layernorm", "m": a.m, "us": ms * 1e3, "gbs": gbs,
+                          "frac_hbm": gbs / bw_peak}))
+    ctx.close()
+
+
+if __name__ == "__main__":
+    main()
