@@ -185,6 +185,33 @@ sam3_status_t sam3_attention(sam3_ctx_t* ctx, const uint16_t* qkv, int32_t batch
                              int32_t seq, int32_t heads, int32_t head_dim, float scale,
                              uint16_t* o);
 
+/* Capacity of sam3_prune_noalloc's fixed score scratch (batch * seq rows). */
+#define SAM3_PRUNE_NOALLOC_MAX_ROWS 65536
+
+/* sam3_prune without a context and without allocating anything: the same
+ * scoring, selection (ties to the lower index) and gather, enqueued on
+ * `cuda_stream` (a cudaStream_t; NULL = the legacy default stream).
+ * No counterpart in the reference; it exists for callers that cannot
+ * allocate device memory: code that runs inside a host application owning
+ * every device allocation under a fixed budget, threads that must not call
+ * cudaMalloc / cudaFree because those calls can block or synchronise the
+ * device, and callers with no sam3 context (creating one allocates its
+ * workspace). Such a caller passes its own input and output buffers; the
+ * per-token score scratch is a fixed 256 KB device array inside the library
+ * (SAM3_PRUNE_NOALLOC_MAX_ROWS floats, held on every GPU that loads the
+ * library until the process exits). batch * seq beyond that limit returns
+ * SAM3_ERR_SHAPE; other argument errors return SAM3_ERR_INVALID_ARG /
+ * SAM3_ERR_SHAPE as sam3_prune does, and a failed launch SAM3_ERR_CUDA.
+ * The first call on each device looks up the array's device address, so make
+ * it before any stream capture. All calls share the one array: calls that
+ * overlap on the GPU (different streams, or graph replays running at the same
+ * time) race on it and must be serialised by the caller. */
+sam3_status_t sam3_prune_noalloc(void* cuda_stream, const uint16_t* x, int32_t batch,
+                                 int32_t seq, int32_t d, int32_t keep, int32_t norm,
+                                 int32_t order, const float* rope_in, int32_t rope_rows,
+                                 int32_t rope_cols, uint16_t* feats, float* rope_out,
+                                 int32_t* idx);
+
 /* Token scores f32 [rows] = L2 norm or L1 (sum |x|) of each row.
  * Reference: TokenPruner.swift:54-56. */
 sam3_status_t sam3_token_scores(sam3_ctx_t* ctx, const uint16_t* x, int32_t rows,

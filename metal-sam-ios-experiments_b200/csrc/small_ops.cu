@@ -2,6 +2,7 @@
 // table and stand-alone RoPE, token scores, token pruning (radix select +
 // stable compaction + gather) and the patch-embedding im2col.
 #include <algorithm>
+#include <mutex>
 
 #include "common.cuh"
 #include "internal.h"
@@ -543,3 +544,81 @@ sam3_status_t sam3_patch_embed(sam3_ctx_t* ctx, const uint16_t* image, int32_t b
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------- allocation-free pruning
+// The score scratch of sam3_prune_noalloc lives in this fixed device array
+// instead of a context workspace. Every GPU that loads the library holds it
+// (SAM3_PRUNE_NOALLOC_MAX_ROWS floats) until the process exits.
+namespace {
+static __device__ __align__(256) float g_noalloc_scores[SAM3_PRUNE_NOALLOC_MAX_ROWS];
+constexpr int kMaxDevices = 64;
+std::mutex g_noalloc_mu;
+float* g_noalloc_addr[kMaxDevices] = {};  // device address of the array, per device
+}  // namespace
+
+extern "C" sam3_status_t sam3_prune_noalloc(void* cuda_stream, const uint16_t* x, int32_t batch,
+                                            int32_t seq, int32_t d, int32_t keep, int32_t norm,
+                                            int32_t order, const float* rope_in,
+                                            int32_t rope_rows, int32_t rope_cols,
+                                            uint16_t* feats, float* rope_out, int32_t* idx) {
+  if (!x || !feats || !idx) return SAM3_ERR_INVALID_ARG;
+  if (batch <= 0 || seq <= 0 || d <= 0 || d % 8 || keep <= 0 || keep > seq || seq > 16384)
+    return SAM3_ERR_SHAPE;
+  if ((long long)batch * seq > SAM3_PRUNE_NOALLOC_MAX_ROWS) return SAM3_ERR_SHAPE;
+  if (norm != SAM3_SCORE_L2 && norm != SAM3_SCORE_L1) return SAM3_ERR_INVALID_ARG;
+  if (order != SAM3_ORDER_INDEX && order != SAM3_ORDER_SCORE) return SAM3_ERR_INVALID_ARG;
+  if (order == SAM3_ORDER_SCORE && keep > 8192) return SAM3_ERR_SHAPE;
+  if ((rope_in == nullptr) != (rope_out == nullptr) ||
+      (rope_in && (rope_rows <= 0 || rope_cols <= 0)))
+    return SAM3_ERR_INVALID_ARG;
+  if (!aligned16(x) || !aligned16(feats)) return SAM3_ERR_INVALID_ARG;
+
+  // Set-up, once per device with that device current: the host-side name of
+  // a __device__ array is only a stand-in, so ask the runtime for its device
+  // address and hand that to the kernels.
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+    cudaGetLastError();
+    return SAM3_ERR_CUDA;
+  }
+  float* scores = nullptr;
+  {
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (!g_noalloc_addr[dev]) {
+      void* p = nullptr;
+      if (cudaGetSymbolAddress(&p, g_noalloc_scores) != cudaSuccess || !p) {
+        cudaGetLastError();
+        return SAM3_ERR_CUDA;
+      }
+      g_noalloc_addr[dev] = static_cast<float*>(p);
+    }
+    scores = g_noalloc_addr[dev];
+  }
+
+  cudaStream_t stream = static_cast<cudaStream_t>(cuda_stream);
+  const long long rows = (long long)batch * seq;
+  // Every score is rewritten before it is read, so nothing needs clearing.
+  token_score_kernel<<<blocks_for(rows, 8), 256, 0, stream>>>(
+      reinterpret_cast<const __half*>(x), (int)rows, d, norm, scores);
+  if (cudaGetLastError() != cudaSuccess) return SAM3_ERR_CUDA;
+  size_t smem = ((size_t)seq * 4 + 15) & ~(size_t)15;
+  if (order == SAM3_ORDER_SCORE) {
+    int p2 = 1;
+    while (p2 < keep) p2 <<= 1;
+    smem += (size_t)p2 * 8;
+  }
+  if (smem > 48 * 1024 &&
+      cudaFuncSetAttribute(prune_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)smem) != cudaSuccess) {
+    cudaGetLastError();
+    return SAM3_ERR_CUDA;
+  }
+  prune_select_kernel<<<batch, 1024, smem, stream>>>(scores, seq, keep, order, idx);
+  if (cudaGetLastError() != cudaSuccess) return SAM3_ERR_CUDA;
+  const int total = batch * keep;
+  prune_gather_kernel<<<blocks_for(total, 8), 256, 0, stream>>>(
+      reinterpret_cast<const __half*>(x), seq, d, keep, idx, rope_in, rope_rows > 0 ? rope_rows : 1,
+      rope_cols, reinterpret_cast<__half*>(feats), rope_out, total);
+  if (cudaGetLastError() != cudaSuccess) return SAM3_ERR_CUDA;
+  return SAM3_OK;
+}

@@ -103,7 +103,10 @@ SIGNATURES = {
     "sam3_encoder_out_tokens": (C.c_int32, [_P]),
     "sam3_profile_enable": (_S, [_P, _I]),
     "sam3_profile_read": (_S, [_P, C.POINTER(Profile)]),
+    "sam3_prune_noalloc": (_S, [_P, _P, _I, _I, _I, _I, _I, _I, _P, _I, _I, _P, _P, _P]),
 }
+
+PRUNE_NOALLOC_MAX_ROWS = 65536
 
 
 def _load():
