@@ -67,6 +67,15 @@ def workload_config(args, world):
     }
 
 
+def image_shard(rank, world, images):
+    """Contiguous block of images owned by `rank`: (first global index, count).
+    Images are independent, so the ranks exchange nothing."""
+    if world <= 0 or images % world:
+        raise ValueError(f"{images} images do not split evenly over {world} ranks")
+    per = images // world
+    return rank * per, per
+
+
 def encoder_flops_per_image():
     lin_pre = 2.0 * SEQ * DIM * (3 * DIM + DIM + 2 * HIDDEN)
     lin_post = 2.0 * KEEP * DIM * (3 * DIM + DIM + 2 * HIDDEN)
@@ -251,21 +260,21 @@ def run_ours(args):
     world, rank, local = dist_env()
     if world != args.gpus:
         args.gpus = world
-    if args.images % world:
-        raise SystemExit(f"--images {args.images} not divisible by {world} ranks")
     torch.cuda.set_device(local)
     if world > 1:
         import datetime
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=torch.device("cuda", local))
-    per_rank = args.images // world
+    first, per_rank = image_shard(rank, world, args.images)
     batch = min(args.batch, per_rank)
     dev = torch.device("cuda", local)
     ctx = sam3.Context(local, max_batch=batch)
     w = make_weights(torch, sam3, dev, 1234)
     gen = torch.Generator(device=dev)
-    gen.manual_seed(99 + rank)
-    imgs = (torch.rand((per_rank, IMAGE, IMAGE, 3), generator=gen, device=dev) * 2 - 1).half()
+    imgs = torch.empty((per_rank, IMAGE, IMAGE, 3), dtype=torch.float16, device=dev)
+    for i in range(per_rank):  # image i of the job is seeded by its global index
+        gen.manual_seed(1000 + first + i)
+        imgs[i] = (torch.rand((IMAGE, IMAGE, 3), generator=gen, device=dev) * 2 - 1).half()
     keep = ctx.out_tokens
     feats = torch.empty((per_rank, keep, DIM), dtype=torch.float16, device=dev)
     idx = torch.empty((per_rank, keep), dtype=torch.int32, device=dev)

@@ -14,10 +14,14 @@
 // buffer in 128B-XOR-swizzled shared memory; fp16 m16n8k16 tensor-core MMAs
 // with fp32 accumulation; online softmax in fp32 (exp2 with the scale folded
 // into log2 e); P is rounded to fp16 for the PV product.
+#include <stdlib.h>
+
 #include "common.cuh"
 #include "internal.h"
 
 namespace sam3 {
+sam3_status_t attention_tc(sam3_ctx_t* ctx, const uint16_t* qkv, int batch, int seq, int heads,
+                           float scale, uint16_t* o);
 namespace {
 
 constexpr int HD = 64;
@@ -237,6 +241,15 @@ sam3_status_t attention(sam3_ctx_t* ctx, const uint16_t* qkv, int batch, int seq
     return set_error(ctx, SAM3_ERR_SHAPE, "attention: bad shape");
   if (!aligned16(qkv) || !aligned16(o))
     return set_error(ctx, SAM3_ERR_INVALID_ARG, "attention: pointers must be 16-byte aligned");
+  static const bool legacy = [] {
+    const char* v = getenv("SAM3_ATTENTION_MMA_SYNC");
+    return v && v[0] == '1';
+  }();
+  if (!legacy) {
+    ProfScope prof(ctx, SAM3_PROF_ATTENTION, 4.0 * batch * heads * (double)seq * seq * HD,
+                   8.0 * batch * seq * heads * HD);
+    return attention_tc(ctx, qkv, batch, seq, heads, scale, o);
+  }
   const float scale_log2 = scale * 1.4426950408889634f;
   dim3 grid((seq + BQ - 1) / BQ, heads, batch);
   ProfScope prof(ctx, SAM3_PROF_ATTENTION, 4.0 * batch * heads * (double)seq * seq * HD,

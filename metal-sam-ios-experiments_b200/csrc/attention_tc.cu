@@ -1,0 +1,298 @@
+// attention_tc.cu - global softmax attention on the sm_100a tensor cores
+// (tcgen05 MMAs with tensor-memory accumulators, TMA-fed K/V stages).
+//
+// o[b*S + i, h*64 + :] = softmax_j(q_i . k_j * scale) v_j for every image b
+// and head h, read straight from the packed QKV GEMM output [B*S, 3*H*64].
+// Reference: scaledDotProductAttention (MPSAttention.swift:165-176, scale
+// 1/sqrt(64), no mask) and AttentionKernels.swift:48-68 (explicit form).
+//
+// One CTA = 128 query rows of one (image, head); two CTAs per SM so one CTA's
+// softmax overlaps the other's MMAs. Warp roles:
+//   warp 0   TMA producer: Q tile once, then K/V tiles of 128 keys through a
+//            2-stage ring (128B-swizzled, straight from the packed rows).
+//   warp 1   TMEM allocator + single-thread MMA issuer:
+//              S = Q K^T   (M=128, N=128, K=64, both operands K-major)
+//              O = P V     (M=128, N=64,  K=128, P read from tensor memory,
+//                           V as an MN-major operand)
+//   warps 2-5  one thread per query row (its TMEM lane): row max over the
+//            valid keys, p = 2^(s*scale*log2e - m) rounded to fp16 and written
+//            back over S in tensor memory, running sum, and the rescaled
+//            fp32 output accumulator kept in registers.
+// Tensor memory (256 columns): S / P at columns [0,128), O at [128,192).
+#include "common.cuh"
+#include "internal.h"
+
+namespace sam3 {
+namespace {
+
+constexpr int HD = 64, BQ = 128, BKV = 128, STAGES = 2;
+constexpr int THREADS = 192;
+constexpr int TILE_BYTES = BQ * HD * 2;  // 16 KB per Q / K / V tile
+constexpr int OFF_Q = 0;
+constexpr int OFF_K = OFF_Q + TILE_BYTES;
+constexpr int OFF_V = OFF_K + STAGES * TILE_BYTES;
+constexpr int OFF_BAR = OFF_V + STAGES * TILE_BYTES;
+constexpr int NUM_BARS = 1 + 2 * STAGES + 4 + 1;
+constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;
+constexpr int SMEM_BYTES = OFF_MISC + 16 + 1024;
+constexpr uint32_t TMEM_COLS = 256;
+constexpr uint32_t COL_S = 0, COL_O = 128;
+constexpr uint32_t IDESC_S = umma_idesc_f16(128, BKV, 0);  // K-major B (keys x d)
+constexpr uint32_t IDESC_O = umma_idesc_f16(128, HD, 1);   // MN-major B (keys x d)
+
+struct AttnArgs {
+  __half* out;
+  int* err;
+  int seq, heads, dim;
+  float scale_log2;
+};
+
+__global__ void __launch_bounds__(THREADS, 2)
+    attn_tc_kernel(const __grid_constant__ CUtensorMap tmap_qkv, const AttnArgs args) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  const uint32_t sbase = smem_u32(smem);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int qt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int seq = args.seq, dim = args.dim;
+  const int row0 = b * seq;  // first packed row of this image
+  const int q0 = qt * BQ;
+  const int ntiles = (seq + BKV - 1) / BKV;
+
+  const uint32_t bar_q = sbase + OFF_BAR;
+  const uint32_t bar_kv_full = bar_q + 8;
+  const uint32_t bar_kv_empty = bar_kv_full + 8 * STAGES;
+  const uint32_t bar_s_full = bar_kv_empty + 8 * STAGES;
+  const uint32_t bar_p_full = bar_s_full + 8;
+  const uint32_t bar_o_full = bar_p_full + 8;
+  const uint32_t bar_o_free = bar_o_full + 8;
+  const uint32_t bar_drain = bar_o_free + 8;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + OFF_MISC);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + OFF_MISC + 4);
+
+  if (threadIdx.x == 0) {
+    mbar_init(bar_q, 1);
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(bar_kv_full + 8 * s, 1);
+      mbar_init(bar_kv_empty + 8 * s, 1);
+    }
+    mbar_init(bar_s_full, 1);
+    mbar_init(bar_p_full, 128);
+    mbar_init(bar_o_full, 1);
+    mbar_init(bar_o_free, 128);
+    mbar_init(bar_drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    prefetch_tmap(&tmap_qkv);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------- producer
+    if (lane == 0) {
+      uint32_t issued = 0, issued_par = 0;
+      bool q_issued = false;
+      mbar_arrive_expect_tx(bar_q, TILE_BYTES);
+      tma_load_2d(sbase + OFF_Q, &tmap_qkv, bar_q, h * HD, row0 + q0);
+      q_issued = true;
+      for (int j = 0; j < ntiles; ++j) {
+        const int s = j % STAGES;
+        const uint32_t ph = (uint32_t)(j / STAGES) & 1u;
+        if (!mbar_wait(bar_kv_empty + 8 * s, ph ^ 1, abort_flag, args.err, kDevErrTimeoutAttn))
+          break;
+        mbar_arrive_expect_tx(bar_kv_full + 8 * s, 2 * TILE_BYTES);
+        const int r = row0 + j * BKV;
+        tma_load_2d(sbase + OFF_K + s * TILE_BYTES, &tmap_qkv, bar_kv_full + 8 * s, dim + h * HD, r);
+        tma_load_2d(sbase + OFF_V + s * TILE_BYTES, &tmap_qkv, bar_kv_full + 8 * s,
+                    2 * dim + h * HD, r);
+        issued |= 1u << s;
+        issued_par = (issued_par & ~(1u << s)) | (ph << s);
+      }
+      if (*abort_flag) {
+        if (q_issued) mbar_wait_drain(bar_q, 0);
+        for (int s = 0; s < STAGES; ++s)
+          if (issued & (1u << s)) mbar_wait_drain(bar_kv_full + 8 * s, (issued_par >> s) & 1u);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      bool issued_any = false;
+      if (mbar_wait(bar_q, 0, abort_flag, args.err, kDevErrTimeoutAttn)) {
+        const uint32_t q_addr = sbase + OFF_Q;
+        for (int j = 0; j < ntiles; ++j) {
+          const int s = j % STAGES;
+          const uint32_t ph = (uint32_t)(j / STAGES) & 1u;
+          if (!mbar_wait(bar_kv_full + 8 * s, ph, abort_flag, args.err, kDevErrTimeoutAttn)) break;
+          // S aliases P of the previous tile: let that P V MMA finish reading first.
+          if (j > 0 && !mbar_wait(bar_o_full, (uint32_t)(j - 1) & 1u, abort_flag, args.err,
+                                  kDevErrTimeoutAttn))
+            break;
+          tc_fence_after();
+          const uint32_t k_addr = sbase + OFF_K + s * TILE_BYTES;
+          const uint32_t v_addr = sbase + OFF_V + s * TILE_BYTES;
+          // S = Q K^T
+#pragma unroll
+          for (int kk = 0; kk < HD / 16; ++kk)
+            umma_f16_ss(tmem + COL_S, umma_desc_sw128(q_addr + kk * 32),
+                        umma_desc_sw128(k_addr + kk * 32), IDESC_S, kk != 0);
+          umma_commit(bar_s_full);
+          issued_any = true;
+          // O = P V once the softmax wrote P and read the previous O.
+          if (!mbar_wait(bar_p_full, (uint32_t)j & 1u, abort_flag, args.err, kDevErrTimeoutAttn) ||
+              !mbar_wait(bar_o_free, ((uint32_t)j & 1u) ^ 1u, abort_flag, args.err,
+                         kDevErrTimeoutAttn))
+            break;
+          tc_fence_after();
+#pragma unroll
+          for (int kk = 0; kk < BKV / 16; ++kk)
+            umma_f16_ts(tmem + COL_O, tmem + COL_S + kk * 8,
+                        umma_desc_sw128_mn(v_addr + kk * 2048), IDESC_O, kk != 0);
+          umma_commit(bar_o_full);
+          umma_commit(bar_kv_empty + 8 * s);
+        }
+      }
+      if (*abort_flag && issued_any) {
+        umma_commit(bar_drain);
+        mbar_wait_drain(bar_drain, 0);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------- softmax rows
+    const int quad = warp & 3;
+    const int r = quad * 32 + lane;  // query row within the tile (TMEM lane)
+    const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16);
+    const float c = args.scale_log2;
+    float m_run = -INFINITY, l_run = 0.f;
+    float acc[HD];
+#pragma unroll
+    for (int d = 0; d < HD; ++d) acc[d] = 0.f;
+    bool ok = true;
+    for (int j = 0; j < ntiles && ok; ++j) {
+      ok = __all_sync(0xffffffffu, mbar_wait(bar_s_full, (uint32_t)j & 1u, abort_flag, args.err,
+                                             kDevErrTimeoutAttn));
+      if (!ok) break;
+      tc_fence_after();
+      const int valid = min(BKV, seq - j * BKV);  // keys of this tile inside the image
+      // pass 1: row max of the valid scores
+      float mx = -INFINITY;
+#pragma unroll 1
+      for (int cc = 0; cc < BKV / 32; ++cc) {
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(lane_base + COL_S + cc * 32, v);
+        tmem_wait_ld();
+#pragma unroll
+        for (int e = 0; e < 32; ++e)
+          if (cc * 32 + e < valid) mx = fmaxf(mx, __uint_as_float(v[e]));
+      }
+      const float m_new = fmaxf(m_run, mx * c);
+      const float alpha = ex2_approx(m_run - m_new);  // 0 on the first tile
+      // pass 2: p = 2^(s c - m), fp16 pairs over the S columns, running sum
+      float rs = 0.f;
+#pragma unroll 1
+      for (int cc = 0; cc < BKV / 32; ++cc) {
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(lane_base + COL_S + cc * 32, v);
+        tmem_wait_ld();
+        uint32_t pk[16];
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          const int k0 = cc * 32 + 2 * e;
+          const float p0 = k0 < valid ? ex2_approx(fmaf(__uint_as_float(v[2 * e]), c, -m_new)) : 0.f;
+          const float p1 =
+              k0 + 1 < valid ? ex2_approx(fmaf(__uint_as_float(v[2 * e + 1]), c, -m_new)) : 0.f;
+          rs += p0 + p1;
+          pk[e] = pack_half2(p0, p1);
+        }
+        tmem_st_32x32b_x16(lane_base + COL_S + cc * 16, pk);
+      }
+      tmem_wait_st();
+      m_run = m_new;
+      l_run = l_run * alpha + rs;
+      tc_fence_before();
+      mbar_arrive(bar_p_full);
+      // O_j = P_j V_j: fold into the register accumulator
+      ok = __all_sync(0xffffffffu, mbar_wait(bar_o_full, (uint32_t)j & 1u, abort_flag, args.err,
+                                             kDevErrTimeoutAttn));
+      if (!ok) break;
+      tc_fence_after();
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(lane_base + COL_O + half * 32, v);
+        tmem_wait_ld();
+#pragma unroll
+        for (int e = 0; e < 32; ++e) acc[half * 32 + e] = fmaf(acc[half * 32 + e], alpha, __uint_as_float(v[e]));
+      }
+      tc_fence_before();
+      mbar_arrive(bar_o_free);
+    }
+    if (ok) {
+      const int q = q0 + r;
+      if (q < seq) {
+        const float inv = 1.f / l_run;
+        uint4* dst = reinterpret_cast<uint4*>(args.out + (size_t)(row0 + q) * dim + h * HD);
+#pragma unroll
+        for (int c8 = 0; c8 < HD / 8; ++c8) {
+          uint4 o;
+          o.x = pack_half2(acc[8 * c8 + 0] * inv, acc[8 * c8 + 1] * inv);
+          o.y = pack_half2(acc[8 * c8 + 2] * inv, acc[8 * c8 + 3] * inv);
+          o.z = pack_half2(acc[8 * c8 + 4] * inv, acc[8 * c8 + 5] * inv);
+          o.w = pack_half2(acc[8 * c8 + 6] * inv, acc[8 * c8 + 7] * inv);
+          dst[c8] = o;
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, TMEM_COLS);
+  }
+}
+
+}  // namespace
+
+sam3_status_t attention_tc(sam3_ctx_t* ctx, const uint16_t* qkv, int batch, int seq, int heads,
+                           float scale, uint16_t* o) {
+  const int dim = heads * HD;
+  CUtensorMap map;
+  cuuint64_t dims[2] = {(cuuint64_t)(3 * dim), (cuuint64_t)batch * seq};
+  cuuint64_t strides[1] = {(cuuint64_t)(3 * dim) * 2};
+  cuuint32_t box[2] = {HD, BQ};
+  cuuint32_t es[2] = {1, 1};
+  CUresult r = encode_tiled()(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<uint16_t*>(qkv),
+                              dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                              CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return set_error(ctx, SAM3_ERR_CUDA, "attention: cuTensorMapEncodeTiled failed (%d)", (int)r);
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaError_t e = cudaFuncSetAttribute(attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         SMEM_BYTES);
+    if (e != cudaSuccess) return check_cuda(ctx, e, "attention smem attribute");
+    attr_set = true;
+  }
+  AttnArgs a;
+  a.out = reinterpret_cast<__half*>(o);
+  a.err = ctx->dev_err;
+  a.seq = seq;
+  a.heads = heads;
+  a.dim = dim;
+  a.scale_log2 = scale * 1.4426950408889634f;
+  dim3 grid((seq + BQ - 1) / BQ, heads, batch);
+  attn_tc_kernel<<<grid, THREADS, SMEM_BYTES, ctx->stream>>>(map, a);
+  return check_launch(ctx, "attn_tc_kernel");
+}
+
+}  // namespace sam3

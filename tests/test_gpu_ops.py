@@ -208,6 +208,18 @@ def test_attention_zero_query_is_mean_of_v(ctx, sam3, oracle):
     assert np.abs(got - v.mean(0)).max() < 2e-3
 
 
+@pytest.mark.parametrize("batch,seq,heads", [(3, 300, 2), (2, 2592, 4), (1, 129, 1)])
+def test_attention_batched_ragged_tiles(ctx, sam3, oracle, batch, seq, heads):
+    # key tiles of 128 that straddle image boundaries or end past the buffer
+    qkv = oracle.gen_normal(15, seq, (batch * seq, 3 * heads * 64))
+    o = ctx.alloc(batch * seq * heads * 64 * 2)
+    ctx.attention(ctx.upload(qkv), batch, seq, heads, 64, 0.125, o)
+    ctx.sync()
+    got = ctx.download(o, (batch * seq, heads * 64), F16)
+    ref = oracle.attention(qkv, batch, seq, heads, 64)
+    assert max_rel_err(got, ref) < 5e-3
+
+
 def test_attention_full_size_72x72_grid(ctx, sam3, oracle):
     seq, heads = 5184, 16
     qkv = oracle.gen_normal(11, 1, (seq, 3 * 1024))

@@ -1,0 +1,54 @@
+"""Host-side logic of the multi-GPU benchmark on CPU: image sharding over
+ranks (world size 2, gloo) and the max-over-ranks timing reduction."""
+import os
+import socket
+import sys
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from conftest import ROOT
+
+sys.path.insert(0, ROOT)
+import bench  # noqa: E402
+
+
+def test_image_shard_covers_every_image_once():
+    for world in (1, 2, 4, 8):
+        seen = []
+        for r in range(world):
+            first, count = bench.image_shard(r, world, 64)
+            seen.extend(range(first, first + count))
+        assert sorted(seen) == list(range(64))
+    with pytest.raises(ValueError):
+        bench.image_shard(0, 3, 64)
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, out):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    first, count = bench.image_shard(rank, world, 64)
+    owned = torch.zeros(64, dtype=torch.int64)
+    owned[first:first + count] = 1
+    dist.all_reduce(owned)  # every image owned by exactly one rank
+    t = torch.tensor([10.0 * (rank + 1)], dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)  # the job time is the slowest rank's
+    out[rank] = (int(owned.min()), int(owned.max()), float(t.item()))
+    dist.destroy_process_group()
+
+
+def test_two_rank_gloo_sharding_and_max_reduction():
+    port = _free_port()
+    with mp.Manager() as m:
+        out = m.dict()
+        mp.spawn(_worker, args=(2, port, out), nprocs=2, join=True)
+        res = dict(out)
+    assert res[0] == res[1] == (1, 1, 20.0)
