@@ -181,6 +181,7 @@ __global__ void __launch_bounds__(THREADS, 2)
       if (!ok) break;
       tc_fence_after();
       const int valid = min(BKV, seq - j * BKV);  // keys of this tile inside the image
+      const bool full = valid == BKV;               // only the last tile can be ragged
       // pass 1: row max of the valid scores
       float mx = -INFINITY;
 #pragma unroll 1
@@ -188,31 +189,51 @@ __global__ void __launch_bounds__(THREADS, 2)
         uint32_t v[32];
         tmem_ld_32x32b_x32(lane_base + COL_S + cc * 32, v);
         tmem_wait_ld();
+        if (full) {
 #pragma unroll
-        for (int e = 0; e < 32; ++e)
-          if (cc * 32 + e < valid) mx = fmaxf(mx, __uint_as_float(v[e]));
+          for (int e = 0; e < 32; e += 2)
+            mx = fmaxf(mx, fmaxf(__uint_as_float(v[e]), __uint_as_float(v[e + 1])));
+        } else {
+#pragma unroll
+          for (int e = 0; e < 32; ++e)
+            if (cc * 32 + e < valid) mx = fmaxf(mx, __uint_as_float(v[e]));
+        }
       }
       const float m_new = fmaxf(m_run, mx * c);
       const float alpha = ex2_approx(m_run - m_new);  // 0 on the first tile
       // pass 2: p = 2^(s c - m), fp16 pairs over the S columns, running sum
-      float rs = 0.f;
+      float rs0 = 0.f, rs1 = 0.f;
 #pragma unroll 1
       for (int cc = 0; cc < BKV / 32; ++cc) {
         uint32_t v[32];
         tmem_ld_32x32b_x32(lane_base + COL_S + cc * 32, v);
         tmem_wait_ld();
         uint32_t pk[16];
+        if (full) {
 #pragma unroll
-        for (int e = 0; e < 16; ++e) {
-          const int k0 = cc * 32 + 2 * e;
-          const float p0 = k0 < valid ? ex2_approx(fmaf(__uint_as_float(v[2 * e]), c, -m_new)) : 0.f;
-          const float p1 =
-              k0 + 1 < valid ? ex2_approx(fmaf(__uint_as_float(v[2 * e + 1]), c, -m_new)) : 0.f;
-          rs += p0 + p1;
-          pk[e] = pack_half2(p0, p1);
+          for (int e = 0; e < 16; ++e) {
+            const float p0 = ex2_approx(fmaf(__uint_as_float(v[2 * e]), c, -m_new));
+            const float p1 = ex2_approx(fmaf(__uint_as_float(v[2 * e + 1]), c, -m_new));
+            rs0 += p0;
+            rs1 += p1;
+            pk[e] = pack_half2(p0, p1);
+          }
+        } else {
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            const int k0 = cc * 32 + 2 * e;
+            const float p0 =
+                k0 < valid ? ex2_approx(fmaf(__uint_as_float(v[2 * e]), c, -m_new)) : 0.f;
+            const float p1 =
+                k0 + 1 < valid ? ex2_approx(fmaf(__uint_as_float(v[2 * e + 1]), c, -m_new)) : 0.f;
+            rs0 += p0;
+            rs1 += p1;
+            pk[e] = pack_half2(p0, p1);
+          }
         }
         tmem_st_32x32b_x16(lane_base + COL_S + cc * 16, pk);
       }
+      const float rs = rs0 + rs1;
       tmem_wait_st();
       m_run = m_new;
       l_run = l_run * alpha + rs;

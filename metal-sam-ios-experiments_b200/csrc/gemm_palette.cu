@@ -367,6 +367,285 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   }
 }
 
+// ============================================================================
+// Weight-stationary pair kernel (K <= 1024): a cluster of two CTAs owns a
+// 128-row weight slab (64 rows per CTA); each CTA expands its 64 x K slab into
+// shared memory ONCE (128 KB fp16, 128B-swizzled K-major, one 8 KB block per
+// 64-wide k-block) and then streams every 256-row M tile of its range past it
+// with pair MMAs (tcgen05 cta_group::2, M=256, N=128, K=16): the even CTA
+// issues, A rows come from both CTAs, B columns from both slabs, and each
+// CTA's tensor memory receives its own 128 output rows. Lookups drop from one
+// per MAC-row to one per weight per slab, and shared-memory operand traffic is
+// 96 B/clk/SM instead of the 1-CTA kernel's 128.
+//   warp 0     TMA producer of this CTA's A tiles (6-stage ring); completion
+//              is signalled on the even CTA's barrier.
+//   warp 1     TMEM allocator (512 columns = 4 accumulators of 128) and, in
+//              the even CTA, the MMA issuer.
+//   warps 2-9  slab expanders when the N tile changes, epilogue otherwise
+//              (two warps per TMEM lane quadrant, 64 columns each).
+// ============================================================================
+constexpr int WS_BM = 128, WS_BN = 64, WS_BK = 64, WS_KMAX = 1024;
+constexpr int WS_STAGES = 6;
+constexpr int WS_A_STAGE = WS_BM * WS_BK * 2;         // 16 KB
+constexpr int WS_SLAB_KB = WS_BN * WS_BK * 2;         // 8 KB per k-block
+constexpr int WS_OFF_SLAB = 0;
+constexpr int WS_OFF_A = (WS_KMAX / WS_BK) * WS_SLAB_KB;  // 128 KB
+constexpr int WS_OFF_PAL = WS_OFF_A;  // palette staging overlays the drained A ring
+constexpr int WS_NUM_ACC = 4, WS_ACC_COLS = 128;
+constexpr int WS_OFF_BAR = WS_OFF_A + WS_STAGES * WS_A_STAGE;
+constexpr int WS_NUM_BARS = 2 * WS_STAGES + 2 * WS_NUM_ACC + 4;
+constexpr int WS_OFF_MISC = WS_OFF_BAR + WS_NUM_BARS * 8;
+constexpr int WS_SMEM_BYTES = WS_OFF_MISC + 16 + 1024;
+constexpr int WS_THREADS = 320;
+constexpr int WS_NUM_EXP = 256;  // warps 2-9
+constexpr uint32_t WS_TMEM_COLS = 512;
+constexpr uint32_t WS_IDESC = umma_idesc_f16(2 * WS_BM, 2 * WS_BN);
+static_assert(WS_SMEM_BYTES <= 232448, "shared memory budget");
+static_assert(WS_BN * 128 * 4 <= WS_STAGES * WS_A_STAGE, "palette staging fits the A ring");
+
+struct WsArgs {
+  GemmArgs g;
+  const uint8_t* idx;
+  int kblocks;
+  int m_tiles;  // 256-row pair tiles
+  int units;    // (n / 128) * m_tiles
+};
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(WS_THREADS, 1)
+    gemm_ws_kernel(const __grid_constant__ CUtensorMap tmap_a, const WsArgs wa) {
+  const GemmArgs& args = wa.g;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  const uint32_t sbase = smem_u32(smem);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+
+  const uint32_t bar_a_full = sbase + WS_OFF_BAR;
+  const uint32_t bar_a_empty = bar_a_full + 8 * WS_STAGES;
+  const uint32_t bar_tfull = bar_a_empty + 8 * WS_STAGES;
+  const uint32_t bar_tempty = bar_tfull + 8 * WS_NUM_ACC;
+  const uint32_t bar_slab_full = bar_tempty + 8 * WS_NUM_ACC;  // even CTA's copy used
+  const uint32_t bar_slab_local = bar_slab_full + 8;
+  const uint32_t bar_exp_sync = bar_slab_local + 8;
+  const uint32_t bar_drain = bar_exp_sync + 8;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + WS_OFF_MISC);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + WS_OFF_MISC + 4);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < WS_STAGES; ++s) {
+      mbar_init(bar_a_full + 8 * s, 1);
+      mbar_init(bar_a_empty + 8 * s, 1);
+    }
+    for (int a = 0; a < WS_NUM_ACC; ++a) {
+      mbar_init(bar_tfull + 8 * a, 1);
+      mbar_init(bar_tempty + 8 * a, 2 * WS_NUM_EXP);
+    }
+    mbar_init(bar_slab_full, 2 * WS_NUM_EXP);
+    mbar_init(bar_slab_local, WS_NUM_EXP);
+    mbar_init(bar_exp_sync, WS_NUM_EXP);
+    mbar_init(bar_drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    prefetch_tmap(&tmap_a);
+  }
+  if (warp == 1) {
+    tmem_alloc_cg2(smem_u32(tmem_slot), WS_TMEM_COLS);
+    tmem_relinquish_cg2();
+  }
+  tc_fence_before();
+  __syncthreads();
+  __syncwarp();
+  cluster_sync_all();  // both CTAs' barriers initialised before any remote arrive
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+  const int u_begin = (int)((long long)pair * wa.units / npairs);
+  const int u_end = (int)((long long)(pair + 1) * wa.units / npairs);
+  const int kblocks = wa.kblocks;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------- producer
+    if (lane == 0) {
+      const uint64_t policy = l2_policy_evict_last();
+      int s = 0;
+      uint32_t ph = 0, gen = 0;
+      int cur_n = -1;
+      bool ok = true;
+      for (int u = u_begin; u < u_end && ok; ++u) {
+        const int n_tile = u / wa.m_tiles, m_tile = u % wa.m_tiles;
+        if (n_tile != cur_n) {
+          // the slab (and the palette staged over this ring) must be done first
+          ok = mbar_wait(bar_slab_local, gen & 1u, abort_flag, args.err, kDevErrTimeoutProducer);
+          if (!ok) break;
+          ++gen;
+          cur_n = n_tile;
+        }
+        const int row = m_tile * 2 * WS_BM + (int)rank * WS_BM;
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait_cluster(bar_a_empty + 8 * s, ph ^ 1, abort_flag, args.err,
+                                 kDevErrTimeoutProducer)) {
+            ok = false;
+            break;
+          }
+          if (leader) mbar_arrive_expect_tx(bar_a_full + 8 * s, 2 * WS_A_STAGE);
+          tma_load_2d_cg2(sbase + WS_OFF_A + s * WS_A_STAGE, &tmap_a,
+                          mapa_shared(bar_a_full + 8 * s, 0), kb * WS_BK, row, policy);
+          if (++s == WS_STAGES) {
+            s = 0;
+            ph ^= 1;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------- MMA issuer (even CTA)
+    if (leader && lane == 0) {
+      int s = 0, it = 0;
+      uint32_t ph = 0, gen = 0;
+      int cur_n = -1;
+      bool issued_any = false, ok = true;
+      for (int u = u_begin; u < u_end && ok; ++u, ++it) {
+        const int n_tile = u / wa.m_tiles;
+        if (n_tile != cur_n) {
+          ok = mbar_wait_cluster(bar_slab_full, gen & 1u, abort_flag, args.err, kDevErrTimeoutMma);
+          if (!ok) break;
+          ++gen;
+          cur_n = n_tile;
+        }
+        const int acc = it % WS_NUM_ACC;
+        const uint32_t use = (uint32_t)(it / WS_NUM_ACC) & 1u;
+        if (!mbar_wait_cluster(bar_tempty + 8 * acc, use ^ 1, abort_flag, args.err,
+                               kDevErrTimeoutMma))
+          break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem + (uint32_t)(acc * WS_ACC_COLS);
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait_cluster(bar_a_full + 8 * s, ph, abort_flag, args.err, kDevErrTimeoutMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = sbase + WS_OFF_A + s * WS_A_STAGE;
+          const uint32_t b_addr = sbase + WS_OFF_SLAB + kb * WS_SLAB_KB;
+#pragma unroll
+          for (int kk = 0; kk < WS_BK / 16; ++kk)
+            umma_f16_ss_cg2(d_tmem, umma_desc_sw128(a_addr + kk * 32),
+                            umma_desc_sw128(b_addr + kk * 32), WS_IDESC, (kb | kk) != 0);
+          umma_commit_cg2_mc(bar_a_empty + 8 * s, 0x3);
+          issued_any = true;
+          if (++s == WS_STAGES) {
+            s = 0;
+            ph ^= 1;
+          }
+        }
+        if (!ok) break;
+        umma_commit_cg2_mc(bar_tfull + 8 * acc, 0x3);
+      }
+      if (*abort_flag && issued_any) {
+        umma_commit_cg2(bar_drain);
+        mbar_wait_cluster_drain(bar_drain, 0);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------- expanders + epilogue
+    const int ew = warp - 2;                     // 0..7
+    const int exp_row = lane + 32 * (ew & 1);    // slab row 0..63
+    const int exp_q = ew >> 1;                   // k quarter 0..3
+    const int quad = warp & 3;                   // TMEM lane quadrant of this warp
+    const int colhalf = ew >> 2;                 // accumulator columns [64*colhalf, +64)
+    uint32_t sync_ph = 0;
+    int cur_n = -1, it = 0;
+    bool ok = true;
+    for (int u = u_begin; u < u_end && ok; ++u, ++it) {
+      const int n_tile = u / wa.m_tiles, m_tile = u % wa.m_tiles;
+      if (n_tile != cur_n) {
+        // ---- expand this CTA's 64 x K slab of weight rows (all earlier MMAs
+        // are complete: their accumulators were drained by this loop).
+        const int wrow = n_tile * 2 * WS_BN + (int)rank * WS_BN + exp_row;
+        uint32_t* pal = reinterpret_cast<uint32_t*>(smem + WS_OFF_PAL) + exp_row;  // word[e][r] at pal[e*64]
+        {
+          const uint4* prow = reinterpret_cast<const uint4*>(args.palette + (size_t)wrow * 256);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {  // entries [exp_q*32 + 8j, +8) and +128
+            const uint4 lo = __ldg(prow + exp_q * 4 + j), hi = __ldg(prow + 16 + exp_q * 4 + j);
+            const uint32_t l[4] = {lo.x, lo.y, lo.z, lo.w}, h[4] = {hi.x, hi.y, hi.z, hi.w};
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              const int e = exp_q * 32 + 8 * j + 2 * q;
+              pal[e * 64] = __byte_perm(l[q], h[q], 0x5410u);
+              pal[(e + 1) * 64] = __byte_perm(l[q], h[q], 0x7632u);
+            }
+          }
+        }
+        mbar_arrive(bar_exp_sync);
+        ok = __all_sync(0xffffffffu, mbar_wait(bar_exp_sync, sync_ph, abort_flag, args.err,
+                                               kDevErrTimeoutDequant));
+        sync_ph ^= 1;
+        if (!ok) break;
+        const int kq = args.k / 4;
+        const uint8_t* irow = wa.idx + (size_t)wrow * args.k;
+        const int sw = exp_row & 7;
+        for (int k = exp_q * kq; k < (exp_q + 1) * kq; k += 16) {
+          const uint4 v = __ldg(reinterpret_cast<const uint4*>(irow + k));
+          uint32_t o[8];
+          // word[e][r] at pal[e*64]: the same expansion as expand16 with a
+          // 64-row stride
+          const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const uint32_t uu = w4[q];
+            const uint32_t p0 = pal[(uu & 0x7Fu) << 6];
+            const uint32_t p1 = pal[((uu >> 8) & 0x7Fu) << 6];
+            const uint32_t p2 = pal[((uu >> 16) & 0x7Fu) << 6];
+            const uint32_t p3 = pal[((uu >> 24) & 0x7Fu) << 6];
+            const uint32_t t = (uu >> 6) & 0x02020202u;
+            o[2 * q] = __byte_perm(p0, p1, 0x5410u | ((t & 0x0202u) * 0x11u));
+            o[2 * q + 1] = __byte_perm(p2, p3, 0x5410u | (((t >> 16) & 0x0202u) * 0x11u));
+          }
+          const int kb = k >> 6, c = (k & 63) >> 3;
+          uint8_t* dst = smem + WS_OFF_SLAB + kb * WS_SLAB_KB + exp_row * 128;
+          *reinterpret_cast<uint4*>(dst + ((c ^ sw) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
+          *reinterpret_cast<uint4*>(dst + (((c + 1) ^ sw) << 4)) = make_uint4(o[4], o[5], o[6], o[7]);
+        }
+        fence_proxy_async_smem();
+        mbar_arrive(bar_slab_local);
+        mbar_arrive_cluster(mapa_shared(bar_slab_full, 0));
+        cur_n = n_tile;
+      }
+      // ---- epilogue of unit u
+      const int acc = it % WS_NUM_ACC;
+      const uint32_t use = (uint32_t)(it / WS_NUM_ACC) & 1u;
+      ok = __all_sync(0xffffffffu, mbar_wait_cluster(bar_tfull + 8 * acc, use, abort_flag,
+                                                     args.err, kDevErrTimeoutEpilogue));
+      if (!ok) break;
+      tc_fence_after();
+      const int row = m_tile * 2 * WS_BM + (int)rank * WS_BM + quad * 32 + lane;
+      const uint32_t taddr = tmem + ((uint32_t)(quad * 32) << 16) +
+                             (uint32_t)(acc * WS_ACC_COLS + colhalf * 64);
+#pragma unroll 1
+      for (int c = 0; c < 2; ++c) {
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(taddr + (uint32_t)(c * 32), v);
+        tmem_wait_ld();
+        epilogue_chunk(args, row, n_tile * 2 * WS_BN + colhalf * 64 + c * 32, v);
+      }
+      tc_fence_before();
+      mbar_arrive_cluster(mapa_shared(bar_tempty + 8 * acc, 0));
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  __syncwarp();
+  cluster_sync_all();  // no CTA leaves while its pair may still touch its memory
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_cg2(tmem, WS_TMEM_COLS);
+  }
+}
+
 // Stand-alone LUT expansion, the bit-exact check of the in-GEMM expansion and
 // the B200 form of dequantize_int8_optimized (Metal/Dequantize.metal:71-93):
 // 8 weight rows per CTA, their palettes staged in shared memory, 16-byte
@@ -416,6 +695,20 @@ sam3_status_t make_map_2d(sam3_ctx_t* ctx, CUtensorMap* map, CUtensorMapDataType
   if (r != CUDA_SUCCESS)
     return set_error(ctx, SAM3_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
   return SAM3_OK;
+}
+
+sam3_status_t launch_ws(sam3_ctx_t* ctx, const CUtensorMap& ma, const WsArgs& wa) {
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaError_t e = cudaFuncSetAttribute(gemm_ws_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         WS_SMEM_BYTES);
+    if (e != cudaSuccess) return check_cuda(ctx, e, "gemm_ws smem attribute");
+    attr_set = true;
+  }
+  const int max_pairs = ctx->num_sms / 2;
+  const int pairs = wa.units < max_pairs ? wa.units : max_pairs;
+  gemm_ws_kernel<<<2 * pairs, WS_THREADS, WS_SMEM_BYTES, ctx->stream>>>(ma, wa);
+  return check_launch(ctx, "gemm_ws_kernel");
 }
 
 template <int MODE>
@@ -472,9 +765,6 @@ sam3_status_t gemm_palette(sam3_ctx_t* ctx, const uint16_t* x, int m, int k, con
   if ((st = make_map_2d(ctx, &ma, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, x, (uint64_t)k, (uint64_t)m,
                         BK, BM, CU_TENSOR_MAP_SWIZZLE_128B)) != SAM3_OK)
     return st;
-  if ((st = make_map_2d(ctx, &mb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, idx, (uint64_t)k, (uint64_t)n,
-                        BK, BN, CU_TENSOR_MAP_SWIZZLE_64B)) != SAM3_OK)
-    return st;
   GemmArgs a;
   a.bias = reinterpret_cast<const __half*>(bias);
   a.residual = reinterpret_cast<const __half*>(residual);
@@ -493,6 +783,19 @@ sam3_status_t gemm_palette(sam3_ctx_t* ctx, const uint16_t* x, int m, int k, con
   const double bytes = 2.0 * m * k + 1.0 * n * k + 512.0 * n + 2.0 * m * n *
                        (epi == SAM3_EPI_BIAS_RESIDUAL ? 2 : 1);
   ProfScope prof(ctx, SAM3_PROF_GEMM, 2.0 * m * n * k, bytes);
+  if (k <= WS_KMAX) {
+    // weight-stationary pair kernel: the A map's box is 64 x 128 as above
+    WsArgs wa;
+    wa.g = a;
+    wa.idx = idx;
+    wa.kblocks = k / WS_BK;
+    wa.m_tiles = (m + 2 * WS_BM - 1) / (2 * WS_BM);
+    wa.units = wa.m_tiles * (n / (2 * WS_BN));
+    return launch_ws(ctx, ma, wa);
+  }
+  if ((st = make_map_2d(ctx, &mb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, idx, (uint64_t)k, (uint64_t)n,
+                        BK, BN, CU_TENSOR_MAP_SWIZZLE_64B)) != SAM3_OK)
+    return st;
   return launch<kPalette>(ctx, ma, mb, a);
 }
 
