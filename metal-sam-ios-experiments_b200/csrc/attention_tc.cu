@@ -14,10 +14,11 @@
 //              S = Q K^T   (M=128, N=128, K=64, both operands K-major)
 //              O = P V     (M=128, N=64,  K=128, P read from tensor memory,
 //                           V as an MN-major operand)
-//   warps 2-5  one thread per query row (its TMEM lane): row max over the
-//            valid keys, p = 2^(s*scale*log2e - m) rounded to fp16 and written
-//            back over S in tensor memory, running sum, and the rescaled
-//            fp32 output accumulator kept in registers.
+//   warps 2-5  one thread per query row (its TMEM lane): the row's scores
+//            read once, row max over the valid keys, p = 2^(s*scale*log2e - m)
+//            rounded to fp16 and written back over S in tensor memory, fp32
+//            running sum; O accumulates in tensor memory and is rescaled in
+//            place only when the running max grows by more than 8 (log2).
 // Tensor memory (256 columns): S / P at columns [0,128), O at [128,192).
 #include "common.cuh"
 #include "internal.h"
@@ -145,16 +146,14 @@ __global__ void __launch_bounds__(THREADS, 2)
                         umma_desc_sw128(k_addr + kk * 32), IDESC_S, kk != 0);
           umma_commit(bar_s_full);
           issued_any = true;
-          // O = P V once the softmax wrote P and read the previous O.
-          if (!mbar_wait(bar_p_full, (uint32_t)j & 1u, abort_flag, args.err, kDevErrTimeoutAttn) ||
-              !mbar_wait(bar_o_free, ((uint32_t)j & 1u) ^ 1u, abort_flag, args.err,
-                         kDevErrTimeoutAttn))
+          // O += P V once the softmax wrote P (and rescaled O if needed).
+          if (!mbar_wait(bar_p_full, (uint32_t)j & 1u, abort_flag, args.err, kDevErrTimeoutAttn))
             break;
           tc_fence_after();
 #pragma unroll
           for (int kk = 0; kk < BKV / 16; ++kk)
             umma_f16_ts(tmem + COL_O, tmem + COL_S + kk * 8,
-                        umma_desc_sw128_mn(v_addr + kk * 2048), IDESC_O, kk != 0);
+                        umma_desc_sw128_mn(v_addr + kk * 2048), IDESC_O, (j | kk) != 0);
           umma_commit(bar_o_full);
           umma_commit(bar_kv_empty + 8 * s);
         }
@@ -166,108 +165,101 @@ __global__ void __launch_bounds__(THREADS, 2)
     }
   } else {
     // ------------------------------------------------------------- softmax rows
+    // One thread per query row (its TMEM lane). The row's 128 scores are read
+    // from tensor memory once; O accumulates in tensor memory across tiles (the
+    // PV MMA accumulates) and is rescaled in place only when the running max
+    // grows by more than kRescaleLog2 (so p stays <= 2^8, exact in fp16).
+    constexpr float kRescaleLog2 = 8.0f;
     const int quad = warp & 3;
-    const int r = quad * 32 + lane;  // query row within the tile (TMEM lane)
+    const int r = quad * 32 + lane;
     const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16);
     const float c = args.scale_log2;
     float m_run = -INFINITY, l_run = 0.f;
-    float acc[HD];
-#pragma unroll
-    for (int d = 0; d < HD; ++d) acc[d] = 0.f;
     bool ok = true;
     for (int j = 0; j < ntiles && ok; ++j) {
       ok = __all_sync(0xffffffffu, mbar_wait(bar_s_full, (uint32_t)j & 1u, abort_flag, args.err,
                                              kDevErrTimeoutAttn));
       if (!ok) break;
       tc_fence_after();
-      const int valid = min(BKV, seq - j * BKV);  // keys of this tile inside the image
-      const bool full = valid == BKV;               // only the last tile can be ragged
-      // pass 1: row max of the valid scores
-      float mx = -INFINITY;
-#pragma unroll 1
-      for (int cc = 0; cc < BKV / 32; ++cc) {
-        uint32_t v[32];
-        tmem_ld_32x32b_x32(lane_base + COL_S + cc * 32, v);
-        tmem_wait_ld();
-        if (full) {
+      uint32_t v[BKV];
 #pragma unroll
-          for (int e = 0; e < 32; e += 2)
-            mx = fmaxf(mx, fmaxf(__uint_as_float(v[e]), __uint_as_float(v[e + 1])));
-        } else {
+      for (int cc = 0; cc < BKV / 32; ++cc)
+        tmem_ld_32x32b_x32(lane_base + COL_S + cc * 32, *reinterpret_cast<uint32_t(*)[32]>(v + cc * 32));
+      tmem_wait_ld();
+      const int valid = min(BKV, seq - j * BKV);  // only the last tile can be ragged
+      if (valid < BKV) {
 #pragma unroll
-          for (int e = 0; e < 32; ++e)
-            if (cc * 32 + e < valid) mx = fmaxf(mx, __uint_as_float(v[e]));
-        }
+        for (int e = 0; e < BKV; ++e)
+          if (e >= valid) v[e] = __float_as_uint(-INFINITY);
       }
-      const float m_new = fmaxf(m_run, mx * c);
-      const float alpha = ex2_approx(m_run - m_new);  // 0 on the first tile
-      // pass 2: p = 2^(s c - m), fp16 pairs over the S columns, running sum
+      float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+      for (int e = 0; e < BKV; e += 2) {
+        mx0 = fmaxf(mx0, __uint_as_float(v[e]));
+        mx1 = fmaxf(mx1, __uint_as_float(v[e + 1]));
+      }
+      const float m_tile = fmaxf(mx0, mx1) * c;
+      // keep the running max unless it grows by more than the threshold
+      const bool grow = m_tile > m_run + kRescaleLog2;
+      const float m_use = grow ? m_tile : m_run;
+      const float alpha = grow ? ex2_approx(m_run - m_use) : 1.0f;  // 0 on the first tile
       float rs0 = 0.f, rs1 = 0.f;
-#pragma unroll 1
+#pragma unroll
       for (int cc = 0; cc < BKV / 32; ++cc) {
-        uint32_t v[32];
-        tmem_ld_32x32b_x32(lane_base + COL_S + cc * 32, v);
-        tmem_wait_ld();
         uint32_t pk[16];
-        if (full) {
 #pragma unroll
-          for (int e = 0; e < 16; ++e) {
-            const float p0 = ex2_approx(fmaf(__uint_as_float(v[2 * e]), c, -m_new));
-            const float p1 = ex2_approx(fmaf(__uint_as_float(v[2 * e + 1]), c, -m_new));
-            rs0 += p0;
-            rs1 += p1;
-            pk[e] = pack_half2(p0, p1);
-          }
-        } else {
-#pragma unroll
-          for (int e = 0; e < 16; ++e) {
-            const int k0 = cc * 32 + 2 * e;
-            const float p0 =
-                k0 < valid ? ex2_approx(fmaf(__uint_as_float(v[2 * e]), c, -m_new)) : 0.f;
-            const float p1 =
-                k0 + 1 < valid ? ex2_approx(fmaf(__uint_as_float(v[2 * e + 1]), c, -m_new)) : 0.f;
-            rs0 += p0;
-            rs1 += p1;
-            pk[e] = pack_half2(p0, p1);
-          }
+        for (int e = 0; e < 16; ++e) {
+          const float p0 = ex2_approx(fmaf(__uint_as_float(v[cc * 32 + 2 * e]), c, -m_use));
+          const float p1 = ex2_approx(fmaf(__uint_as_float(v[cc * 32 + 2 * e + 1]), c, -m_use));
+          rs0 += p0;
+          rs1 += p1;
+          pk[e] = pack_half2(p0, p1);
         }
         tmem_st_32x32b_x16(lane_base + COL_S + cc * 16, pk);
       }
-      const float rs = rs0 + rs1;
-      tmem_wait_st();
-      m_run = m_new;
-      l_run = l_run * alpha + rs;
-      tc_fence_before();
-      mbar_arrive(bar_p_full);
-      // O_j = P_j V_j: fold into the register accumulator
-      ok = __all_sync(0xffffffffu, mbar_wait(bar_o_full, (uint32_t)j & 1u, abort_flag, args.err,
-                                             kDevErrTimeoutAttn));
-      if (!ok) break;
-      tc_fence_after();
-#pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        uint32_t v[32];
-        tmem_ld_32x32b_x32(lane_base + COL_O + half * 32, v);
+      l_run = l_run * alpha + (rs0 + rs1);
+      m_run = m_use;
+      if (grow && j > 0) {
+        // O holds the previous tiles' sum (their PV finished before this tile's
+        // S was computed); rescale this row in place before PV of tile j adds.
+        uint32_t o[HD];
+        tmem_ld_32x32b_x32(lane_base + COL_O, *reinterpret_cast<uint32_t(*)[32]>(o));
+        tmem_ld_32x32b_x32(lane_base + COL_O + 32, *reinterpret_cast<uint32_t(*)[32]>(o + 32));
         tmem_wait_ld();
 #pragma unroll
-        for (int e = 0; e < 32; ++e) acc[half * 32 + e] = fmaf(acc[half * 32 + e], alpha, __uint_as_float(v[e]));
+        for (int d = 0; d < HD; ++d) o[d] = __float_as_uint(__uint_as_float(o[d]) * alpha);
+        tmem_st_32x32b_x16(lane_base + COL_O, *reinterpret_cast<uint32_t(*)[16]>(o));
+        tmem_st_32x32b_x16(lane_base + COL_O + 16, *reinterpret_cast<uint32_t(*)[16]>(o + 16));
+        tmem_st_32x32b_x16(lane_base + COL_O + 32, *reinterpret_cast<uint32_t(*)[16]>(o + 32));
+        tmem_st_32x32b_x16(lane_base + COL_O + 48, *reinterpret_cast<uint32_t(*)[16]>(o + 48));
       }
+      tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(bar_o_free);
+      mbar_arrive(bar_p_full);
     }
     if (ok) {
+      // final O = sum over tiles, after the last PV
+      ok = __all_sync(0xffffffffu, mbar_wait(bar_o_full, (uint32_t)(ntiles - 1) & 1u, abort_flag,
+                                             args.err, kDevErrTimeoutAttn));
+    }
+    if (ok) {
+      tc_fence_after();
+      uint32_t o[HD];
+      tmem_ld_32x32b_x32(lane_base + COL_O, *reinterpret_cast<uint32_t(*)[32]>(o));
+      tmem_ld_32x32b_x32(lane_base + COL_O + 32, *reinterpret_cast<uint32_t(*)[32]>(o + 32));
+      tmem_wait_ld();
       const int q = q0 + r;
       if (q < seq) {
         const float inv = 1.f / l_run;
         uint4* dst = reinterpret_cast<uint4*>(args.out + (size_t)(row0 + q) * dim + h * HD);
 #pragma unroll
         for (int c8 = 0; c8 < HD / 8; ++c8) {
-          uint4 o;
-          o.x = pack_half2(acc[8 * c8 + 0] * inv, acc[8 * c8 + 1] * inv);
-          o.y = pack_half2(acc[8 * c8 + 2] * inv, acc[8 * c8 + 3] * inv);
-          o.z = pack_half2(acc[8 * c8 + 4] * inv, acc[8 * c8 + 5] * inv);
-          o.w = pack_half2(acc[8 * c8 + 6] * inv, acc[8 * c8 + 7] * inv);
-          dst[c8] = o;
+          uint4 w;
+          w.x = pack_half2(__uint_as_float(o[8 * c8 + 0]) * inv, __uint_as_float(o[8 * c8 + 1]) * inv);
+          w.y = pack_half2(__uint_as_float(o[8 * c8 + 2]) * inv, __uint_as_float(o[8 * c8 + 3]) * inv);
+          w.z = pack_half2(__uint_as_float(o[8 * c8 + 4]) * inv, __uint_as_float(o[8 * c8 + 5]) * inv);
+          w.w = pack_half2(__uint_as_float(o[8 * c8 + 6]) * inv, __uint_as_float(o[8 * c8 + 7]) * inv);
+          dst[c8] = w;
         }
       }
     }

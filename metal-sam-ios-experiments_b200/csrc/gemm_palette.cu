@@ -646,6 +646,308 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(WS_THREADS, 1)
   }
 }
 
+// ============================================================================
+// Chunked weight-stationary pair kernel (K > 1024, K % 512 == 0; fc2 with
+// K = 4096): the pair's 128-row slab is expanded one 512-wide K chunk at a
+// time into two alternating 64 KB shared-memory buffers, so the expansion of
+// chunk c+1 overlaps the MMAs on chunk c. Each expanded chunk feeds a group of
+// two 256-row M tiles accumulating in their own TMEM buffers (4 x 128
+// columns: groups alternate between accumulator pairs, so the epilogue of one
+// group overlaps the MMAs of the next). The palette of the CTA's 64 rows stays
+// staged (32 KB) while the N tile is unchanged.
+// ============================================================================
+constexpr int WSC_KC = 512;
+constexpr int WSC_KB_PER_CHUNK = WSC_KC / WS_BK;                    // 8
+constexpr int WSC_BUF = WSC_KB_PER_CHUNK * WS_SLAB_KB;              // 64 KB
+constexpr int WSC_STAGES = 4;
+constexpr int WSC_GROUP = 2;                                        // M tiles per group
+constexpr int WSC_OFF_SLAB = 0;                                     // 2 buffers
+constexpr int WSC_OFF_PAL = 2 * WSC_BUF;                            // 128 KB
+constexpr int WSC_OFF_A = WSC_OFF_PAL + WS_BN * 128 * 4;            // 160 KB
+constexpr int WSC_OFF_BAR = WSC_OFF_A + WSC_STAGES * WS_A_STAGE;    // 224 KB
+constexpr int WSC_NUM_BARS = 2 * WSC_STAGES + 2 + 2 + 2 + 2 + 2;
+constexpr int WSC_OFF_MISC = WSC_OFF_BAR + WSC_NUM_BARS * 8;
+constexpr int WSC_SMEM_BYTES = WSC_OFF_MISC + 16 + 1024;
+static_assert(WSC_SMEM_BYTES <= 232448, "shared memory budget");
+
+struct WscArgs {
+  GemmArgs g;
+  const uint8_t* idx;
+  int chunks;   // K / 512
+  int m_tiles;  // 256-row pair tiles
+  int groups;   // ceil(m_tiles / 2)
+  int units;    // (n / 128) * groups
+};
+
+// Expand weight row `exp_row` (0..63) of this CTA, columns [k0, k1), into a
+// slab buffer laid out as 64-row x 128-byte swizzled blocks per 64-wide
+// k-block, k-blocks counted from `kbase`. pal = word[e][r] at pal[e*64].
+__device__ __forceinline__ void ws_expand_range(const uint8_t* irow, const uint32_t* pal,
+                                                uint8_t* buf, int exp_row, int k0, int k1,
+                                                int kbase) {
+  const int sw = exp_row & 7;
+  for (int k = k0; k < k1; k += 16) {
+    const uint4 v = __ldg(reinterpret_cast<const uint4*>(irow + k));
+    const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
+    uint32_t o[8];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const uint32_t uu = w4[q];
+      const uint32_t p0 = pal[(uu & 0x7Fu) << 6];
+      const uint32_t p1 = pal[((uu >> 8) & 0x7Fu) << 6];
+      const uint32_t p2 = pal[((uu >> 16) & 0x7Fu) << 6];
+      const uint32_t p3 = pal[((uu >> 24) & 0x7Fu) << 6];
+      const uint32_t t = (uu >> 6) & 0x02020202u;
+      o[2 * q] = __byte_perm(p0, p1, 0x5410u | ((t & 0x0202u) * 0x11u));
+      o[2 * q + 1] = __byte_perm(p2, p3, 0x5410u | (((t >> 16) & 0x0202u) * 0x11u));
+    }
+    const int kb = (k - kbase) >> 6, c = (k & 63) >> 3;
+    uint8_t* dst = buf + kb * WS_SLAB_KB + exp_row * 128;
+    *reinterpret_cast<uint4*>(dst + ((c ^ sw) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
+    *reinterpret_cast<uint4*>(dst + (((c + 1) ^ sw) << 4)) = make_uint4(o[4], o[5], o[6], o[7]);
+  }
+}
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(WS_THREADS, 1)
+    gemm_wsc_kernel(const __grid_constant__ CUtensorMap tmap_a, const WscArgs wa) {
+  const GemmArgs& args = wa.g;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  const uint32_t sbase = smem_u32(smem);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+
+  const uint32_t bar_a_full = sbase + WSC_OFF_BAR;
+  const uint32_t bar_a_empty = bar_a_full + 8 * WSC_STAGES;
+  const uint32_t bar_slab_full = bar_a_empty + 8 * WSC_STAGES;  // [2], even CTA's copy used
+  const uint32_t bar_slab_empty = bar_slab_full + 16;           // [2], per CTA (multicast)
+  const uint32_t bar_tfull = bar_slab_empty + 16;               // [2] accumulator pairs
+  const uint32_t bar_tempty = bar_tfull + 16;                   // [2], even CTA's copy used
+  const uint32_t bar_pal = bar_tempty + 16;
+  const uint32_t bar_drain = bar_pal + 8;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + WSC_OFF_MISC);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + WSC_OFF_MISC + 4);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < WSC_STAGES; ++s) {
+      mbar_init(bar_a_full + 8 * s, 1);
+      mbar_init(bar_a_empty + 8 * s, 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(bar_slab_full + 8 * b, 2 * WS_NUM_EXP);
+      mbar_init(bar_slab_empty + 8 * b, 1);
+      mbar_init(bar_tfull + 8 * b, 1);
+      mbar_init(bar_tempty + 8 * b, 2 * WS_NUM_EXP);
+    }
+    mbar_init(bar_pal, WS_NUM_EXP);
+    mbar_init(bar_drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    prefetch_tmap(&tmap_a);
+  }
+  if (warp == 1) {
+    tmem_alloc_cg2(smem_u32(tmem_slot), WS_TMEM_COLS);
+    tmem_relinquish_cg2();
+  }
+  tc_fence_before();
+  __syncthreads();
+  __syncwarp();
+  cluster_sync_all();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+  const int u_begin = (int)((long long)pair * wa.units / npairs);
+  const int u_end = (int)((long long)(pair + 1) * wa.units / npairs);
+  const int chunks = wa.chunks;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------- producer
+    if (lane == 0) {
+      const uint64_t policy = l2_policy_evict_last();
+      int s = 0;
+      uint32_t ph = 0;
+      bool ok = true;
+      for (int u = u_begin; u < u_end && ok; ++u) {
+        const int g = u % wa.groups;
+        for (int c = 0; c < chunks && ok; ++c)
+          for (int t = 0; t < WSC_GROUP && ok; ++t) {
+            const int row = (g * WSC_GROUP + t) * 2 * WS_BM + (int)rank * WS_BM;
+            for (int kb = 0; kb < WSC_KB_PER_CHUNK; ++kb) {
+              if (!mbar_wait_cluster(bar_a_empty + 8 * s, ph ^ 1, abort_flag, args.err,
+                                     kDevErrTimeoutProducer)) {
+                ok = false;
+                break;
+              }
+              if (leader) mbar_arrive_expect_tx(bar_a_full + 8 * s, 2 * WS_A_STAGE);
+              tma_load_2d_cg2(sbase + WSC_OFF_A + s * WS_A_STAGE, &tmap_a,
+                              mapa_shared(bar_a_full + 8 * s, 0), c * WSC_KC + kb * WS_BK, row,
+                              policy);
+              if (++s == WSC_STAGES) {
+                s = 0;
+                ph ^= 1;
+              }
+            }
+          }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------- MMA issuer (even CTA)
+    if (leader && lane == 0) {
+      int s = 0, it = 0, q = 0;
+      uint32_t ph = 0;
+      bool issued_any = false, ok = true;
+      for (int u = u_begin; u < u_end && ok; ++u, ++it) {
+        const int gp = it & 1;
+        if (!mbar_wait_cluster(bar_tempty + 8 * gp, ((uint32_t)(it >> 1) & 1u) ^ 1u, abort_flag,
+                               args.err, kDevErrTimeoutMma))
+          break;
+        tc_fence_after();
+        for (int c = 0; c < chunks && ok; ++c, ++q) {
+          const int b = q & 1;
+          if (!mbar_wait_cluster(bar_slab_full + 8 * b, (uint32_t)(q >> 1) & 1u, abort_flag,
+                                 args.err, kDevErrTimeoutMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          for (int t = 0; t < WSC_GROUP && ok; ++t) {
+            const uint32_t d_tmem = tmem + (uint32_t)((2 * gp + t) * WS_ACC_COLS);
+            for (int kb = 0; kb < WSC_KB_PER_CHUNK; ++kb) {
+              if (!mbar_wait_cluster(bar_a_full + 8 * s, ph, abort_flag, args.err,
+                                     kDevErrTimeoutMma)) {
+                ok = false;
+                break;
+              }
+              tc_fence_after();
+              const uint32_t a_addr = sbase + WSC_OFF_A + s * WS_A_STAGE;
+              const uint32_t b_addr = sbase + WSC_OFF_SLAB + b * WSC_BUF + kb * WS_SLAB_KB;
+#pragma unroll
+              for (int kk = 0; kk < WS_BK / 16; ++kk)
+                umma_f16_ss_cg2(d_tmem, umma_desc_sw128(a_addr + kk * 32),
+                                umma_desc_sw128(b_addr + kk * 32), WS_IDESC,
+                                (c | kb | kk) != 0);
+              umma_commit_cg2_mc(bar_a_empty + 8 * s, 0x3);
+              issued_any = true;
+              if (++s == WSC_STAGES) {
+                s = 0;
+                ph ^= 1;
+              }
+            }
+          }
+          if (ok) umma_commit_cg2_mc(bar_slab_empty + 8 * b, 0x3);
+        }
+        if (!ok) break;
+        umma_commit_cg2_mc(bar_tfull + 8 * gp, 0x3);
+      }
+      if (*abort_flag && issued_any) {
+        umma_commit_cg2(bar_drain);
+        mbar_wait_cluster_drain(bar_drain, 0);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------- expanders + epilogue
+    const int ew = warp - 2;
+    const int exp_row = lane + 32 * (ew & 1);
+    const int exp_q = ew >> 1;
+    const int quad = warp & 3;
+    const int colhalf = ew >> 2;
+    uint32_t* pal = reinterpret_cast<uint32_t*>(smem + WSC_OFF_PAL) + exp_row;
+    uint32_t pal_ph = 0;
+    int cur_n = -1, it = 0, q = 0;
+    int pend_it = -1, pend_u = -1;  // group whose epilogue is still to do
+    bool ok = true;
+    auto epilogue = [&](int e_it, int e_u) -> bool {
+      const int gp = e_it & 1;
+      const bool w = __all_sync(0xffffffffu,
+                                mbar_wait_cluster(bar_tfull + 8 * gp, (uint32_t)(e_it >> 1) & 1u,
+                                                  abort_flag, args.err, kDevErrTimeoutEpilogue));
+      if (!w) return false;
+      tc_fence_after();
+      const int n_tile = e_u / wa.groups, g = e_u % wa.groups;
+#pragma unroll 1
+      for (int t = 0; t < WSC_GROUP; ++t) {
+        const int row = (g * WSC_GROUP + t) * 2 * WS_BM + (int)rank * WS_BM + quad * 32 + lane;
+        const uint32_t taddr = tmem + ((uint32_t)(quad * 32) << 16) +
+                               (uint32_t)((2 * gp + t) * WS_ACC_COLS + colhalf * 64);
+#pragma unroll 1
+        for (int cc = 0; cc < 2; ++cc) {
+          uint32_t v[32];
+          tmem_ld_32x32b_x32(taddr + (uint32_t)(cc * 32), v);
+          tmem_wait_ld();
+          epilogue_chunk(args, row, n_tile * 2 * WS_BN + colhalf * 64 + cc * 32, v);
+        }
+      }
+      tc_fence_before();
+      mbar_arrive_cluster(mapa_shared(bar_tempty + 8 * gp, 0));
+      return true;
+    };
+    for (int u = u_begin; u < u_end && ok; ++u, ++it) {
+      const int n_tile = u / wa.groups;
+      const int wrow = n_tile * 2 * WS_BN + (int)rank * WS_BN + exp_row;
+      if (n_tile != cur_n) {
+        if (cur_n >= 0) {  // every expander is done with the old palette
+          mbar_arrive(bar_pal);
+          ok = __all_sync(0xffffffffu, mbar_wait(bar_pal, pal_ph, abort_flag, args.err,
+                                                 kDevErrTimeoutDequant));
+          pal_ph ^= 1;
+          if (!ok) break;
+        }
+        const uint4* prow = reinterpret_cast<const uint4*>(args.palette + (size_t)wrow * 256);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const uint4 lo = __ldg(prow + exp_q * 4 + j), hi = __ldg(prow + 16 + exp_q * 4 + j);
+          const uint32_t l[4] = {lo.x, lo.y, lo.z, lo.w}, h[4] = {hi.x, hi.y, hi.z, hi.w};
+#pragma unroll
+          for (int qq = 0; qq < 4; ++qq) {
+            const int e = exp_q * 32 + 8 * j + 2 * qq;
+            pal[e * 64] = __byte_perm(l[qq], h[qq], 0x5410u);
+            pal[(e + 1) * 64] = __byte_perm(l[qq], h[qq], 0x7632u);
+          }
+        }
+        mbar_arrive(bar_pal);
+        ok = __all_sync(0xffffffffu, mbar_wait(bar_pal, pal_ph, abort_flag, args.err,
+                                               kDevErrTimeoutDequant));
+        pal_ph ^= 1;
+        if (!ok) break;
+        cur_n = n_tile;
+      }
+      const uint8_t* irow = wa.idx + (size_t)wrow * args.k;
+      for (int c = 0; c < chunks && ok; ++c, ++q) {
+        const int b = q & 1;
+        if (q >= 2) {
+          ok = __all_sync(0xffffffffu,
+                          mbar_wait_cluster(bar_slab_empty + 8 * b, (uint32_t)((q >> 1) - 1) & 1u,
+                                            abort_flag, args.err, kDevErrTimeoutDequant));
+          if (!ok) break;
+        }
+        const int k0 = c * WSC_KC + exp_q * (WSC_KC / 4);
+        ws_expand_range(irow, pal, smem + WSC_OFF_SLAB + b * WSC_BUF, exp_row, k0,
+                        k0 + WSC_KC / 4, c * WSC_KC);
+        fence_proxy_async_smem();
+        mbar_arrive_cluster(mapa_shared(bar_slab_full + 8 * b, 0));
+        if (c == 0 && pend_it >= 0) {
+          ok = epilogue(pend_it, pend_u);
+          pend_it = -1;
+        }
+      }
+      pend_it = it;
+      pend_u = u;
+    }
+    if (ok && pend_it >= 0) epilogue(pend_it, pend_u);
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  __syncwarp();
+  cluster_sync_all();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_cg2(tmem, WS_TMEM_COLS);
+  }
+}
+
 // Stand-alone LUT expansion, the bit-exact check of the in-GEMM expansion and
 // the B200 form of dequantize_int8_optimized (Metal/Dequantize.metal:71-93):
 // 8 weight rows per CTA, their palettes staged in shared memory, 16-byte
@@ -709,6 +1011,20 @@ sam3_status_t launch_ws(sam3_ctx_t* ctx, const CUtensorMap& ma, const WsArgs& wa
   const int pairs = wa.units < max_pairs ? wa.units : max_pairs;
   gemm_ws_kernel<<<2 * pairs, WS_THREADS, WS_SMEM_BYTES, ctx->stream>>>(ma, wa);
   return check_launch(ctx, "gemm_ws_kernel");
+}
+
+sam3_status_t launch_wsc(sam3_ctx_t* ctx, const CUtensorMap& ma, const WscArgs& wa) {
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaError_t e = cudaFuncSetAttribute(gemm_wsc_kernel,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, WSC_SMEM_BYTES);
+    if (e != cudaSuccess) return check_cuda(ctx, e, "gemm_wsc smem attribute");
+    attr_set = true;
+  }
+  const int max_pairs = ctx->num_sms / 2;
+  const int pairs = wa.units < max_pairs ? wa.units : max_pairs;
+  gemm_wsc_kernel<<<2 * pairs, WS_THREADS, WSC_SMEM_BYTES, ctx->stream>>>(ma, wa);
+  return check_launch(ctx, "gemm_wsc_kernel");
 }
 
 template <int MODE>
@@ -792,6 +1108,17 @@ sam3_status_t gemm_palette(sam3_ctx_t* ctx, const uint16_t* x, int m, int k, con
     wa.m_tiles = (m + 2 * WS_BM - 1) / (2 * WS_BM);
     wa.units = wa.m_tiles * (n / (2 * WS_BN));
     return launch_ws(ctx, ma, wa);
+  }
+  if (k % WSC_KC == 0) {
+    // chunked weight-stationary pair kernel
+    WscArgs wa;
+    wa.g = a;
+    wa.idx = idx;
+    wa.chunks = k / WSC_KC;
+    wa.m_tiles = (m + 2 * WS_BM - 1) / (2 * WS_BM);
+    wa.groups = (wa.m_tiles + WSC_GROUP - 1) / WSC_GROUP;
+    wa.units = wa.groups * (n / (2 * WS_BN));
+    return launch_wsc(ctx, ma, wa);
   }
   if ((st = make_map_2d(ctx, &mb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, idx, (uint64_t)k, (uint64_t)n,
                         BK, BN, CU_TENSOR_MAP_SWIZZLE_64B)) != SAM3_OK)

@@ -125,6 +125,20 @@ def test_linear_many_tiles_gelu_and_rope(ctx, sam3, oracle):
     assert max_rel_err(y2, ref2) < 2e-3
 
 
+@pytest.mark.parametrize("m,n,k", [(300, 256, 2048), (700, 512, 1536)])
+def test_linear_chunked_k(ctx, sam3, oracle, m, n, k):
+    # K > 1024 takes the chunked weight-stationary kernel; 300 rows leave the
+    # second M tile of the only group entirely out of range
+    x = oracle.gen_normal(16, m, (m, k))
+    idx = oracle.gen_u8(16, 2, (n, k))
+    pal = oracle.gen_palette(16, 3, n)
+    bias = oracle.gen_normal(16, 4, (n,), 0.0, 0.01)
+    res = oracle.gen_normal(16, 5, (m, n))
+    y = run_linear(ctx, sam3, x, idx, pal, bias, sam3.EPI_BIAS_RESIDUAL, residual=res)
+    ref = oracle.linear(x, idx, pal, bias, epilogue=oracle.EPI_BIAS_RESIDUAL, residual=res)
+    assert max_rel_err(y, ref) < 2e-3
+
+
 def test_linear_in_place_residual(ctx, sam3, oracle):
     x = oracle.gen_normal(8, 1, (256, 512))
     idx = oracle.gen_u8(8, 2, (512, 512))
