@@ -6,38 +6,41 @@
 // Reference: scaledDotProductAttention (MPSAttention.swift:165-176, scale
 // 1/sqrt(64), no mask) and AttentionKernels.swift:48-68 (explicit form).
 //
-// One CTA = 128 query rows of one (image, head); two CTAs per SM so one CTA's
-// softmax overlaps the other's MMAs. Warp roles:
-//   warp 0   TMA producer: Q tile once, then K/V tiles of 128 keys through a
-//            2-stage ring (128B-swizzled, straight from the packed rows).
+// One CTA = 128 query rows of one (image, head); two CTAs per SM. Keys come
+// in tiles of 64 and S is double-buffered in tensor memory, so Q K^T of tile
+// j+2 is queued while the softmax works on tile j+1. Warp roles:
+//   warp 0   TMA producer: Q tile once, then K/V tiles of 64 keys through a
+//            4-stage ring (128B-swizzled, straight from the packed rows).
 //   warp 1   TMEM allocator + single-thread MMA issuer:
-//              S = Q K^T   (M=128, N=128, K=64, both operands K-major)
-//              O = P V     (M=128, N=64,  K=128, P read from tensor memory,
+//              S = Q K^T   (M=128, N=64, K=64, both operands K-major)
+//              O += P V    (M=128, N=64, K=64, P read from tensor memory,
 //                           V as an MN-major operand)
 //   warps 2-5  one thread per query row (its TMEM lane): the row's scores
 //            read once, row max over the valid keys, p = 2^(s*scale*log2e - m)
 //            rounded to fp16 and written back over S in tensor memory, fp32
 //            running sum; O accumulates in tensor memory and is rescaled in
 //            place only when the running max grows by more than 8 (log2).
-// Tensor memory (256 columns): S / P at columns [0,128), O at [128,192).
+// Tensor memory (256 columns): S/P buffers at [0,64) and [64,128), O at
+// [128,192).
 #include "common.cuh"
 #include "internal.h"
 
 namespace sam3 {
 namespace {
 
-constexpr int HD = 64, BQ = 128, BKV = 128, STAGES = 2;
+constexpr int HD = 64, BQ = 128, BKV = 64, STAGES = 4;
 constexpr int THREADS = 192;
-constexpr int TILE_BYTES = BQ * HD * 2;  // 16 KB per Q / K / V tile
+constexpr int Q_BYTES = BQ * HD * 2;    // 16 KB
+constexpr int KV_BYTES = BKV * HD * 2;  // 8 KB per K or V tile
 constexpr int OFF_Q = 0;
-constexpr int OFF_K = OFF_Q + TILE_BYTES;
-constexpr int OFF_V = OFF_K + STAGES * TILE_BYTES;
-constexpr int OFF_BAR = OFF_V + STAGES * TILE_BYTES;
-constexpr int NUM_BARS = 1 + 2 * STAGES + 4 + 1;
+constexpr int OFF_K = OFF_Q + Q_BYTES;
+constexpr int OFF_V = OFF_K + STAGES * KV_BYTES;
+constexpr int OFF_BAR = OFF_V + STAGES * KV_BYTES;
+constexpr int NUM_BARS = 1 + 2 * STAGES + 2 + 2 + 1 + 1 + 1;
 constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;
 constexpr int SMEM_BYTES = OFF_MISC + 16 + 1024;
 constexpr uint32_t TMEM_COLS = 256;
-constexpr uint32_t COL_S = 0, COL_O = 128;
+constexpr uint32_t COL_S0 = 0, COL_O = 128;  // S/P buffers at 0 and 64, O at 128
 constexpr uint32_t IDESC_S = umma_idesc_f16(128, BKV, 0);  // K-major B (keys x d)
 constexpr uint32_t IDESC_O = umma_idesc_f16(128, HD, 1);   // MN-major B (keys x d)
 
@@ -63,11 +66,16 @@ __global__ void __launch_bounds__(THREADS, 2)
   const uint32_t bar_q = sbase + OFF_BAR;
   const uint32_t bar_kv_full = bar_q + 8;
   const uint32_t bar_kv_empty = bar_kv_full + 8 * STAGES;
-  const uint32_t bar_s_full = bar_kv_empty + 8 * STAGES;
-  const uint32_t bar_p_full = bar_s_full + 8;
-  const uint32_t bar_o_full = bar_p_full + 8;
-  const uint32_t bar_o_free = bar_o_full + 8;
-  const uint32_t bar_drain = bar_o_free + 8;
+  const uint32_t bar_s_full = bar_kv_empty + 8 * STAGES;  // [2], per S buffer
+  // [2], per S buffer: tile j completes phase j/2 of p_full[j%2]. (A single
+  // barrier could alias: the softmax may finish tiles j and j+1 before the
+  // MMA thread waits for tile j.)
+  const uint32_t bar_p_full = bar_s_full + 16;
+  const uint32_t bar_o_full = bar_p_full + 16;
+  const uint32_t bar_drain = bar_o_full + 8;
+  // Completes once, after the last PV: the read-out of O cannot use a parity
+  // wait on o_full, whose phase may still be two behind at that point.
+  const uint32_t bar_o_done = bar_drain + 8;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + OFF_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + OFF_MISC + 4);
 
@@ -78,10 +86,12 @@ __global__ void __launch_bounds__(THREADS, 2)
       mbar_init(bar_kv_empty + 8 * s, 1);
     }
     mbar_init(bar_s_full, 1);
+    mbar_init(bar_s_full + 8, 1);
     mbar_init(bar_p_full, 128);
+    mbar_init(bar_p_full + 8, 128);
     mbar_init(bar_o_full, 1);
-    mbar_init(bar_o_free, 128);
     mbar_init(bar_drain, 1);
+    mbar_init(bar_o_done, 1);
     *abort_flag = 0;
     fence_mbar_init();
     prefetch_tmap(&tmap_qkv);
@@ -99,63 +109,74 @@ __global__ void __launch_bounds__(THREADS, 2)
     // ------------------------------------------------------------- producer
     if (lane == 0) {
       uint32_t issued = 0, issued_par = 0;
-      bool q_issued = false;
-      mbar_arrive_expect_tx(bar_q, TILE_BYTES);
+      mbar_arrive_expect_tx(bar_q, Q_BYTES);
       tma_load_2d(sbase + OFF_Q, &tmap_qkv, bar_q, h * HD, row0 + q0);
-      q_issued = true;
+      tma_load_2d(sbase + OFF_Q + KV_BYTES, &tmap_qkv, bar_q, h * HD, row0 + q0 + BKV);
       for (int j = 0; j < ntiles; ++j) {
         const int s = j % STAGES;
         const uint32_t ph = (uint32_t)(j / STAGES) & 1u;
         if (!mbar_wait(bar_kv_empty + 8 * s, ph ^ 1, abort_flag, args.err, kDevErrTimeoutAttn))
           break;
-        mbar_arrive_expect_tx(bar_kv_full + 8 * s, 2 * TILE_BYTES);
+        mbar_arrive_expect_tx(bar_kv_full + 8 * s, 2 * KV_BYTES);
         const int r = row0 + j * BKV;
-        tma_load_2d(sbase + OFF_K + s * TILE_BYTES, &tmap_qkv, bar_kv_full + 8 * s, dim + h * HD, r);
-        tma_load_2d(sbase + OFF_V + s * TILE_BYTES, &tmap_qkv, bar_kv_full + 8 * s,
+        tma_load_2d(sbase + OFF_K + s * KV_BYTES, &tmap_qkv, bar_kv_full + 8 * s, dim + h * HD, r);
+        tma_load_2d(sbase + OFF_V + s * KV_BYTES, &tmap_qkv, bar_kv_full + 8 * s,
                     2 * dim + h * HD, r);
         issued |= 1u << s;
         issued_par = (issued_par & ~(1u << s)) | (ph << s);
       }
       if (*abort_flag) {
-        if (q_issued) mbar_wait_drain(bar_q, 0);
+        mbar_wait_drain(bar_q, 0);
         for (int s = 0; s < STAGES; ++s)
           if (issued & (1u << s)) mbar_wait_drain(bar_kv_full + 8 * s, (issued_par >> s) & 1u);
       }
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------- MMA issuer
+    // Order: S0 = Q K0^T, S1 = Q K1^T, then per tile j: O += P_j V_j and,
+    // once that PV has read P_j, S_(j%2) = Q K_(j+2)^T.
     if (lane == 0) {
-      bool issued_any = false;
-      if (mbar_wait(bar_q, 0, abort_flag, args.err, kDevErrTimeoutAttn)) {
-        const uint32_t q_addr = sbase + OFF_Q;
-        for (int j = 0; j < ntiles; ++j) {
-          const int s = j % STAGES;
-          const uint32_t ph = (uint32_t)(j / STAGES) & 1u;
-          if (!mbar_wait(bar_kv_full + 8 * s, ph, abort_flag, args.err, kDevErrTimeoutAttn)) break;
-          // S aliases P of the previous tile: let that P V MMA finish reading first.
-          if (j > 0 && !mbar_wait(bar_o_full, (uint32_t)(j - 1) & 1u, abort_flag, args.err,
-                                  kDevErrTimeoutAttn))
-            break;
-          tc_fence_after();
-          const uint32_t k_addr = sbase + OFF_K + s * TILE_BYTES;
-          const uint32_t v_addr = sbase + OFF_V + s * TILE_BYTES;
-          // S = Q K^T
+      bool issued_any = false, ok = true;
+      const uint32_t q_addr = sbase + OFF_Q;
+      auto issue_qk = [&](int j) -> bool {
+        const int s = j % STAGES;
+        if (!mbar_wait(bar_kv_full + 8 * s, (uint32_t)(j / STAGES) & 1u, abort_flag, args.err,
+                       kDevErrTimeoutAttn))
+          return false;
+        tc_fence_after();
+        const uint32_t k_addr = sbase + OFF_K + s * KV_BYTES;
+        const uint32_t d = tmem + COL_S0 + (uint32_t)((j & 1) * BKV);
 #pragma unroll
-          for (int kk = 0; kk < HD / 16; ++kk)
-            umma_f16_ss(tmem + COL_S, umma_desc_sw128(q_addr + kk * 32),
-                        umma_desc_sw128(k_addr + kk * 32), IDESC_S, kk != 0);
-          umma_commit(bar_s_full);
-          issued_any = true;
-          // O += P V once the softmax wrote P (and rescaled O if needed).
-          if (!mbar_wait(bar_p_full, (uint32_t)j & 1u, abort_flag, args.err, kDevErrTimeoutAttn))
-            break;
-          tc_fence_after();
+        for (int kk = 0; kk < HD / 16; ++kk)
+          umma_f16_ss(d, umma_desc_sw128(q_addr + kk * 32), umma_desc_sw128(k_addr + kk * 32),
+                      IDESC_S, kk != 0);
+        umma_commit(bar_s_full + 8 * (j & 1));
+        issued_any = true;
+        return true;
+      };
+      ok = mbar_wait(bar_q, 0, abort_flag, args.err, kDevErrTimeoutAttn);
+      if (ok) ok = issue_qk(0);
+      if (ok && ntiles > 1) ok = issue_qk(1);
+      for (int j = 0; j < ntiles && ok; ++j) {
+        const int s = j % STAGES;
+        if (!mbar_wait(bar_p_full + 8 * (j & 1), (uint32_t)(j >> 1) & 1u, abort_flag, args.err,
+                       kDevErrTimeoutAttn))
+          break;
+        tc_fence_after();
+        const uint32_t v_addr = sbase + OFF_V + s * KV_BYTES;
+        const uint32_t p_col = tmem + COL_S0 + (uint32_t)((j & 1) * BKV);
 #pragma unroll
-          for (int kk = 0; kk < BKV / 16; ++kk)
-            umma_f16_ts(tmem + COL_O, tmem + COL_S + kk * 8,
-                        umma_desc_sw128_mn(v_addr + kk * 2048), IDESC_O, (j | kk) != 0);
-          umma_commit(bar_o_full);
-          umma_commit(bar_kv_empty + 8 * s);
+        for (int kk = 0; kk < BKV / 16; ++kk)
+          umma_f16_ts(tmem + COL_O, p_col + kk * 8, umma_desc_sw128_mn(v_addr + kk * 2048),
+                      IDESC_O, (j | kk) != 0);
+        umma_commit(bar_o_full);
+        umma_commit(bar_kv_empty + 8 * s);
+        if (j == ntiles - 1) umma_commit(bar_o_done);
+        if (j + 2 < ntiles) {
+          // S_(j%2) holds P_j until this PV has read it
+          if (!mbar_wait(bar_o_full, (uint32_t)j & 1u, abort_flag, args.err, kDevErrTimeoutAttn))
+            break;
+          ok = issue_qk(j + 2);
         }
       }
       if (*abort_flag && issued_any) {
@@ -165,10 +186,10 @@ __global__ void __launch_bounds__(THREADS, 2)
     }
   } else {
     // ------------------------------------------------------------- softmax rows
-    // One thread per query row (its TMEM lane). The row's 128 scores are read
-    // from tensor memory once; O accumulates in tensor memory across tiles (the
-    // PV MMA accumulates) and is rescaled in place only when the running max
-    // grows by more than kRescaleLog2 (so p stays <= 2^8, exact in fp16).
+    // One thread per query row (its TMEM lane): the tile's 64 scores are read
+    // once; p = 2^(s*scale*log2e - m) rounded to fp16 overwrites S as P; O
+    // accumulates in tensor memory and is rescaled in place only when the
+    // running max grows by more than kRescaleLog2 (so p <= 2^8, exact in fp16).
     constexpr float kRescaleLog2 = 8.0f;
     const int quad = warp & 3;
     const int r = quad * 32 + lane;
@@ -177,14 +198,14 @@ __global__ void __launch_bounds__(THREADS, 2)
     float m_run = -INFINITY, l_run = 0.f;
     bool ok = true;
     for (int j = 0; j < ntiles && ok; ++j) {
-      ok = __all_sync(0xffffffffu, mbar_wait(bar_s_full, (uint32_t)j & 1u, abort_flag, args.err,
-                                             kDevErrTimeoutAttn));
+      ok = __all_sync(0xffffffffu, mbar_wait(bar_s_full + 8 * (j & 1), (uint32_t)(j >> 1) & 1u,
+                                             abort_flag, args.err, kDevErrTimeoutAttn));
       if (!ok) break;
       tc_fence_after();
+      const uint32_t s_col = lane_base + COL_S0 + (uint32_t)((j & 1) * BKV);
       uint32_t v[BKV];
-#pragma unroll
-      for (int cc = 0; cc < BKV / 32; ++cc)
-        tmem_ld_32x32b_x32(lane_base + COL_S + cc * 32, *reinterpret_cast<uint32_t(*)[32]>(v + cc * 32));
+      tmem_ld_32x32b_x32(s_col, *reinterpret_cast<uint32_t(*)[32]>(v));
+      tmem_ld_32x32b_x32(s_col + 32, *reinterpret_cast<uint32_t(*)[32]>(v + 32));
       tmem_wait_ld();
       const int valid = min(BKV, seq - j * BKV);  // only the last tile can be ragged
       if (valid < BKV) {
@@ -199,7 +220,6 @@ __global__ void __launch_bounds__(THREADS, 2)
         mx1 = fmaxf(mx1, __uint_as_float(v[e + 1]));
       }
       const float m_tile = fmaxf(mx0, mx1) * c;
-      // keep the running max unless it grows by more than the threshold
       const bool grow = m_tile > m_run + kRescaleLog2;
       const float m_use = grow ? m_tile : m_run;
       const float alpha = grow ? ex2_approx(m_run - m_use) : 1.0f;  // 0 on the first tile
@@ -215,33 +235,35 @@ __global__ void __launch_bounds__(THREADS, 2)
           rs1 += p1;
           pk[e] = pack_half2(p0, p1);
         }
-        tmem_st_32x32b_x16(lane_base + COL_S + cc * 16, pk);
+        tmem_st_32x32b_x16(s_col + cc * 16, pk);
       }
       l_run = l_run * alpha + (rs0 + rs1);
       m_run = m_use;
-      if (grow && j > 0) {
-        // O holds the previous tiles' sum (their PV finished before this tile's
-        // S was computed); rescale this row in place before PV of tile j adds.
+      // The rescale uses warp-collective tcgen05.ld/st, so the whole warp takes
+      // the branch when any of its rows grew (alpha is 1 for the others).
+      if (j > 0 && __any_sync(0xffffffffu, grow)) {
+        // wait for the previous tiles' sum, then rescale the rows in place
+        ok = __all_sync(0xffffffffu, mbar_wait(bar_o_full, (uint32_t)(j - 1) & 1u, abort_flag,
+                                               args.err, kDevErrTimeoutAttn));
+        if (!ok) break;
+        tc_fence_after();
         uint32_t o[HD];
         tmem_ld_32x32b_x32(lane_base + COL_O, *reinterpret_cast<uint32_t(*)[32]>(o));
         tmem_ld_32x32b_x32(lane_base + COL_O + 32, *reinterpret_cast<uint32_t(*)[32]>(o + 32));
         tmem_wait_ld();
 #pragma unroll
         for (int d = 0; d < HD; ++d) o[d] = __float_as_uint(__uint_as_float(o[d]) * alpha);
-        tmem_st_32x32b_x16(lane_base + COL_O, *reinterpret_cast<uint32_t(*)[16]>(o));
-        tmem_st_32x32b_x16(lane_base + COL_O + 16, *reinterpret_cast<uint32_t(*)[16]>(o + 16));
-        tmem_st_32x32b_x16(lane_base + COL_O + 32, *reinterpret_cast<uint32_t(*)[16]>(o + 32));
-        tmem_st_32x32b_x16(lane_base + COL_O + 48, *reinterpret_cast<uint32_t(*)[16]>(o + 48));
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          tmem_st_32x32b_x16(lane_base + COL_O + q * 16, *reinterpret_cast<uint32_t(*)[16]>(o + 16 * q));
       }
       tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(bar_p_full);
+      mbar_arrive(bar_p_full + 8 * (j & 1));
     }
-    if (ok) {
-      // final O = sum over tiles, after the last PV
-      ok = __all_sync(0xffffffffu, mbar_wait(bar_o_full, (uint32_t)(ntiles - 1) & 1u, abort_flag,
+    if (ok)
+      ok = __all_sync(0xffffffffu, mbar_wait(bar_o_done, 0u, abort_flag,
                                              args.err, kDevErrTimeoutAttn));
-    }
     if (ok) {
       tc_fence_after();
       uint32_t o[HD];
@@ -281,7 +303,7 @@ sam3_status_t attention_tc(sam3_ctx_t* ctx, const uint16_t* qkv, int batch, int 
   CUtensorMap map;
   cuuint64_t dims[2] = {(cuuint64_t)(3 * dim), (cuuint64_t)batch * seq};
   cuuint64_t strides[1] = {(cuuint64_t)(3 * dim) * 2};
-  cuuint32_t box[2] = {HD, BQ};
+  cuuint32_t box[2] = {HD, BKV};
   cuuint32_t es[2] = {1, 1};
   CUresult r = encode_tiled()(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<uint16_t*>(qkv),
                               dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,

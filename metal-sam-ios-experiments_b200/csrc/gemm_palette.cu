@@ -408,8 +408,26 @@ struct WsArgs {
   const uint8_t* idx;
   int kblocks;
   int m_tiles;  // 256-row pair tiles
-  int units;    // (n / 128) * m_tiles
+  int n_tiles;  // n / 128
+  int units;    // n_tiles * m_tiles
+  int sets;     // > 0: pair p owns N tile p % n_tiles and M tiles p / n_tiles + k * sets;
+                // 0: pair p owns a contiguous range of N-major units
 };
+
+// Unit k of pair `pair` -> (n_tile, m_tile); false when the pair has no unit k.
+__device__ __forceinline__ bool ws_unit(const WsArgs& wa, int pair, int npairs, int k, int& n_tile,
+                                        int& m_tile) {
+  if (wa.sets > 0) {
+    n_tile = pair % wa.n_tiles;
+    m_tile = pair / wa.n_tiles + k * wa.sets;
+    return m_tile < wa.m_tiles;
+  }
+  const int u = (int)((long long)pair * wa.units / npairs) + k;
+  if (u >= (int)((long long)(pair + 1) * wa.units / npairs)) return false;
+  n_tile = u / wa.m_tiles;
+  m_tile = u % wa.m_tiles;
+  return true;
+}
 
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(WS_THREADS, 1)
     gemm_ws_kernel(const __grid_constant__ CUtensorMap tmap_a, const WsArgs wa) {
@@ -439,7 +457,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(WS_THREADS, 1)
     }
     for (int a = 0; a < WS_NUM_ACC; ++a) {
       mbar_init(bar_tfull + 8 * a, 1);
-      mbar_init(bar_tempty + 8 * a, 2 * WS_NUM_EXP);
+      mbar_init(bar_tempty + 8 * a, 2 * WS_NUM_EXP / 32);  // one arrive per epilogue warp
     }
     mbar_init(bar_slab_full, 2 * WS_NUM_EXP);
     mbar_init(bar_slab_local, WS_NUM_EXP);
@@ -461,8 +479,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(WS_THREADS, 1)
   const uint32_t tmem = *tmem_slot;
 
   const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
-  const int u_begin = (int)((long long)pair * wa.units / npairs);
-  const int u_end = (int)((long long)(pair + 1) * wa.units / npairs);
   const int kblocks = wa.kblocks;
 
   if (warp == 0) {
@@ -473,8 +489,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(WS_THREADS, 1)
       uint32_t ph = 0, gen = 0;
       int cur_n = -1;
       bool ok = true;
-      for (int u = u_begin; u < u_end && ok; ++u) {
-        const int n_tile = u / wa.m_tiles, m_tile = u % wa.m_tiles;
+      int n_tile, m_tile;
+      for (int k = 0; ok && ws_unit(wa, pair, npairs, k, n_tile, m_tile); ++k) {
         if (n_tile != cur_n) {
           // the slab (and the palette staged over this ring) must be done first
           ok = mbar_wait(bar_slab_local, gen & 1u, abort_flag, args.err, kDevErrTimeoutProducer);
@@ -506,8 +522,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(WS_THREADS, 1)
       uint32_t ph = 0, gen = 0;
       int cur_n = -1;
       bool issued_any = false, ok = true;
-      for (int u = u_begin; u < u_end && ok; ++u, ++it) {
-        const int n_tile = u / wa.m_tiles;
+      int n_tile, m_tile;
+      for (int k = 0; ok && ws_unit(wa, pair, npairs, k, n_tile, m_tile); ++k, ++it) {
         if (n_tile != cur_n) {
           ok = mbar_wait_cluster(bar_slab_full, gen & 1u, abort_flag, args.err, kDevErrTimeoutMma);
           if (!ok) break;
@@ -558,8 +574,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(WS_THREADS, 1)
     uint32_t sync_ph = 0;
     int cur_n = -1, it = 0;
     bool ok = true;
-    for (int u = u_begin; u < u_end && ok; ++u, ++it) {
-      const int n_tile = u / wa.m_tiles, m_tile = u % wa.m_tiles;
+    int n_tile, m_tile;
+    for (int k = 0; ok && ws_unit(wa, pair, npairs, k, n_tile, m_tile); ++k, ++it) {
       if (n_tile != cur_n) {
         // ---- expand this CTA's 64 x K slab of weight rows (all earlier MMAs
         // are complete: their accumulators were drained by this loop).
@@ -632,7 +648,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(WS_THREADS, 1)
         epilogue_chunk(args, row, n_tile * 2 * WS_BN + colhalf * 64 + c * 32, v);
       }
       tc_fence_before();
-      mbar_arrive_cluster(mapa_shared(bar_tempty + 8 * acc, 0));
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(mapa_shared(bar_tempty + 8 * acc, 0));
     }
   }
 
@@ -653,8 +670,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(WS_THREADS, 1)
 // chunk c+1 overlaps the MMAs on chunk c. Each expanded chunk feeds a group of
 // two 256-row M tiles accumulating in their own TMEM buffers (4 x 128
 // columns: groups alternate between accumulator pairs, so the epilogue of one
-// group overlaps the MMAs of the next). The palette of the CTA's 64 rows stays
-// staged (32 KB) while the N tile is unchanged.
+// group overlaps the MMAs of the next). Each pair keeps one N tile (palette
+// staged once, 32 KB) and the pairs of a "set" sweep the M groups in lockstep.
 // ============================================================================
 constexpr int WSC_KC = 512;
 constexpr int WSC_KB_PER_CHUNK = WSC_KC / WS_BK;                    // 8
@@ -676,7 +693,8 @@ struct WscArgs {
   int chunks;   // K / 512
   int m_tiles;  // 256-row pair tiles
   int groups;   // ceil(m_tiles / 2)
-  int units;    // (n / 128) * groups
+  int n_tiles;  // n / 128
+  int sets;     // pairs / n_tiles
 };
 
 // Expand weight row `exp_row` (0..63) of this CTA, columns [k0, k1), into a
@@ -738,7 +756,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(WS_THREADS, 1)
       mbar_init(bar_slab_full + 8 * b, 2 * WS_NUM_EXP);
       mbar_init(bar_slab_empty + 8 * b, 1);
       mbar_init(bar_tfull + 8 * b, 1);
-      mbar_init(bar_tempty + 8 * b, 2 * WS_NUM_EXP);
+      mbar_init(bar_tempty + 8 * b, 2 * WS_NUM_EXP / 32);  // one arrive per epilogue warp
     }
     mbar_init(bar_pal, WS_NUM_EXP);
     mbar_init(bar_drain, 1);
@@ -757,9 +775,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(WS_THREADS, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
-  const int u_begin = (int)((long long)pair * wa.units / npairs);
-  const int u_end = (int)((long long)(pair + 1) * wa.units / npairs);
+  // Pair p owns N tile p % n_tiles and M groups p / n_tiles + k * sets: the
+  // n_tiles pairs of a set sweep the same A groups together (one DRAM read,
+  // the other N tiles hit L2) and each pair stages its palette once.
+  const int pair = blockIdx.x >> 1;
+  const int my_n = pair % wa.n_tiles, my_set = pair / wa.n_tiles;
   const int chunks = wa.chunks;
 
   if (warp == 0) {
@@ -769,8 +789,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(WS_THREADS, 1)
       int s = 0;
       uint32_t ph = 0;
       bool ok = true;
-      for (int u = u_begin; u < u_end && ok; ++u) {
-        const int g = u % wa.groups;
+      for (int g = my_set; g < wa.groups && ok; g += wa.sets) {
         for (int c = 0; c < chunks && ok; ++c)
           for (int t = 0; t < WSC_GROUP && ok; ++t) {
             const int row = (g * WSC_GROUP + t) * 2 * WS_BM + (int)rank * WS_BM;
@@ -798,7 +817,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(WS_THREADS, 1)
       int s = 0, it = 0, q = 0;
       uint32_t ph = 0;
       bool issued_any = false, ok = true;
-      for (int u = u_begin; u < u_end && ok; ++u, ++it) {
+      for (int g = my_set; g < wa.groups && ok; g += wa.sets, ++it) {
         const int gp = it & 1;
         if (!mbar_wait_cluster(bar_tempty + 8 * gp, ((uint32_t)(it >> 1) & 1u) ^ 1u, abort_flag,
                                args.err, kDevErrTimeoutMma))
@@ -856,16 +875,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(WS_THREADS, 1)
     uint32_t* pal = reinterpret_cast<uint32_t*>(smem + WSC_OFF_PAL) + exp_row;
     uint32_t pal_ph = 0;
     int cur_n = -1, it = 0, q = 0;
-    int pend_it = -1, pend_u = -1;  // group whose epilogue is still to do
+    int pend_it = -1, pend_g = -1;  // group whose epilogue is still to do
     bool ok = true;
-    auto epilogue = [&](int e_it, int e_u) -> bool {
+    auto epilogue = [&](int e_it, int g) -> bool {
       const int gp = e_it & 1;
       const bool w = __all_sync(0xffffffffu,
                                 mbar_wait_cluster(bar_tfull + 8 * gp, (uint32_t)(e_it >> 1) & 1u,
                                                   abort_flag, args.err, kDevErrTimeoutEpilogue));
       if (!w) return false;
       tc_fence_after();
-      const int n_tile = e_u / wa.groups, g = e_u % wa.groups;
+      const int n_tile = my_n;
 #pragma unroll 1
       for (int t = 0; t < WSC_GROUP; ++t) {
         const int row = (g * WSC_GROUP + t) * 2 * WS_BM + (int)rank * WS_BM + quad * 32 + lane;
@@ -880,11 +899,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(WS_THREADS, 1)
         }
       }
       tc_fence_before();
-      mbar_arrive_cluster(mapa_shared(bar_tempty + 8 * gp, 0));
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(mapa_shared(bar_tempty + 8 * gp, 0));
       return true;
     };
-    for (int u = u_begin; u < u_end && ok; ++u, ++it) {
-      const int n_tile = u / wa.groups;
+    for (int g = my_set; g < wa.groups && ok; g += wa.sets, ++it) {
+      const int n_tile = my_n;
       const int wrow = n_tile * 2 * WS_BN + (int)rank * WS_BN + exp_row;
       if (n_tile != cur_n) {
         if (cur_n >= 0) {  // every expander is done with the old palette
@@ -928,14 +948,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(WS_THREADS, 1)
         fence_proxy_async_smem();
         mbar_arrive_cluster(mapa_shared(bar_slab_full + 8 * b, 0));
         if (c == 0 && pend_it >= 0) {
-          ok = epilogue(pend_it, pend_u);
+          ok = epilogue(pend_it, pend_g);
           pend_it = -1;
         }
       }
       pend_it = it;
-      pend_u = u;
+      pend_g = g;
     }
-    if (ok && pend_it >= 0) epilogue(pend_it, pend_u);
+    if (ok && pend_it >= 0) epilogue(pend_it, pend_g);
   }
 
   tc_fence_before();
@@ -1008,7 +1028,8 @@ sam3_status_t launch_ws(sam3_ctx_t* ctx, const CUtensorMap& ma, const WsArgs& wa
     attr_set = true;
   }
   const int max_pairs = ctx->num_sms / 2;
-  const int pairs = wa.units < max_pairs ? wa.units : max_pairs;
+  const int pairs = wa.sets > 0 ? wa.sets * wa.n_tiles
+                                : (wa.units < max_pairs ? wa.units : max_pairs);
   gemm_ws_kernel<<<2 * pairs, WS_THREADS, WS_SMEM_BYTES, ctx->stream>>>(ma, wa);
   return check_launch(ctx, "gemm_ws_kernel");
 }
@@ -1021,8 +1042,7 @@ sam3_status_t launch_wsc(sam3_ctx_t* ctx, const CUtensorMap& ma, const WscArgs& 
     if (e != cudaSuccess) return check_cuda(ctx, e, "gemm_wsc smem attribute");
     attr_set = true;
   }
-  const int max_pairs = ctx->num_sms / 2;
-  const int pairs = wa.units < max_pairs ? wa.units : max_pairs;
+  const int pairs = wa.sets * wa.n_tiles;
   gemm_wsc_kernel<<<2 * pairs, WS_THREADS, WSC_SMEM_BYTES, ctx->stream>>>(ma, wa);
   return check_launch(ctx, "gemm_wsc_kernel");
 }
@@ -1106,10 +1126,19 @@ sam3_status_t gemm_palette(sam3_ctx_t* ctx, const uint16_t* x, int m, int k, con
     wa.idx = idx;
     wa.kblocks = k / WS_BK;
     wa.m_tiles = (m + 2 * WS_BM - 1) / (2 * WS_BM);
-    wa.units = wa.m_tiles * (n / (2 * WS_BN));
+    wa.n_tiles = n / (2 * WS_BN);
+    wa.units = wa.m_tiles * wa.n_tiles;
+    // Fixed N tile per pair when that idles at most 10% of the pairs and
+    // leaves every pair at least two M tiles; contiguous ranges otherwise.
+    const int max_pairs = ctx->num_sms / 2;
+    const int sets = wa.n_tiles <= max_pairs ? max_pairs / wa.n_tiles : 0;
+    wa.sets = (sets > 0 && (max_pairs - sets * wa.n_tiles) * 10 <= max_pairs &&
+               wa.m_tiles >= 2 * sets)
+                  ? sets
+                  : 0;
     return launch_ws(ctx, ma, wa);
   }
-  if (k % WSC_KC == 0) {
+  if (k % WSC_KC == 0 && n / (2 * WS_BN) <= ctx->num_sms / 2) {
     // chunked weight-stationary pair kernel
     WscArgs wa;
     wa.g = a;
@@ -1117,7 +1146,9 @@ sam3_status_t gemm_palette(sam3_ctx_t* ctx, const uint16_t* x, int m, int k, con
     wa.chunks = k / WSC_KC;
     wa.m_tiles = (m + 2 * WS_BM - 1) / (2 * WS_BM);
     wa.groups = (wa.m_tiles + WSC_GROUP - 1) / WSC_GROUP;
-    wa.units = wa.groups * (n / (2 * WS_BN));
+    wa.n_tiles = n / (2 * WS_BN);
+    wa.sets = (ctx->num_sms / 2) / wa.n_tiles;
+    if (wa.sets > wa.groups) wa.sets = wa.groups;
     return launch_wsc(ctx, ma, wa);
   }
   if ((st = make_map_2d(ctx, &mb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, idx, (uint64_t)k, (uint64_t)n,

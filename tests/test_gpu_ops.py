@@ -139,6 +139,55 @@ def test_linear_chunked_k(ctx, sam3, oracle, m, n, k):
     assert max_rel_err(y, ref) < 2e-3
 
 
+@pytest.mark.parametrize("n,k,epi", [(4096, 1024, 1), (3072, 1024, 3), (1024, 1024, 2),
+                                     (1024, 4096, 2)])
+def test_linear_batch8_shapes_deterministic(ctx_full, sam3, oracle, n, k, epi):
+    # The 8-image GEMM shapes of the encoder (both weight-stationary kernels
+    # and their schedules): two runs bit-identical, edge row tiles vs oracle.
+    ctx = ctx_full
+    m = 8 * 5184
+    x = oracle.gen_normal(18, n + k, (m, k))
+    idx = oracle.gen_u8(18, 2, (n, k))
+    pal = oracle.gen_palette(18, 3, n)
+    bias = oracle.gen_normal(18, 4, (n,), 0.0, 0.01)
+    res = oracle.gen_normal(18, 5, (m, n)) if epi == 2 else None
+    table = oracle.rope_table(72, 72) if epi == 3 else None
+    w = upload_linear(ctx, sam3, idx, pal, bias)
+    dx, dy = ctx.upload(x), ctx.alloc(m * n * 2)
+    dres = ctx.upload(res) if res is not None else None
+    drope = ctx.upload(table) if table is not None else None
+    outs = []
+    for _ in range(2):
+        ctx.linear_palette(dx, m, w, epi, dy, dres, drope, 5184)
+        ctx.sync()
+        outs.append(ctx.download(dy, (m, n), F16))
+    assert np.array_equal(outs[0].view(np.uint16), outs[1].view(np.uint16))
+    rows = np.r_[0:256, m // 2:m // 2 + 256, m - 256:m]
+    ref = oracle.linear(x[rows], idx, pal, bias, epilogue=epi,
+                        residual=res[rows] if res is not None else None,
+                        rope=table[rows % 5184] if table is not None else None,
+                        rope_period=len(rows), heads=16, head_dim=64)
+    assert max_rel_err(outs[0][rows], ref) < 2e-3
+
+
+def test_encoder_batch8_deterministic(sam3, oracle):
+    # Two 2-block encoder passes over the same 8 images: bit-identical.
+    with sam3.Context(0, num_blocks=2, prune_after_block=1, max_batch=8) as ctx:
+        blocks = [oracle.SyntheticBlock(43, i) for i in range(2)]
+        pw = oracle.gen_normal(43, 900, (1024, 3, 14, 14), 0.0, 0.02)
+        pb = oracle.gen_normal(43, 901, (1024,), 0.0, 0.02)
+        w = _upload_encoder(ctx, sam3, blocks, pw, pb)
+        img = oracle.gen_uniform(43, 77, (8, 1008, 1008, 3), -1.0, 1.0)
+        res = []
+        for _ in range(2):
+            hf = np.empty((8, 2592, 1024), F16)
+            hi = np.empty((8, 2592), np.int32)
+            ctx.encoder_forward_host(img, 8, w, hf, hi)
+            res.append((hf.view(np.uint16).copy(), hi.copy()))
+        assert np.array_equal(res[0][1], res[1][1])
+        assert np.array_equal(res[0][0], res[1][0])
+
+
 def test_linear_in_place_residual(ctx, sam3, oracle):
     x = oracle.gen_normal(8, 1, (256, 512))
     idx = oracle.gen_u8(8, 2, (512, 512))
@@ -232,6 +281,29 @@ def test_attention_batched_ragged_tiles(ctx, sam3, oracle, batch, seq, heads):
     got = ctx.download(o, (batch * seq, heads * 64), F16)
     ref = oracle.attention(qkv, batch, seq, heads, 64)
     assert max_rel_err(got, ref) < 5e-3
+
+
+def test_attention_batch8_repeated_is_batch_invariant(ctx_full, sam3, oracle):
+    # Eight 72x72-grid images at once, three times in a row (many co-resident
+    # CTAs, the regime where pipeline races would show), each image's rows
+    # bit-identical to a single-image call.
+    ctx = ctx_full
+    batch, seq, heads = 8, 5184, 16
+    qkv = oracle.gen_normal(17, 1, (batch * seq, 3 * heads * 64))
+    dq = ctx.upload(qkv)
+    o = ctx.alloc(batch * seq * heads * 64 * 2)
+    outs = []
+    for _ in range(3):
+        ctx.attention(dq, batch, seq, heads, 64, 0.125, o)
+        ctx.sync()
+        outs.append(ctx.download(o, (batch * seq, heads * 64), F16).view(np.uint16))
+    assert all(np.array_equal(outs[0], x) for x in outs[1:])
+    one = ctx.alloc(seq * heads * 64 * 2)
+    for b in (0, 5):
+        ctx.attention(ctx.upload(qkv[b * seq:(b + 1) * seq]), 1, seq, heads, 64, 0.125, one)
+        ctx.sync()
+        single = ctx.download(one, (seq, heads * 64), F16).view(np.uint16)
+        assert np.array_equal(single, outs[0][b * seq:(b + 1) * seq])
 
 
 def test_attention_full_size_72x72_grid(ctx, sam3, oracle):
