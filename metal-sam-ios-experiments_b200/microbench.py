@@ -56,6 +56,7 @@ def main():
     g.manual_seed(0)
 
     def run(fn):
+        torch.cuda.synchronize()  # inputs are filled on torch's stream, the operator runs on ctx's
         for _ in range(a.warmup):
             fn()
         ctx.sync()

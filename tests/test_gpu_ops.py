@@ -306,6 +306,36 @@ def test_attention_batch8_repeated_is_batch_invariant(ctx_full, sam3, oracle):
         assert np.array_equal(single, outs[0][b * seq:(b + 1) * seq])
 
 
+@pytest.mark.parametrize("seq", [700, 5184])
+def test_attention_growing_scores_rescale_path(ctx, sam3, oracle, seq):
+    # Keys whose scores climb along the sequence (up to ~90 in log2 units), so
+    # the running row max grows past the lazy-rescale threshold many times;
+    # query rows scaled from -1 to 1 mix rows that rescale often, rarely and
+    # never. Three repeats must be bit-identical and match the oracle.
+    heads, batch = 2, 2
+    rng = np.random.default_rng(21)
+    d = heads * 64
+    qkv = np.empty((batch * seq, 3 * d), np.float32)
+    qs = np.linspace(-1.0, 1.0, seq)[:, None]
+    ramp = np.linspace(0.0, 8.0, seq)[:, None]
+    for b in range(batch):
+        rows = slice(b * seq, (b + 1) * seq)
+        qkv[rows, :d] = qs + 0.1 * rng.standard_normal((seq, d))
+        qkv[rows, d:2 * d] = ramp + 0.3 * rng.standard_normal((seq, d))
+        qkv[rows, 2 * d:] = rng.standard_normal((seq, d))
+    qkv = qkv.astype(F16)
+    dq = ctx.upload(qkv)
+    o = ctx.alloc(batch * seq * d * 2)
+    outs = []
+    for _ in range(3):
+        ctx.attention(dq, batch, seq, heads, 64, 0.125, o)
+        ctx.sync()
+        outs.append(ctx.download(o, (batch * seq, d), F16))
+    assert all(np.array_equal(outs[0].view(np.uint16), x.view(np.uint16)) for x in outs[1:])
+    ref = oracle.attention(qkv, batch, seq, heads, 64)
+    assert max_rel_err(outs[0], ref) < 5e-3
+
+
 def test_attention_full_size_72x72_grid(ctx, sam3, oracle):
     seq, heads = 5184, 16
     qkv = oracle.gen_normal(11, 1, (seq, 3 * 1024))
