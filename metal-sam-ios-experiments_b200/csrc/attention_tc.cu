@@ -10,49 +10,81 @@
 // in tiles of 64 and S is double-buffered in tensor memory, so Q K^T of tile
 // j+2 is queued while the softmax works on tile j+1. Warp roles:
 //   warp 0   TMA producer: Q tile once, then K/V tiles of 64 keys through a
-//            4-stage ring (128B-swizzled, straight from the packed rows).
+//            3-stage ring (128B-swizzled, straight from the packed rows).
 //   warp 1   TMEM allocator + single-thread MMA issuer:
-//              S = Q K^T   (M=128, N=64, K=64, both operands K-major)
-//              O += P V    (M=128, N=64, K=64, P read from tensor memory,
-//                           V as an MN-major operand)
+//              S = Q K^T        (M=128, N=64, K=64, both operands K-major)
+//              O += P [V | 1]   (M=128, N=80, K=64, P read from tensor
+//                                memory, V as an MN-major operand followed by
+//                                a constant block of ones)
 //   warps 2-5  one thread per query row (its TMEM lane): the row's scores
-//            read once, row max over the valid keys, p = 2^(s*scale*log2e - m)
-//            rounded to fp16 and written back over S in tensor memory, fp32
-//            running sum; O accumulates in tensor memory and is rescaled in
+//            read once, row max over the valid keys (three-input max),
+//            p = 2^(s*scale*log2e - m) rounded to fp16 and written back over S
+//            in tensor memory. The ones columns make the tensor core keep the
+//            row sums of the fp16 P (O column 64), so the softmax threads add
+//            nothing up and the normaliser has exactly the rounding of the P
+//            that multiplied V. O stays in tensor memory and is rescaled in
 //            place only when the running max grows by more than 8 (log2).
-// Tensor memory (256 columns): S/P buffers at [0,64) and [64,128), O at
-// [128,192).
+// Tensor memory (256 columns): S/P buffers at [0,64) and [64,128), O and the
+// row sums at [128,208).
 #include "common.cuh"
 #include "internal.h"
 
 namespace sam3 {
 namespace {
 
-constexpr int HD = 64, BQ = 128, BKV = 64, STAGES = 4;
+constexpr int HD = 64, BQ = 128, BKV = 64, STAGES = 3;
 constexpr int THREADS = 192;
 constexpr int Q_BYTES = BQ * HD * 2;    // 16 KB
 constexpr int KV_BYTES = BKV * HD * 2;  // 8 KB per K or V tile
 constexpr int OFF_Q = 0;
-constexpr int OFF_K = OFF_Q + Q_BYTES;
-constexpr int OFF_V = OFF_K + STAGES * KV_BYTES;
-constexpr int OFF_BAR = OFF_V + STAGES * KV_BYTES;
+// A K/V stage is 24 KB: the K tile, the V tile (one 3-D TMA request brings
+// both), then an 8 KB block of fp16 ones that the PV MMA reads as 16 extra B
+// columns (the row sums of P land in O column 64).
+constexpr int KV_STAGE = 3 * KV_BYTES;
+constexpr int OFF_KV = OFF_Q + Q_BYTES;
+constexpr int OFF_BAR = OFF_KV + STAGES * KV_STAGE;
 constexpr int NUM_BARS = 1 + 2 * STAGES + 2 + 2 + 1 + 1 + 1;
 constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;
 constexpr int SMEM_BYTES = OFF_MISC + 16 + 1024;
 constexpr uint32_t TMEM_COLS = 256;
 constexpr uint32_t COL_S0 = 0, COL_O = 128;  // S/P buffers at 0 and 64, O at 128
 constexpr uint32_t IDESC_S = umma_idesc_f16(128, BKV, 0);  // K-major B (keys x d)
-constexpr uint32_t IDESC_O = umma_idesc_f16(128, HD, 1);   // MN-major B (keys x d)
+constexpr int OW = HD + 16;                                // O columns: d, then sum(P)
+constexpr uint32_t IDESC_O = umma_idesc_f16(128, OW, 1);   // MN-major B (keys x (d | 1))
 
 struct AttnArgs {
   __half* out;
   int* err;
   int seq, heads, dim;
   float scale_log2;
+  int kv3d;  // 1: tmap_kv is the 3-D K|V map (one request per stage), 0: use 2-D boxes
 };
 
+// B descriptor of the PV MMA: V (MN-major, 128B swizzle) with the ones block
+// one 64-column group further (leading byte offset = one tile, 8 KB).
+__device__ __forceinline__ uint64_t desc_v_ones(uint32_t saddr) {
+  return (umma_desc_sw128_mn(saddr) & ~(0x3FFFull << 16)) |
+         (static_cast<uint64_t>(KV_BYTES >> 4) << 16);
+}
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+__device__ __forceinline__ void tmem_ld_32x32b_x16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr)
+      : "memory");
+}
+
 __global__ void __launch_bounds__(THREADS, 2)
-    attn_tc_kernel(const __grid_constant__ CUtensorMap tmap_qkv, const AttnArgs args) {
+    attn_tc_kernel(const __grid_constant__ CUtensorMap tmap_qkv,
+                   const __grid_constant__ CUtensorMap tmap_kv, const AttnArgs args) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   const uint32_t sbase = smem_u32(smem);
@@ -95,7 +127,14 @@ __global__ void __launch_bounds__(THREADS, 2)
     *abort_flag = 0;
     fence_mbar_init();
     prefetch_tmap(&tmap_qkv);
+    prefetch_tmap(&tmap_kv);
   }
+  for (int i = threadIdx.x; i < STAGES * KV_BYTES / 16; i += THREADS) {  // fp16 1.0 blocks
+    const int st = i / (KV_BYTES / 16), w = i % (KV_BYTES / 16);
+    reinterpret_cast<uint4*>(smem + OFF_KV + st * KV_STAGE + 2 * KV_BYTES)[w] =
+        make_uint4(0x3C003C00u, 0x3C003C00u, 0x3C003C00u, 0x3C003C00u);
+  }
+  fence_proxy_async_smem();
   if (warp == 1) {
     tmem_alloc(smem_u32(tmem_slot), TMEM_COLS);
     tmem_relinquish();
@@ -119,9 +158,13 @@ __global__ void __launch_bounds__(THREADS, 2)
           break;
         mbar_arrive_expect_tx(bar_kv_full + 8 * s, 2 * KV_BYTES);
         const int r = row0 + j * BKV;
-        tma_load_2d(sbase + OFF_K + s * KV_BYTES, &tmap_qkv, bar_kv_full + 8 * s, dim + h * HD, r);
-        tma_load_2d(sbase + OFF_V + s * KV_BYTES, &tmap_qkv, bar_kv_full + 8 * s,
-                    2 * dim + h * HD, r);
+        const uint32_t dst = sbase + OFF_KV + s * KV_STAGE;
+        if (args.kv3d) {
+          tma_load_3d(dst, &tmap_kv, bar_kv_full + 8 * s, h * HD, r, 0);
+        } else {
+          tma_load_2d(dst, &tmap_qkv, bar_kv_full + 8 * s, dim + h * HD, r);
+          tma_load_2d(dst + KV_BYTES, &tmap_qkv, bar_kv_full + 8 * s, 2 * dim + h * HD, r);
+        }
         issued |= 1u << s;
         issued_par = (issued_par & ~(1u << s)) | (ph << s);
       }
@@ -144,7 +187,7 @@ __global__ void __launch_bounds__(THREADS, 2)
                        kDevErrTimeoutAttn))
           return false;
         tc_fence_after();
-        const uint32_t k_addr = sbase + OFF_K + s * KV_BYTES;
+        const uint32_t k_addr = sbase + OFF_KV + s * KV_STAGE;
         const uint32_t d = tmem + COL_S0 + (uint32_t)((j & 1) * BKV);
 #pragma unroll
         for (int kk = 0; kk < HD / 16; ++kk)
@@ -163,11 +206,11 @@ __global__ void __launch_bounds__(THREADS, 2)
                        kDevErrTimeoutAttn))
           break;
         tc_fence_after();
-        const uint32_t v_addr = sbase + OFF_V + s * KV_BYTES;
+        const uint32_t v_addr = sbase + OFF_KV + s * KV_STAGE + KV_BYTES;
         const uint32_t p_col = tmem + COL_S0 + (uint32_t)((j & 1) * BKV);
 #pragma unroll
         for (int kk = 0; kk < BKV / 16; ++kk)
-          umma_f16_ts(tmem + COL_O, p_col + kk * 8, umma_desc_sw128_mn(v_addr + kk * 2048),
+          umma_f16_ts(tmem + COL_O, p_col + kk * 8, desc_v_ones(v_addr + kk * 2048),
                       IDESC_O, (j | kk) != 0);
         umma_commit(bar_o_full);
         umma_commit(bar_kv_empty + 8 * s);
@@ -195,7 +238,7 @@ __global__ void __launch_bounds__(THREADS, 2)
     const int r = quad * 32 + lane;
     const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16);
     const float c = args.scale_log2;
-    float m_run = -INFINITY, l_run = 0.f;
+    float m_run = -INFINITY;
     bool ok = true;
     for (int j = 0; j < ntiles && ok; ++j) {
       ok = __all_sync(0xffffffffu, mbar_wait(bar_s_full + 8 * (j & 1), (uint32_t)(j >> 1) & 1u,
@@ -213,17 +256,16 @@ __global__ void __launch_bounds__(THREADS, 2)
         for (int e = 0; e < BKV; ++e)
           if (e >= valid) v[e] = __float_as_uint(-INFINITY);
       }
-      float mx0 = -INFINITY, mx1 = -INFINITY;
+      float mx0 = __uint_as_float(v[0]), mx1 = __uint_as_float(v[32]);
 #pragma unroll
-      for (int e = 0; e < BKV; e += 2) {
-        mx0 = fmaxf(mx0, __uint_as_float(v[e]));
-        mx1 = fmaxf(mx1, __uint_as_float(v[e + 1]));
+      for (int e = 1; e < 31; e += 2) {
+        mx0 = max3f(mx0, __uint_as_float(v[e]), __uint_as_float(v[e + 1]));
+        mx1 = max3f(mx1, __uint_as_float(v[32 + e]), __uint_as_float(v[32 + e + 1]));
       }
-      const float m_tile = fmaxf(mx0, mx1) * c;
+      const float m_tile = max3f(fmaxf(mx0, __uint_as_float(v[31])), mx1, __uint_as_float(v[63])) * c;
       const bool grow = m_tile > m_run + kRescaleLog2;
       const float m_use = grow ? m_tile : m_run;
       const float alpha = grow ? ex2_approx(m_run - m_use) : 1.0f;  // 0 on the first tile
-      float rs0 = 0.f, rs1 = 0.f;
 #pragma unroll
       for (int cc = 0; cc < BKV / 32; ++cc) {
         uint32_t pk[16];
@@ -231,13 +273,10 @@ __global__ void __launch_bounds__(THREADS, 2)
         for (int e = 0; e < 16; ++e) {
           const float p0 = ex2_approx(fmaf(__uint_as_float(v[cc * 32 + 2 * e]), c, -m_use));
           const float p1 = ex2_approx(fmaf(__uint_as_float(v[cc * 32 + 2 * e + 1]), c, -m_use));
-          rs0 += p0;
-          rs1 += p1;
           pk[e] = pack_half2(p0, p1);
         }
         tmem_st_32x32b_x16(s_col + cc * 16, pk);
       }
-      l_run = l_run * alpha + (rs0 + rs1);
       m_run = m_use;
       // The rescale uses warp-collective tcgen05.ld/st, so the whole warp takes
       // the branch when any of its rows grew (alpha is 1 for the others).
@@ -247,14 +286,15 @@ __global__ void __launch_bounds__(THREADS, 2)
                                                args.err, kDevErrTimeoutAttn));
         if (!ok) break;
         tc_fence_after();
-        uint32_t o[HD];
+        uint32_t o[OW];
         tmem_ld_32x32b_x32(lane_base + COL_O, *reinterpret_cast<uint32_t(*)[32]>(o));
         tmem_ld_32x32b_x32(lane_base + COL_O + 32, *reinterpret_cast<uint32_t(*)[32]>(o + 32));
+        tmem_ld_32x32b_x16(lane_base + COL_O + 64, *reinterpret_cast<uint32_t(*)[16]>(o + 64));
         tmem_wait_ld();
 #pragma unroll
-        for (int d = 0; d < HD; ++d) o[d] = __float_as_uint(__uint_as_float(o[d]) * alpha);
+        for (int d = 0; d < OW; ++d) o[d] = __float_as_uint(__uint_as_float(o[d]) * alpha);
 #pragma unroll
-        for (int q = 0; q < 4; ++q)
+        for (int q = 0; q < OW / 16; ++q)
           tmem_st_32x32b_x16(lane_base + COL_O + q * 16, *reinterpret_cast<uint32_t(*)[16]>(o + 16 * q));
       }
       tmem_wait_st();
@@ -266,13 +306,14 @@ __global__ void __launch_bounds__(THREADS, 2)
                                              args.err, kDevErrTimeoutAttn));
     if (ok) {
       tc_fence_after();
-      uint32_t o[HD];
+      uint32_t o[OW];
       tmem_ld_32x32b_x32(lane_base + COL_O, *reinterpret_cast<uint32_t(*)[32]>(o));
       tmem_ld_32x32b_x32(lane_base + COL_O + 32, *reinterpret_cast<uint32_t(*)[32]>(o + 32));
+      tmem_ld_32x32b_x16(lane_base + COL_O + 64, *reinterpret_cast<uint32_t(*)[16]>(o + 64));
       tmem_wait_ld();
       const int q = q0 + r;
       if (q < seq) {
-        const float inv = 1.f / l_run;
+        const float inv = 1.f / __uint_as_float(o[HD]);  // sum of P, from the ones columns
         uint4* dst = reinterpret_cast<uint4*>(args.out + (size_t)(row0 + q) * dim + h * HD);
 #pragma unroll
         for (int c8 = 0; c8 < HD / 8; ++c8) {
@@ -311,6 +352,18 @@ sam3_status_t attention_tc(sam3_ctx_t* ctx, const uint16_t* qkv, int batch, int 
                               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS)
     return set_error(ctx, SAM3_ERR_CUDA, "attention: cuTensorMapEncodeTiled failed (%d)", (int)r);
+  // K and V of all heads as a 3-D tensor (dim columns, B*S rows, {k, v}): the
+  // box {64, BKV, 2} is one head's K tile followed by its V tile.
+  CUtensorMap map_kv;
+  cuuint64_t dims3[3] = {(cuuint64_t)dim, (cuuint64_t)batch * seq, 2};
+  cuuint64_t strides3[2] = {(cuuint64_t)(3 * dim) * 2, (cuuint64_t)dim * 2};
+  cuuint32_t box3[3] = {HD, BKV, 2};
+  cuuint32_t es3[3] = {1, 1, 1};
+  const bool kv3d =
+      encode_tiled()(&map_kv, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<uint16_t*>(qkv + dim),
+                     dims3, strides3, box3, es3, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                     CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
   static bool attr_set = false;
   if (!attr_set) {
     cudaError_t e = cudaFuncSetAttribute(attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -325,8 +378,9 @@ sam3_status_t attention_tc(sam3_ctx_t* ctx, const uint16_t* qkv, int batch, int 
   a.heads = heads;
   a.dim = dim;
   a.scale_log2 = scale * 1.4426950408889634f;
+  a.kv3d = kv3d ? 1 : 0;
   dim3 grid((seq + BQ - 1) / BQ, heads, batch);
-  attn_tc_kernel<<<grid, THREADS, SMEM_BYTES, ctx->stream>>>(map, a);
+  attn_tc_kernel<<<grid, THREADS, SMEM_BYTES, ctx->stream>>>(map, kv3d ? map_kv : map, a);
   return check_launch(ctx, "attn_tc_kernel");
 }
 

@@ -320,6 +320,27 @@ __device__ __forceinline__ void tma_load_2d_cg2(uint32_t dst, const CUtensorMap*
       "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster), "r"(x), "r"(y), "l"(policy)
       : "memory");
 }
+// 3-D tiled loads: one request brings several 2-D tiles (the outer box
+// dimension) into consecutive shared memory. TMA throughput per CTA is bound
+// by requests rather than bytes, so bigger boxes stream faster.
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, uint32_t bar,
+                                            int32_t x, int32_t y, int32_t z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(x), "r"(y), "r"(z)
+      : "memory");
+}
+__device__ __forceinline__ void tma_load_3d_cg2(uint32_t dst, const CUtensorMap* map,
+                                                uint32_t bar_cluster, int32_t x, int32_t y,
+                                                int32_t z, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      ".L2::cache_hint [%0], [%1, {%3, %4, %5}], [%2], %6;" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster), "r"(x), "r"(y), "r"(z),
+      "l"(policy)
+      : "memory");
+}
 __device__ __forceinline__ void tmem_alloc_cg2(uint32_t slot_smem, uint32_t ncols) {
   asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(slot_smem),
                "r"(ncols)
@@ -387,6 +408,26 @@ __device__ __forceinline__ float2 unpack_half2(uint32_t v) {
 }
 __device__ __forceinline__ float gelu_erf(float v) {
   return 0.5f * v * (1.0f + erff(v * 0.70710678118654752f));
+}
+__device__ __forceinline__ float rcp_approx(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+// GELU(v) = v * Phi(v) = 0.5 v erfc(-v / sqrt 2), with erfc from Abramowitz &
+// Stegun, Handbook of Mathematical Functions, eq. 7.1.26: for z >= 0,
+// erfc(z) = t (a1 + t (a2 + t (a3 + t (a4 + t a5)))) exp(-z^2), t = 1/(1 + p z),
+// |error| <= 1.5e-7. One reciprocal and one exp2 on the MUFU pipe, the rest on
+// FMA; the negative side uses erfc directly (no 1 - erf cancellation).
+__device__ __forceinline__ float gelu_as(float v) {
+  const float z = fabsf(v) * 0.70710678118654752f;
+  const float t = rcp_approx(fmaf(0.3275911f, z, 1.0f));
+  float q = fmaf(1.061405429f, t, -1.453152027f);
+  q = fmaf(q, t, 1.421413741f);
+  q = fmaf(q, t, -0.284496736f);
+  q = fmaf(q, t, 0.254829592f);
+  q *= t * ex2_approx(-1.4426950408889634f * z * z);  // erfc(z)
+  return 0.5f * v * (v >= 0.f ? 2.0f - q : q);
 }
 
 }  // namespace sam3

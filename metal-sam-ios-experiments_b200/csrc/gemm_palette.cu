@@ -74,6 +74,23 @@ __device__ __forceinline__ void add_half8(float* f, uint4 v) {
   }
 }
 
+__device__ __forceinline__ void prefetch_l1(const void* p) {
+  asm volatile("prefetch.global.L1 [%0];" ::"l"(p));
+}
+
+// Warm L1 with an epilogue's inputs for 64 columns of one output row (bias,
+// RoPE table row, residual row) while the accumulator is still being computed.
+__device__ __forceinline__ void epilogue_prefetch(const GemmArgs& a, int row, int col0) {
+  if (a.bias) prefetch_l1(a.bias + col0);
+  if (a.epi == SAM3_EPI_BIAS_ROPE_QKV && col0 < a.qk_cols) {
+    const float* t = a.rope + (size_t)(row % a.rope_rows) * 64;
+    prefetch_l1(t);
+    prefetch_l1(t + 32);
+  }
+  if (a.epi == SAM3_EPI_BIAS_RESIDUAL && row < a.m)
+    prefetch_l1(a.residual + (size_t)row * a.n + col0);
+}
+
 // Epilogue for 32 consecutive accumulator columns of one output row.
 __device__ __forceinline__ void epilogue_chunk(const GemmArgs& a, int row, int col0,
                                                const uint32_t (&v)[32]) {
@@ -87,7 +104,7 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs& a, int row, int c
   }
   if (a.epi == SAM3_EPI_BIAS_GELU) {
 #pragma unroll
-    for (int j = 0; j < 32; ++j) f[j] = gelu_erf(f[j]);
+    for (int j = 0; j < 32; ++j) f[j] = gelu_as(f[j]);
   } else if (a.epi == SAM3_EPI_BIAS_ROPE_QKV && col0 < a.qk_cols) {
     // 32 columns = 16 interleaved (even, odd) pairs of one 64-wide head;
     // table row holds 32 (cos, sin) pairs, pair j at float offset 2j.
@@ -385,8 +402,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 //              (two warps per TMEM lane quadrant, 64 columns each).
 // ============================================================================
 constexpr int WS_BM = 128, WS_BN = 64, WS_BK = 64, WS_KMAX = 1024;
-constexpr int WS_STAGES = 6;
-constexpr int WS_A_STAGE = WS_BM * WS_BK * 2;         // 16 KB
+// An A stage holds WS_KSPLIT 64-wide k-blocks (two TMA boxes): the MMA
+// issuer then issues 8 pair MMAs per barrier wait. Each mbarrier wait costs
+// the single issuing thread far longer than a pair MMA of N=128 takes to
+// execute, so 4 MMAs per wait starve the tensor pipe.
+constexpr int WS_KSPLIT = 2;
+constexpr int WS_A_BOX = WS_BM * WS_BK * 2;           // 16 KB per 64-wide k-block
+constexpr int WS_STAGES = 3;
+constexpr int WS_A_STAGE = WS_KSPLIT * WS_A_BOX;      // 32 KB
 constexpr int WS_SLAB_KB = WS_BN * WS_BK * 2;         // 8 KB per k-block
 constexpr int WS_OFF_SLAB = 0;
 constexpr int WS_OFF_A = (WS_KMAX / WS_BK) * WS_SLAB_KB;  // 128 KB
@@ -412,6 +435,7 @@ struct WsArgs {
   int units;    // n_tiles * m_tiles
   int sets;     // > 0: pair p owns N tile p % n_tiles and M tiles p / n_tiles + k * sets;
                 // 0: pair p owns a contiguous range of N-major units
+  int a3d;      // 1: the A map is 3-D (one request per A stage), 0: 2-D boxes
 };
 
 // Unit k of pair `pair` -> (n_tile, m_tile); false when the pair has no unit k.
@@ -499,15 +523,21 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(WS_THREADS, 1)
           cur_n = n_tile;
         }
         const int row = m_tile * 2 * WS_BM + (int)rank * WS_BM;
-        for (int kb = 0; kb < kblocks; ++kb) {
+        for (int ks = 0; ks < kblocks / WS_KSPLIT; ++ks) {
           if (!mbar_wait_cluster(bar_a_empty + 8 * s, ph ^ 1, abort_flag, args.err,
                                  kDevErrTimeoutProducer)) {
             ok = false;
             break;
           }
           if (leader) mbar_arrive_expect_tx(bar_a_full + 8 * s, 2 * WS_A_STAGE);
-          tma_load_2d_cg2(sbase + WS_OFF_A + s * WS_A_STAGE, &tmap_a,
-                          mapa_shared(bar_a_full + 8 * s, 0), kb * WS_BK, row, policy);
+          if (wa.a3d)
+            tma_load_3d_cg2(sbase + WS_OFF_A + s * WS_A_STAGE, &tmap_a,
+                            mapa_shared(bar_a_full + 8 * s, 0), 0, row, ks * WS_KSPLIT, policy);
+          else
+            for (int h = 0; h < WS_KSPLIT; ++h)
+              tma_load_2d_cg2(sbase + WS_OFF_A + s * WS_A_STAGE + h * WS_A_BOX, &tmap_a,
+                              mapa_shared(bar_a_full + 8 * s, 0), (ks * WS_KSPLIT + h) * WS_BK,
+                              row, policy);
           if (++s == WS_STAGES) {
             s = 0;
             ph ^= 1;
@@ -537,18 +567,22 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(WS_THREADS, 1)
           break;
         tc_fence_after();
         const uint32_t d_tmem = tmem + (uint32_t)(acc * WS_ACC_COLS);
-        for (int kb = 0; kb < kblocks; ++kb) {
+        for (int ks = 0; ks < kblocks / WS_KSPLIT; ++ks) {
           if (!mbar_wait_cluster(bar_a_full + 8 * s, ph, abort_flag, args.err, kDevErrTimeoutMma)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t a_addr = sbase + WS_OFF_A + s * WS_A_STAGE;
-          const uint32_t b_addr = sbase + WS_OFF_SLAB + kb * WS_SLAB_KB;
 #pragma unroll
-          for (int kk = 0; kk < WS_BK / 16; ++kk)
-            umma_f16_ss_cg2(d_tmem, umma_desc_sw128(a_addr + kk * 32),
-                            umma_desc_sw128(b_addr + kk * 32), WS_IDESC, (kb | kk) != 0);
+          for (int h = 0; h < WS_KSPLIT; ++h) {
+            const int kb = ks * WS_KSPLIT + h;
+            const uint32_t a_addr = sbase + WS_OFF_A + s * WS_A_STAGE + h * WS_A_BOX;
+            const uint32_t b_addr = sbase + WS_OFF_SLAB + kb * WS_SLAB_KB;
+#pragma unroll
+            for (int kk = 0; kk < WS_BK / 16; ++kk)
+              umma_f16_ss_cg2(d_tmem, umma_desc_sw128(a_addr + kk * 32),
+                              umma_desc_sw128(b_addr + kk * 32), WS_IDESC, (kb | kk) != 0);
+          }
           umma_commit_cg2_mc(bar_a_empty + 8 * s, 0x3);
           issued_any = true;
           if (++s == WS_STAGES) {
@@ -630,26 +664,29 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(WS_THREADS, 1)
         mbar_arrive_cluster(mapa_shared(bar_slab_full, 0));
         cur_n = n_tile;
       }
-      // ---- epilogue of unit u
+      // ---- epilogue of unit u: its 64 columns of this row go from tensor
+      // memory to registers, the accumulator goes straight back to the MMA
+      // issuer, then bias / GELU / RoPE / residual and the stores.
       const int acc = it % WS_NUM_ACC;
       const uint32_t use = (uint32_t)(it / WS_NUM_ACC) & 1u;
+      const int row = m_tile * 2 * WS_BM + (int)rank * WS_BM + quad * 32 + lane;
+      const int col0 = n_tile * 2 * WS_BN + colhalf * 64;
+      epilogue_prefetch(args, row, col0);
       ok = __all_sync(0xffffffffu, mbar_wait_cluster(bar_tfull + 8 * acc, use, abort_flag,
                                                      args.err, kDevErrTimeoutEpilogue));
       if (!ok) break;
       tc_fence_after();
-      const int row = m_tile * 2 * WS_BM + (int)rank * WS_BM + quad * 32 + lane;
       const uint32_t taddr = tmem + ((uint32_t)(quad * 32) << 16) +
                              (uint32_t)(acc * WS_ACC_COLS + colhalf * 64);
-#pragma unroll 1
-      for (int c = 0; c < 2; ++c) {
-        uint32_t v[32];
-        tmem_ld_32x32b_x32(taddr + (uint32_t)(c * 32), v);
-        tmem_wait_ld();
-        epilogue_chunk(args, row, n_tile * 2 * WS_BN + colhalf * 64 + c * 32, v);
-      }
+      uint32_t v[64];
+      tmem_ld_32x32b_x32(taddr, *reinterpret_cast<uint32_t(*)[32]>(v));
+      tmem_ld_32x32b_x32(taddr + 32u, *reinterpret_cast<uint32_t(*)[32]>(v + 32));
+      tmem_wait_ld();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(mapa_shared(bar_tempty + 8 * acc, 0));
+      epilogue_chunk(args, row, col0, *reinterpret_cast<const uint32_t(*)[32]>(v));
+      epilogue_chunk(args, row, col0 + 32, *reinterpret_cast<const uint32_t(*)[32]>(v + 32));
     }
   }
 
@@ -676,7 +713,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(WS_THREADS, 1)
 constexpr int WSC_KC = 512;
 constexpr int WSC_KB_PER_CHUNK = WSC_KC / WS_BK;                    // 8
 constexpr int WSC_BUF = WSC_KB_PER_CHUNK * WS_SLAB_KB;              // 64 KB
-constexpr int WSC_STAGES = 4;
+constexpr int WSC_STAGES = 2;                                      // A stages of WS_KSPLIT k-blocks
 constexpr int WSC_GROUP = 2;                                        // M tiles per group
 constexpr int WSC_OFF_SLAB = 0;                                     // 2 buffers
 constexpr int WSC_OFF_PAL = 2 * WSC_BUF;                            // 128 KB
@@ -695,6 +732,7 @@ struct WscArgs {
   int groups;   // ceil(m_tiles / 2)
   int n_tiles;  // n / 128
   int sets;     // pairs / n_tiles
+  int a3d;      // as WsArgs::a3d
 };
 
 // Expand weight row `exp_row` (0..63) of this CTA, columns [k0, k1), into a
@@ -793,16 +831,22 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(WS_THREADS, 1)
         for (int c = 0; c < chunks && ok; ++c)
           for (int t = 0; t < WSC_GROUP && ok; ++t) {
             const int row = (g * WSC_GROUP + t) * 2 * WS_BM + (int)rank * WS_BM;
-            for (int kb = 0; kb < WSC_KB_PER_CHUNK; ++kb) {
+            for (int ks = 0; ks < WSC_KB_PER_CHUNK / WS_KSPLIT; ++ks) {
               if (!mbar_wait_cluster(bar_a_empty + 8 * s, ph ^ 1, abort_flag, args.err,
                                      kDevErrTimeoutProducer)) {
                 ok = false;
                 break;
               }
               if (leader) mbar_arrive_expect_tx(bar_a_full + 8 * s, 2 * WS_A_STAGE);
-              tma_load_2d_cg2(sbase + WSC_OFF_A + s * WS_A_STAGE, &tmap_a,
-                              mapa_shared(bar_a_full + 8 * s, 0), c * WSC_KC + kb * WS_BK, row,
-                              policy);
+              if (wa.a3d)
+                tma_load_3d_cg2(sbase + WSC_OFF_A + s * WS_A_STAGE, &tmap_a,
+                                mapa_shared(bar_a_full + 8 * s, 0), 0, row,
+                                c * WSC_KB_PER_CHUNK + ks * WS_KSPLIT, policy);
+              else
+                for (int h = 0; h < WS_KSPLIT; ++h)
+                  tma_load_2d_cg2(sbase + WSC_OFF_A + s * WS_A_STAGE + h * WS_A_BOX, &tmap_a,
+                                  mapa_shared(bar_a_full + 8 * s, 0),
+                                  c * WSC_KC + (ks * WS_KSPLIT + h) * WS_BK, row, policy);
               if (++s == WSC_STAGES) {
                 s = 0;
                 ph ^= 1;
@@ -833,20 +877,24 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(WS_THREADS, 1)
           tc_fence_after();
           for (int t = 0; t < WSC_GROUP && ok; ++t) {
             const uint32_t d_tmem = tmem + (uint32_t)((2 * gp + t) * WS_ACC_COLS);
-            for (int kb = 0; kb < WSC_KB_PER_CHUNK; ++kb) {
+            for (int ks = 0; ks < WSC_KB_PER_CHUNK / WS_KSPLIT; ++ks) {
               if (!mbar_wait_cluster(bar_a_full + 8 * s, ph, abort_flag, args.err,
                                      kDevErrTimeoutMma)) {
                 ok = false;
                 break;
               }
               tc_fence_after();
-              const uint32_t a_addr = sbase + WSC_OFF_A + s * WS_A_STAGE;
-              const uint32_t b_addr = sbase + WSC_OFF_SLAB + b * WSC_BUF + kb * WS_SLAB_KB;
 #pragma unroll
-              for (int kk = 0; kk < WS_BK / 16; ++kk)
-                umma_f16_ss_cg2(d_tmem, umma_desc_sw128(a_addr + kk * 32),
-                                umma_desc_sw128(b_addr + kk * 32), WS_IDESC,
-                                (c | kb | kk) != 0);
+              for (int h = 0; h < WS_KSPLIT; ++h) {
+                const int kb = ks * WS_KSPLIT + h;
+                const uint32_t a_addr = sbase + WSC_OFF_A + s * WS_A_STAGE + h * WS_A_BOX;
+                const uint32_t b_addr = sbase + WSC_OFF_SLAB + b * WSC_BUF + kb * WS_SLAB_KB;
+#pragma unroll
+                for (int kk = 0; kk < WS_BK / 16; ++kk)
+                  umma_f16_ss_cg2(d_tmem, umma_desc_sw128(a_addr + kk * 32),
+                                  umma_desc_sw128(b_addr + kk * 32), WS_IDESC,
+                                  (c | kb | kk) != 0);
+              }
               umma_commit_cg2_mc(bar_a_empty + 8 * s, 0x3);
               issued_any = true;
               if (++s == WSC_STAGES) {
@@ -877,30 +925,38 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(WS_THREADS, 1)
     int cur_n = -1, it = 0, q = 0;
     int pend_it = -1, pend_g = -1;  // group whose epilogue is still to do
     bool ok = true;
+    // Epilogue of a group: per M tile, its 64 columns of this row go from
+    // tensor memory to registers (the accumulator pair is handed back to the
+    // MMA issuer as soon as the last tile's values are out), then the math
+    // and the stores.
     auto epilogue = [&](int e_it, int g) -> bool {
       const int gp = e_it & 1;
+      const int col0 = my_n * 2 * WS_BN + colhalf * 64;
+      const int row0 = g * WSC_GROUP * 2 * WS_BM + (int)rank * WS_BM + quad * 32 + lane;
+#pragma unroll
+      for (int t = 0; t < WSC_GROUP; ++t) epilogue_prefetch(args, row0 + t * 2 * WS_BM, col0);
       const bool w = __all_sync(0xffffffffu,
                                 mbar_wait_cluster(bar_tfull + 8 * gp, (uint32_t)(e_it >> 1) & 1u,
                                                   abort_flag, args.err, kDevErrTimeoutEpilogue));
       if (!w) return false;
       tc_fence_after();
-      const int n_tile = my_n;
 #pragma unroll 1
       for (int t = 0; t < WSC_GROUP; ++t) {
-        const int row = (g * WSC_GROUP + t) * 2 * WS_BM + (int)rank * WS_BM + quad * 32 + lane;
+        const int row = row0 + t * 2 * WS_BM;
         const uint32_t taddr = tmem + ((uint32_t)(quad * 32) << 16) +
                                (uint32_t)((2 * gp + t) * WS_ACC_COLS + colhalf * 64);
-#pragma unroll 1
-        for (int cc = 0; cc < 2; ++cc) {
-          uint32_t v[32];
-          tmem_ld_32x32b_x32(taddr + (uint32_t)(cc * 32), v);
-          tmem_wait_ld();
-          epilogue_chunk(args, row, n_tile * 2 * WS_BN + colhalf * 64 + cc * 32, v);
+        uint32_t v[64];
+        tmem_ld_32x32b_x32(taddr, *reinterpret_cast<uint32_t(*)[32]>(v));
+        tmem_ld_32x32b_x32(taddr + 32u, *reinterpret_cast<uint32_t(*)[32]>(v + 32));
+        tmem_wait_ld();
+        if (t == WSC_GROUP - 1) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive_cluster(mapa_shared(bar_tempty + 8 * gp, 0));
         }
+        epilogue_chunk(args, row, col0, *reinterpret_cast<const uint32_t(*)[32]>(v));
+        epilogue_chunk(args, row, col0 + 32, *reinterpret_cast<const uint32_t(*)[32]>(v + 32));
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive_cluster(mapa_shared(bar_tempty + 8 * gp, 0));
       return true;
     };
     for (int g = my_set; g < wa.groups && ok; g += wa.sets, ++it) {
@@ -1019,6 +1075,23 @@ sam3_status_t make_map_2d(sam3_ctx_t* ctx, CUtensorMap* map, CUtensorMapDataType
   return SAM3_OK;
 }
 
+// X [m, k] as a 3-D tensor (64 columns, m rows, k/64 column blocks) whose
+// box {64, 128, WS_KSPLIT} is one A stage of the pair kernels: WS_KSPLIT
+// 128-row x 64-column tiles, 128B-swizzled, one after the other in shared
+// memory, exactly the layout of WS_KSPLIT 2-D boxes but in one request.
+// Returns false when the driver does not accept the map (the kernels then
+// issue the 2-D boxes).
+bool make_map_a3d(CUtensorMap* map, const void* x, int k, int m) {
+  cuuint64_t dims[3] = {(cuuint64_t)WS_BK, (cuuint64_t)m, (cuuint64_t)(k / WS_BK)};
+  cuuint64_t strides[2] = {(cuuint64_t)k * 2, (cuuint64_t)WS_BK * 2};
+  cuuint32_t box[3] = {(cuuint32_t)WS_BK, (cuuint32_t)WS_BM, (cuuint32_t)WS_KSPLIT};
+  cuuint32_t es[3] = {1, 1, 1};
+  return encode_tiled()(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(x), dims,
+                        strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 sam3_status_t launch_ws(sam3_ctx_t* ctx, const CUtensorMap& ma, const WsArgs& wa) {
   static bool attr_set = false;
   if (!attr_set) {
@@ -1119,7 +1192,7 @@ sam3_status_t gemm_palette(sam3_ctx_t* ctx, const uint16_t* x, int m, int k, con
   const double bytes = 2.0 * m * k + 1.0 * n * k + 512.0 * n + 2.0 * m * n *
                        (epi == SAM3_EPI_BIAS_RESIDUAL ? 2 : 1);
   ProfScope prof(ctx, SAM3_PROF_GEMM, 2.0 * m * n * k, bytes);
-  if (k <= WS_KMAX) {
+  if (k <= WS_KMAX && k % (WS_KSPLIT * WS_BK) == 0) {
     // weight-stationary pair kernel: the A map's box is 64 x 128 as above
     WsArgs wa;
     wa.g = a;
@@ -1128,15 +1201,21 @@ sam3_status_t gemm_palette(sam3_ctx_t* ctx, const uint16_t* x, int m, int k, con
     wa.m_tiles = (m + 2 * WS_BM - 1) / (2 * WS_BM);
     wa.n_tiles = n / (2 * WS_BN);
     wa.units = wa.m_tiles * wa.n_tiles;
-    // Fixed N tile per pair when that idles at most 10% of the pairs and
-    // leaves every pair at least two M tiles; contiguous ranges otherwise.
+    // Fixed N tile per pair (the pairs of a set sweep M in lockstep, so X is
+    // read from DRAM once) when that idles at most 10% of the pairs, or 15%
+    // when X is too big to stay in L2 under the contiguous schedule (whose
+    // pairs sweep X at 74 different offsets); every pair needs at least two
+    // M tiles. Contiguous N-major ranges otherwise.
     const int max_pairs = ctx->num_sms / 2;
     const int sets = wa.n_tiles <= max_pairs ? max_pairs / wa.n_tiles : 0;
-    wa.sets = (sets > 0 && (max_pairs - sets * wa.n_tiles) * 10 <= max_pairs &&
+    const int idle_pct_limit = 2.0 * m * k > 64.0 * 1024 * 1024 ? 15 : 10;
+    wa.sets = (sets > 0 && (max_pairs - sets * wa.n_tiles) * 100 <= idle_pct_limit * max_pairs &&
                wa.m_tiles >= 2 * sets)
                   ? sets
                   : 0;
-    return launch_ws(ctx, ma, wa);
+    CUtensorMap ma3;
+    wa.a3d = make_map_a3d(&ma3, x, k, m) ? 1 : 0;
+    return launch_ws(ctx, wa.a3d ? ma3 : ma, wa);
   }
   if (k % WSC_KC == 0 && n / (2 * WS_BN) <= ctx->num_sms / 2) {
     // chunked weight-stationary pair kernel
@@ -1149,7 +1228,9 @@ sam3_status_t gemm_palette(sam3_ctx_t* ctx, const uint16_t* x, int m, int k, con
     wa.n_tiles = n / (2 * WS_BN);
     wa.sets = (ctx->num_sms / 2) / wa.n_tiles;
     if (wa.sets > wa.groups) wa.sets = wa.groups;
-    return launch_wsc(ctx, ma, wa);
+    CUtensorMap ma3;
+    wa.a3d = make_map_a3d(&ma3, x, k, m) ? 1 : 0;
+    return launch_wsc(ctx, wa.a3d ? ma3 : ma, wa);
   }
   if ((st = make_map_2d(ctx, &mb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, idx, (uint64_t)k, (uint64_t)n,
                         BK, BN, CU_TENSOR_MAP_SWIZZLE_64B)) != SAM3_OK)
