@@ -165,6 +165,9 @@ def cpu_oracle_sample(repeats=1):
     import numpy as np
     from oracle import oracle as O
     O.build()
+    # every host core this process may run on (torch.distributed.run sets
+    # OMP_NUM_THREADS=1 for each rank, which would time a single core)
+    O.set_num_threads(len(os.sched_getaffinity(0)))
     blk_a = O.SyntheticBlock(7, 0)
     blk_b = O.SyntheticBlock(7, 16)
     img = O.gen_uniform(7, 1, (1, IMAGE, IMAGE, 3), -1.0, 1.0)

@@ -83,6 +83,8 @@ def _declare(L):
         fn.argtypes = args
         fn.restype = None
     L.so_num_threads.restype = C.c_int
+    L.so_set_num_threads.argtypes = [C.c_int]
+    L.so_set_num_threads.restype = None
     L.so_half_to_float.argtypes = [C.c_uint16]
     L.so_half_to_float.restype = C.c_float
     L.so_float_to_half.argtypes = [C.c_float]
@@ -100,6 +102,12 @@ def _c(a, dtype):
 
 def num_threads() -> int:
     return lib().so_num_threads()
+
+
+def set_num_threads(n: int) -> None:
+    """OpenMP threads for the oracle's loops (process launchers such as
+    torch.distributed.run set OMP_NUM_THREADS=1 per rank)."""
+    lib().so_set_num_threads(int(n))
 
 
 # ---- generators ---------------------------------------------------------------

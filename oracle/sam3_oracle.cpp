@@ -134,6 +134,13 @@ extern "C" {
 
 float so_half_to_float(uint16_t h) { return h2f(h); }
 uint16_t so_float_to_half(float f) { return f2h(f); }
+void so_set_num_threads(int n) {
+#ifdef _OPENMP
+  if (n > 0) omp_set_num_threads(n);
+#else
+  (void)n;
+#endif
+}
 int so_num_threads(void) {
 #ifdef _OPENMP
   return omp_get_max_threads();

@@ -140,6 +140,8 @@ void so_encoder_forward(const uint16_t* image, int batch, int image_size,
 float so_half_to_float(uint16_t h);
 uint16_t so_float_to_half(float f);
 int so_num_threads(void);
+// Threads the OpenMP loops use from now on (n <= 0: unchanged).
+void so_set_num_threads(int n);
 
 #ifdef __cplusplus
 }
