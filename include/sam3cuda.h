@@ -238,6 +238,25 @@ sam3_status_t sam3_patch_embed(sam3_ctx_t* ctx, const uint16_t* image, int32_t b
                                const uint16_t* patch_b, int32_t patch, int32_t dim,
                                uint16_t* out);
 
+/* Camera-frame preprocessing: f32 RGBA [batch, height, width, 4] with values
+ * in [0, 1] -> fp16 RGB [batch, height, width, 3] = (rgb - mean) / std with
+ * the ImageNet mean (0.485, 0.456, 0.406) and std (0.229, 0.224, 0.225), in
+ * fp32 with IEEE division, rounded to fp16; alpha is dropped. rgba 16-byte
+ * aligned. Reference: SAM3Predictor.setImage, the slice_rgb / sub_mean /
+ * div_std nodes, SAM3Predictor.swift:332-341. */
+sam3_status_t sam3_preprocess_rgba(sam3_ctx_t* ctx, const float* rgba, int32_t batch,
+                                   int32_t height, int32_t width, uint16_t* rgb);
+
+/* Patch embedding straight from f32 RGBA frames: the preprocessing above is
+ * applied while the patches are gathered, so the normalised image never
+ * exists in memory. Output equals sam3_patch_embed on sam3_preprocess_rgba's
+ * output, bit for bit. Reference: SAM3Predictor.swift:332-341 followed by
+ * PatchEmbedding.forward, ViTEncoder.swift:218-263. */
+sam3_status_t sam3_patch_embed_rgba(sam3_ctx_t* ctx, const float* rgba, int32_t batch,
+                                    int32_t height, int32_t width, const uint16_t* patch_w,
+                                    const uint16_t* patch_b, int32_t patch, int32_t dim,
+                                    uint16_t* out);
+
 /* x [batch*seq, dim] -> x + attn(LN1(x)) (in place). Reference: LN1 +
  * MPSAttentionLayer.forward + residual of TransformerBlock.forward,
  * ViTEncoder.swift:388-411; MPSAttention.swift:85-244. */
@@ -265,6 +284,15 @@ sam3_status_t sam3_vit_block(sam3_ctx_t* ctx, uint16_t* x, int32_t batch, int32_
 sam3_status_t sam3_encoder_forward(sam3_ctx_t* ctx, const uint16_t* image, int32_t batch,
                                    const sam3_encoder_weights_t* w, uint16_t* feats,
                                    int32_t* idx);
+
+/* Full encoder from f32 RGBA camera frames [batch, S, S, 4] in [0, 1] on the
+ * device: the ImageNet normalisation is fused into the patch embedding (see
+ * sam3_patch_embed_rgba); otherwise as sam3_encoder_forward. Reference:
+ * SAM3Predictor.setImage's preprocessing (SAM3Predictor.swift:332-341) feeding
+ * ViTEncoder.forward (ViTEncoder.swift:1235-1481). */
+sam3_status_t sam3_encoder_forward_rgba(sam3_ctx_t* ctx, const float* rgba, int32_t batch,
+                                        const sam3_encoder_weights_t* w, uint16_t* feats,
+                                        int32_t* idx);
 
 /* Same, from and to HOST buffers (pinned or pageable): copies the images in,
  * runs the encoder and copies feats/idx out, then waits. Reference:

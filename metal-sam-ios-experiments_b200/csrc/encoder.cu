@@ -69,7 +69,7 @@ sam3_status_t check_rows(sam3_ctx_t* ctx, long long rows) {
 
 // Runs the encoder on a device image; returns the final residual stream
 // (pointer into the workspace) and its rows per image; writes kept indices.
-sam3_status_t encoder_run(sam3_ctx_t* ctx, const uint16_t* image, int batch,
+sam3_status_t encoder_run(sam3_ctx_t* ctx, const void* image, bool rgba, int batch,
                           const sam3_encoder_weights_t* w, int32_t* idx, const uint16_t** out,
                           int* rows_out) {
   const sam3_encoder_config_t& c = ctx->cfg;
@@ -91,8 +91,8 @@ sam3_status_t encoder_run(sam3_ctx_t* ctx, const uint16_t* image, int batch,
     if ((st = rope_table(ctx, grid, grid, 64, c.rope_theta, ctx->rope)) != SAM3_OK) return st;
     ctx->rope_ready = 1;
   }
-  if ((st = patch_embed(ctx, image, batch, c.image_size, c.image_size, w->patch_w, w->patch_b,
-                        c.patch, D, ctx->x, ctx->cols, ctx->patch_wp)) != SAM3_OK)
+  if ((st = patch_embed(ctx, image, rgba, batch, c.image_size, c.image_size, w->patch_w,
+                        w->patch_b, c.patch, D, ctx->x, ctx->cols, ctx->patch_wp)) != SAM3_OK)
     return st;
   uint16_t* cur = ctx->x;
   int rows = S;
@@ -179,7 +179,24 @@ sam3_status_t sam3_encoder_forward(sam3_ctx_t* ctx, const uint16_t* image, int32
   cudaSetDevice(ctx->device);
   const uint16_t* out = nullptr;
   int rows = 0;
-  sam3_status_t st = encoder_run(ctx, image, batch, w, idx, &out, &rows);
+  sam3_status_t st = encoder_run(ctx, image, false, batch, w, idx, &out, &rows);
+  if (st != SAM3_OK) return st;
+  const size_t bytes = (size_t)batch * rows * ctx->cfg.embed_dim * 2;
+  return check_cuda(ctx, cudaMemcpyAsync(feats, out, bytes, cudaMemcpyDeviceToDevice, ctx->stream),
+                    "encoder feats copy");
+}
+
+sam3_status_t sam3_encoder_forward_rgba(sam3_ctx_t* ctx, const float* rgba, int32_t batch,
+                                        const sam3_encoder_weights_t* w, uint16_t* feats,
+                                        int32_t* idx) {
+  SAM3_CHECK_CTX(ctx);
+  if (!feats) return set_error(ctx, SAM3_ERR_INVALID_ARG, "encoder: null feats");
+  if (!rgba || !aligned16(rgba))
+    return set_error(ctx, SAM3_ERR_INVALID_ARG, "encoder: rgba must be a 16-byte aligned pointer");
+  cudaSetDevice(ctx->device);
+  const uint16_t* out = nullptr;
+  int rows = 0;
+  sam3_status_t st = encoder_run(ctx, rgba, true, batch, w, idx, &out, &rows);
   if (st != SAM3_OK) return st;
   const size_t bytes = (size_t)batch * rows * ctx->cfg.embed_dim * 2;
   return check_cuda(ctx, cudaMemcpyAsync(feats, out, bytes, cudaMemcpyDeviceToDevice, ctx->stream),
@@ -204,7 +221,8 @@ sam3_status_t sam3_encoder_forward_host(sam3_ctx_t* ctx, const uint16_t* host_im
   if (st != SAM3_OK) return st;
   const uint16_t* out = nullptr;
   int rows = 0;
-  if ((st = encoder_run(ctx, ctx->image, batch, w, ctx->idx, &out, &rows)) != SAM3_OK) return st;
+  if ((st = encoder_run(ctx, ctx->image, false, batch, w, ctx->idx, &out, &rows)) != SAM3_OK)
+    return st;
   const size_t fbytes = (size_t)batch * rows * c.embed_dim * 2;
   if ((st = check_cuda(ctx, cudaMemcpyAsync(host_feats, out, fbytes, cudaMemcpyDeviceToHost,
                                             ctx->stream),

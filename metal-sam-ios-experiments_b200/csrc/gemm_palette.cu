@@ -426,6 +426,43 @@ constexpr uint32_t WS_IDESC = umma_idesc_f16(2 * WS_BM, 2 * WS_BN);
 static_assert(WS_SMEM_BYTES <= 232448, "shared memory budget");
 static_assert(WS_BN * 128 * 4 <= WS_STAGES * WS_A_STAGE, "palette staging fits the A ring");
 
+// Expand weight row `exp_row` (0..63) of this CTA, columns [k0, k0 + 16*N16),
+// into a slab buffer laid out as 64-row x 128-byte swizzled blocks per
+// 64-wide k-block, k-blocks counted from `kbase`. pal = word[e][r] at
+// pal[e*64].
+// All N16 16-byte index loads of the range are issued before the first
+// lookup, so the thread waits for one L2 round trip instead of N16.
+template <int N16>
+__device__ __forceinline__ void ws_expand_range(const uint8_t* irow, const uint32_t* pal,
+                                                uint8_t* buf, int exp_row, int k0, int kbase) {
+  const int sw = exp_row & 7;
+  uint4 iv[N16];
+#pragma unroll
+  for (int i = 0; i < N16; ++i) iv[i] = __ldg(reinterpret_cast<const uint4*>(irow + k0) + i);
+#pragma unroll
+  for (int i = 0; i < N16; ++i) {
+    const int k = k0 + 16 * i;
+    const uint4 v = iv[i];
+    const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
+    uint32_t o[8];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const uint32_t uu = w4[q];
+      const uint32_t p0 = pal[(uu & 0x7Fu) << 6];
+      const uint32_t p1 = pal[((uu >> 8) & 0x7Fu) << 6];
+      const uint32_t p2 = pal[((uu >> 16) & 0x7Fu) << 6];
+      const uint32_t p3 = pal[((uu >> 24) & 0x7Fu) << 6];
+      const uint32_t t = (uu >> 6) & 0x02020202u;
+      o[2 * q] = __byte_perm(p0, p1, 0x5410u | ((t & 0x0202u) * 0x11u));
+      o[2 * q + 1] = __byte_perm(p2, p3, 0x5410u | (((t >> 16) & 0x0202u) * 0x11u));
+    }
+    const int kb = (k - kbase) >> 6, c = (k & 63) >> 3;
+    uint8_t* dst = buf + kb * WS_SLAB_KB + exp_row * 128;
+    *reinterpret_cast<uint4*>(dst + ((c ^ sw) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
+    *reinterpret_cast<uint4*>(dst + (((c + 1) ^ sw) << 4)) = make_uint4(o[4], o[5], o[6], o[7]);
+  }
+}
+
 struct WsArgs {
   GemmArgs g;
   const uint8_t* idx;
@@ -636,29 +673,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(WS_THREADS, 1)
         if (!ok) break;
         const int kq = args.k / 4;
         const uint8_t* irow = wa.idx + (size_t)wrow * args.k;
-        const int sw = exp_row & 7;
-        for (int k = exp_q * kq; k < (exp_q + 1) * kq; k += 16) {
-          const uint4 v = __ldg(reinterpret_cast<const uint4*>(irow + k));
-          uint32_t o[8];
-          // word[e][r] at pal[e*64]: the same expansion as expand16 with a
-          // 64-row stride
-          const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const uint32_t uu = w4[q];
-            const uint32_t p0 = pal[(uu & 0x7Fu) << 6];
-            const uint32_t p1 = pal[((uu >> 8) & 0x7Fu) << 6];
-            const uint32_t p2 = pal[((uu >> 16) & 0x7Fu) << 6];
-            const uint32_t p3 = pal[((uu >> 24) & 0x7Fu) << 6];
-            const uint32_t t = (uu >> 6) & 0x02020202u;
-            o[2 * q] = __byte_perm(p0, p1, 0x5410u | ((t & 0x0202u) * 0x11u));
-            o[2 * q + 1] = __byte_perm(p2, p3, 0x5410u | (((t >> 16) & 0x0202u) * 0x11u));
-          }
-          const int kb = k >> 6, c = (k & 63) >> 3;
-          uint8_t* dst = smem + WS_OFF_SLAB + kb * WS_SLAB_KB + exp_row * 128;
-          *reinterpret_cast<uint4*>(dst + ((c ^ sw) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
-          *reinterpret_cast<uint4*>(dst + (((c + 1) ^ sw) << 4)) = make_uint4(o[4], o[5], o[6], o[7]);
-        }
+        for (int k = exp_q * kq; k < (exp_q + 1) * kq; k += 32)
+          ws_expand_range<2>(irow, pal, smem + WS_OFF_SLAB, exp_row, k, 0);
         fence_proxy_async_smem();
         mbar_arrive(bar_slab_local);
         mbar_arrive_cluster(mapa_shared(bar_slab_full, 0));
@@ -734,35 +750,6 @@ struct WscArgs {
   int sets;     // pairs / n_tiles
   int a3d;      // as WsArgs::a3d
 };
-
-// Expand weight row `exp_row` (0..63) of this CTA, columns [k0, k1), into a
-// slab buffer laid out as 64-row x 128-byte swizzled blocks per 64-wide
-// k-block, k-blocks counted from `kbase`. pal = word[e][r] at pal[e*64].
-__device__ __forceinline__ void ws_expand_range(const uint8_t* irow, const uint32_t* pal,
-                                                uint8_t* buf, int exp_row, int k0, int k1,
-                                                int kbase) {
-  const int sw = exp_row & 7;
-  for (int k = k0; k < k1; k += 16) {
-    const uint4 v = __ldg(reinterpret_cast<const uint4*>(irow + k));
-    const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
-    uint32_t o[8];
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const uint32_t uu = w4[q];
-      const uint32_t p0 = pal[(uu & 0x7Fu) << 6];
-      const uint32_t p1 = pal[((uu >> 8) & 0x7Fu) << 6];
-      const uint32_t p2 = pal[((uu >> 16) & 0x7Fu) << 6];
-      const uint32_t p3 = pal[((uu >> 24) & 0x7Fu) << 6];
-      const uint32_t t = (uu >> 6) & 0x02020202u;
-      o[2 * q] = __byte_perm(p0, p1, 0x5410u | ((t & 0x0202u) * 0x11u));
-      o[2 * q + 1] = __byte_perm(p2, p3, 0x5410u | (((t >> 16) & 0x0202u) * 0x11u));
-    }
-    const int kb = (k - kbase) >> 6, c = (k & 63) >> 3;
-    uint8_t* dst = buf + kb * WS_SLAB_KB + exp_row * 128;
-    *reinterpret_cast<uint4*>(dst + ((c ^ sw) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
-    *reinterpret_cast<uint4*>(dst + (((c + 1) ^ sw) << 4)) = make_uint4(o[4], o[5], o[6], o[7]);
-  }
-}
 
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(WS_THREADS, 1)
     gemm_wsc_kernel(const __grid_constant__ CUtensorMap tmap_a, const WscArgs wa) {
@@ -999,8 +986,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(WS_THREADS, 1)
           if (!ok) break;
         }
         const int k0 = c * WSC_KC + exp_q * (WSC_KC / 4);
-        ws_expand_range(irow, pal, smem + WSC_OFF_SLAB + b * WSC_BUF, exp_row, k0,
-                        k0 + WSC_KC / 4, c * WSC_KC);
+        ws_expand_range<WSC_KC / 4 / 16>(irow, pal, smem + WSC_OFF_SLAB + b * WSC_BUF, exp_row,
+                                         k0, c * WSC_KC);
         fence_proxy_async_smem();
         mbar_arrive_cluster(mapa_shared(bar_slab_full + 8 * b, 0));
         if (c == 0 && pend_it >= 0) {

@@ -86,7 +86,9 @@ sam3_status_t rope_table(sam3_ctx_t* ctx, int gh, int gw, int hd, float theta, f
 sam3_status_t prune(sam3_ctx_t* ctx, const uint16_t* x, int batch, int seq, int d, int keep,
                     int norm, int order, const float* rope_in, int rope_rows, int rope_cols,
                     uint16_t* feats, float* rope_out, int32_t* idx, float* scores_scratch);
-sam3_status_t patch_embed(sam3_ctx_t* ctx, const uint16_t* image, int batch, int h, int w,
+// image: fp16 RGB NHWC, or f32 RGBA NHWC in [0, 1] normalised on the fly
+// (rgba = true).
+sam3_status_t patch_embed(sam3_ctx_t* ctx, const void* image, bool rgba, int batch, int h, int w,
                           const uint16_t* pw, const uint16_t* pb, int patch, int dim,
                           uint16_t* out, uint16_t* cols_scratch, uint16_t* wpad_scratch);
 

@@ -310,24 +310,54 @@ __global__ void __launch_bounds__(256) prune_gather_kernel(
 // ---------------------------------------------------------------- patch embedding
 // im2col of an NHWC fp16 image into [tokens, kp] rows (k = c*P*P + ky*P + kx,
 // the PyTorch conv-weight order), zero-padded from 3*P*P up to kp.
-__global__ void im2col_kernel(const __half* __restrict__ img, int batch, int h, int w, int patch,
-                              int kp, __half* __restrict__ cols) {
+// ImageNet statistics the reference normalises camera frames with
+// (SAM3Predictor.swift:334-335).
+__constant__ float kImageMean[3] = {0.485f, 0.456f, 0.406f};
+__constant__ float kImageStd[3] = {0.229f, 0.224f, 0.225f};
+
+// (x - mean[c]) / std[c] in fp32 (IEEE division), rounded to fp16: the
+// reference's slice_rgb -> sub_mean -> div_std (SAM3Predictor.swift:332-341).
+__device__ __forceinline__ __half normalize_channel(float x, int c) {
+  return __float2half_rn(__fdiv_rn(x - kImageMean[c], kImageStd[c]));
+}
+
+// One CTA per token: its patch is written as the GEMM A row [c][ky][kx]
+// (the conv weight order), zero-padded to kp columns. RGBA: the image is f32
+// RGBA [B, H, W, 4] in [0, 1] and is normalised on the fly (the A-operand side
+// of the reference's preprocessing); otherwise fp16 RGB [B, H, W, 3].
+template <bool RGBA>
+__global__ void __launch_bounds__(128) im2col_kernel(const void* __restrict__ img, int h, int w,
+                                                     int patch, int kp, __half* __restrict__ cols) {
   const int gw = w / patch, gh = h / patch;
-  const long long total = (long long)batch * gh * gw * kp;
-  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= total) return;
-  const int k = (int)(i % kp);
-  const long long t = i / kp;
+  const int token = blockIdx.x;
+  const int b = token / (gh * gw), p = token - b * (gh * gw);
+  const int y0 = (p / gw) * patch, x0 = (p - (p / gw) * gw) * patch;
   const int pp = patch * patch;
-  __half v = __float2half(0.f);
-  if (k < 3 * pp) {
-    const int c = k / pp, ky = (k % pp) / patch, kx = k % patch;
-    const int b = (int)(t / ((long long)gh * gw));
-    const int p = (int)(t % ((long long)gh * gw));
-    const int yy = (p / gw) * patch + ky, xx = (p % gw) * patch + kx;
-    v = img[(((size_t)b * h + yy) * w + xx) * 3 + c];
+  __half* out = cols + (size_t)token * kp;
+  for (int k = threadIdx.x; k < kp; k += blockDim.x) {
+    __half v = __float2half_rn(0.f);
+    if (k < 3 * pp) {
+      const int c = k / pp, r = k - c * pp, ky = r / patch, kx = r - ky * patch;
+      const size_t pix = ((size_t)b * h + y0 + ky) * w + x0 + kx;
+      if (RGBA)
+        v = normalize_channel(__ldg(static_cast<const float*>(img) + pix * 4 + c), c);
+      else
+        v = static_cast<const __half*>(img)[pix * 3 + c];
+    }
+    out[k] = v;
   }
-  cols[i] = v;
+}
+
+// Stand-alone preprocessing: f32 RGBA [pixels, 4] -> fp16 RGB [pixels, 3].
+__global__ void preprocess_rgba_kernel(const float4* __restrict__ rgba, long long pixels,
+                                       __half* __restrict__ rgb) {
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < pixels;
+       i += (long long)gridDim.x * blockDim.x) {
+    const float4 v = __ldg(rgba + i);
+    rgb[3 * i] = normalize_channel(v.x, 0);
+    rgb[3 * i + 1] = normalize_channel(v.y, 1);
+    rgb[3 * i + 2] = normalize_channel(v.z, 2);
+  }
 }
 
 __global__ void pad_weight_kernel(const __half* __restrict__ w, int n, int k, int kp,
@@ -433,8 +463,8 @@ sam3_status_t prune(sam3_ctx_t* ctx, const uint16_t* x, int batch, int seq, int 
   return check_launch(ctx, "prune_gather_kernel");
 }
 
-sam3_status_t patch_embed(sam3_ctx_t* ctx, const uint16_t* image, int batch, int h, int w,
-                          const uint16_t* pw, const uint16_t* pb, int patch, int dim,
+sam3_status_t patch_embed(sam3_ctx_t* ctx, const void* image, bool rgba, int batch, int h,
+                          int w, const uint16_t* pw, const uint16_t* pb, int patch, int dim,
                           uint16_t* out, uint16_t* cols, uint16_t* wpad) {
   if (!image || !pw || !out || !cols || !wpad)
     return set_error(ctx, SAM3_ERR_INVALID_ARG, "patch_embed: null pointer");
@@ -444,13 +474,18 @@ sam3_status_t patch_embed(sam3_ctx_t* ctx, const uint16_t* image, int batch, int
   const int kp = (k + 63) / 64 * 64;
   const long long tokens = (long long)batch * (h / patch) * (w / patch);
   sam3_status_t st;
+  if (tokens > 0x7FFFFFFFll) return set_error(ctx, SAM3_ERR_SHAPE, "patch_embed: too many tokens");
   {
-    ProfScope prof(ctx, SAM3_PROF_PATCH, 0.0, 2.0 * tokens * k + 2.0 * tokens * kp);
-  im2col_kernel<<<blocks_for(tokens * kp, 256), 256, 0, ctx->stream>>>(
-      reinterpret_cast<const __half*>(image), batch, h, w, patch, kp,
-      reinterpret_cast<__half*>(cols));
-  st = check_launch(ctx, "im2col_kernel");
-  if (st != SAM3_OK) return st;
+    ProfScope prof(ctx, SAM3_PROF_PATCH, 0.0,
+                   (rgba ? 16.0 / 3.0 : 2.0) * tokens * k + 2.0 * tokens * kp);
+    if (rgba)
+      im2col_kernel<true><<<(int)tokens, 128, 0, ctx->stream>>>(image, h, w, patch, kp,
+                                                                 reinterpret_cast<__half*>(cols));
+    else
+      im2col_kernel<false><<<(int)tokens, 128, 0, ctx->stream>>>(image, h, w, patch, kp,
+                                                                  reinterpret_cast<__half*>(cols));
+    st = check_launch(ctx, "im2col_kernel");
+    if (st != SAM3_OK) return st;
   }
   {
     ProfScope prof(ctx, SAM3_PROF_PATCH, 0.0, 2.0 * dim * k + 2.0 * dim * kp);
@@ -540,7 +575,42 @@ sam3_status_t sam3_patch_embed(sam3_ctx_t* ctx, const uint16_t* image, int32_t b
   if (patch <= 0 || tokens * kp > cap_cols || (size_t)dim * kp > (size_t)c.embed_dim *
                                                                      ((3 * c.patch * c.patch + 63) / 64 * 64))
     return set_error(ctx, SAM3_ERR_SHAPE, "patch_embed: shape exceeds context workspace");
-  return patch_embed(ctx, image, batch, h, w, pw, pb, patch, dim, out, ctx->cols, ctx->patch_wp);
+  return patch_embed(ctx, image, false, batch, h, w, pw, pb, patch, dim, out, ctx->cols,
+                     ctx->patch_wp);
+}
+
+sam3_status_t sam3_patch_embed_rgba(sam3_ctx_t* ctx, const float* rgba, int32_t batch, int32_t h,
+                                    int32_t w, const uint16_t* pw, const uint16_t* pb,
+                                    int32_t patch, int32_t dim, uint16_t* out) {
+  SAM3_CHECK_CTX(ctx);
+  cudaSetDevice(ctx->device);
+  const int k = 3 * patch * patch, kp = (k + 63) / 64 * 64;
+  const size_t tokens = (size_t)batch * (h / (patch > 0 ? patch : 1)) * (w / (patch > 0 ? patch : 1));
+  const sam3_encoder_config_t& c = ctx->cfg;
+  const size_t cap_cols = ctx->block_rows * (size_t)((3 * c.patch * c.patch + 63) / 64 * 64);
+  if (patch <= 0 || tokens * kp > cap_cols || (size_t)dim * kp > (size_t)c.embed_dim *
+                                                                     ((3 * c.patch * c.patch + 63) / 64 * 64))
+    return set_error(ctx, SAM3_ERR_SHAPE, "patch_embed: shape exceeds context workspace");
+  if (!rgba || !aligned16(rgba))
+    return set_error(ctx, SAM3_ERR_INVALID_ARG, "patch_embed: rgba must be a 16-byte aligned pointer");
+  return patch_embed(ctx, rgba, true, batch, h, w, pw, pb, patch, dim, out, ctx->cols,
+                     ctx->patch_wp);
+}
+
+sam3_status_t sam3_preprocess_rgba(sam3_ctx_t* ctx, const float* rgba, int32_t batch,
+                                   int32_t height, int32_t width, uint16_t* rgb) {
+  SAM3_CHECK_CTX(ctx);
+  cudaSetDevice(ctx->device);
+  if (!rgba || !rgb) return set_error(ctx, SAM3_ERR_INVALID_ARG, "preprocess: null pointer");
+  if (!aligned16(rgba)) return set_error(ctx, SAM3_ERR_INVALID_ARG, "preprocess: rgba must be 16-byte aligned");
+  if (batch <= 0 || height <= 0 || width <= 0)
+    return set_error(ctx, SAM3_ERR_SHAPE, "preprocess: empty shape");
+  const long long pixels = (long long)batch * height * width;
+  ProfScope prof(ctx, SAM3_PROF_PATCH, 0.0, 22.0 * pixels);
+  const int grid = (int)std::min<long long>((pixels + 255) / 256, (long long)ctx->num_sms * 16);
+  preprocess_rgba_kernel<<<grid, 256, 0, ctx->stream>>>(reinterpret_cast<const float4*>(rgba),
+                                                        pixels, reinterpret_cast<__half*>(rgb));
+  return check_launch(ctx, "preprocess_rgba_kernel");
 }
 
 }  // extern "C"

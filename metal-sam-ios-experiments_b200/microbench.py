@@ -4,6 +4,8 @@
     python microbench.py gemm --m 41472 --n 4096 --k 1024 --epi gelu
     python microbench.py attention --batch 8 --seq 5184
     python microbench.py layernorm --m 41472
+    python microbench.py patch --batch 8 [--rgba]
+    python microbench.py preprocess --batch 8
 
 Inputs are synthetic device tensors (torch is used only to allocate and fill
 them); each iteration calls the operator through the C ABI; timings are CUDA
@@ -37,7 +39,10 @@ def main():
     import sam3cuda as sam3
 
     ap = argparse.ArgumentParser()
-    ap.add_argument("op", choices=("gemm", "attention", "layernorm", "dequant"))
+    ap.add_argument("op", choices=("gemm", "attention", "layernorm", "dequant", "patch",
+                                   "preprocess"))
+    ap.add_argument("--rgba", action="store_true",
+                    help="patch: f32 RGBA frames, normalisation fused into the patch gather")
     ap.add_argument("--m", type=int, default=41472)
     ap.add_argument("--n", type=int, default=4096)
     ap.add_argument("--k", type=int, default=1024)
@@ -104,6 +109,34 @@ def main():
         tf = prof["flops"] / prof["launches"] / (ms * 1e-3) / 1e12
         print(json.dumps({"op": "attention", "batch": a.batch, "seq": a.seq, "heads": a.heads,
                           "us": ms * 1e3, "tflops": tf, "frac_burst_peak": tf / tf_peak}))
+    elif a.op in ("patch", "preprocess"):
+        size = 1008
+        ctx.close()
+        ctx = sam3.Context(0, max_batch=a.batch)
+        rgba = torch.rand((a.batch, size, size, 4), generator=g, device=dev)
+        rgb = (torch.rand((a.batch, size, size, 3), generator=g, device=dev) * 2 - 1).half()
+        if a.op == "preprocess":
+            out = torch.empty((a.batch, size, size, 3), dtype=torch.float16, device=dev)
+            prof = run(lambda: ctx.preprocess_rgba(rgba, a.batch, size, size, out))["patch"]
+            ms = prof["ms"] / prof["launches"]
+            gbs = prof["bytes"] / prof["launches"] / (ms * 1e-3) / 1e9
+            print(json.dumps({"op": "preprocess", "batch": a.batch, "us": ms * 1e3, "gbs": gbs,
+                              "frac_hbm": gbs / bw_peak}))
+            return
+        pw = (torch.randn((1024, 3, 14, 14), generator=g, device=dev) * 0.02).half()
+        pb = (torch.randn((1024,), generator=g, device=dev) * 0.02).half()
+        tokens = a.batch * (size // 14) ** 2
+        out = torch.empty((tokens, 1024), dtype=torch.float16, device=dev)
+        if a.rgba:
+            fn = lambda: ctx.patch_embed_rgba(rgba, a.batch, size, size, pw, pb, 14, 1024, out)
+        else:
+            fn = lambda: ctx.patch_embed(rgb, a.batch, size, size, pw, pb, 14, 1024, out)
+        prof = run(fn)["patch"]
+        ms = prof["ms"] / prof["launches"] * 3  # im2col, weight pad and GEMM per call
+        print(json.dumps({"op": "patch", "rgba": a.rgba, "batch": a.batch, "us_per_call": ms * 1e3,
+                          "gbs_gather_and_pad": prof["bytes"] / (prof["ms"] * 1e-3) / 1e9}))
+        ctx.close()
+        return
     else:
         x = torch.randn((a.m, 1024), generator=g, device=dev).half()
         y = torch.empty_like(x)

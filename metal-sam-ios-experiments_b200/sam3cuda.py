@@ -95,10 +95,13 @@ SIGNATURES = {
     "sam3_token_scores": (_S, [_P, _P, _I, _I, _I, _P]),
     "sam3_prune": (_S, [_P, _P, _I, _I, _I, _I, _I, _I, _P, _I, _I, _P, _P, _P]),
     "sam3_patch_embed": (_S, [_P, _P, _I, _I, _I, _P, _P, _I, _I, _P]),
+    "sam3_patch_embed_rgba": (_S, [_P, _P, _I, _I, _I, _P, _P, _I, _I, _P]),
+    "sam3_preprocess_rgba": (_S, [_P, _P, _I, _I, _I, _P]),
     "sam3_attention_block": (_S, [_P, _P, _I, _I, C.POINTER(BlockWeights), _P, _I]),
     "sam3_mlp_block": (_S, [_P, _P, _I, C.POINTER(BlockWeights)]),
     "sam3_vit_block": (_S, [_P, _P, _I, _I, C.POINTER(BlockWeights), _P, _I]),
     "sam3_encoder_forward": (_S, [_P, _P, _I, C.POINTER(EncoderWeights), _P, _P]),
+    "sam3_encoder_forward_rgba": (_S, [_P, _P, _I, C.POINTER(EncoderWeights), _P, _P]),
     "sam3_encoder_forward_host": (_S, [_P, _P, _I, C.POINTER(EncoderWeights), _P, _P]),
     "sam3_encoder_out_tokens": (C.c_int32, [_P]),
     "sam3_profile_enable": (_S, [_P, _I]),
@@ -291,6 +294,18 @@ class Context:
     def vit_block(self, x, batch, seq, w: BlockWeights, rope, rope_rows):
         self._check(lib.sam3_vit_block(self.handle, ptr(x), batch, seq, C.byref(w), ptr(rope),
                                        rope_rows))
+
+    def preprocess_rgba(self, rgba, batch, height, width, rgb):
+        self._check(lib.sam3_preprocess_rgba(self.handle, ptr(rgba), batch, height, width,
+                                             ptr(rgb)))
+
+    def patch_embed_rgba(self, rgba, batch, height, width, patch_w, patch_b, patch, dim, out):
+        self._check(lib.sam3_patch_embed_rgba(self.handle, ptr(rgba), batch, height, width,
+                                              ptr(patch_w), ptr(patch_b), patch, dim, ptr(out)))
+
+    def encoder_forward_rgba(self, rgba, batch, w: EncoderWeights, feats, idx):
+        self._check(lib.sam3_encoder_forward_rgba(self.handle, ptr(rgba), batch, C.byref(w),
+                                                  ptr(feats), ptr(idx)))
 
     def encoder_forward(self, image, batch, w: EncoderWeights, feats, idx):
         self._check(lib.sam3_encoder_forward(self.handle, ptr(image), batch, C.byref(w),

@@ -75,6 +75,7 @@ def _declare(L):
         "so_select_topk": [P, I, I64, I64, I, P],
         "so_prune": [P, I, I64, I64, I64, I, I, P, I64, I, P, P, P],
         "so_patch_embed": [P, I, I, I, P, P, I, I, P],
+        "so_preprocess_rgba": [P, I64, P],
         "so_vit_block": [P, I, I64, I, I, F, P, P, I64],
         "so_encoder_forward": [P, I, I, I, I, I, I, I, I64, I, I, F, F, P, P, P, P, P],
     }
@@ -235,6 +236,15 @@ def prune(x, batch, seq, keep, norm=SCORE_L2, order=ORDER_INDEX, rope=None,
     lib().so_prune(_p(x), batch, seq, d, keep, norm, order, _p(rope),
                    rope_period or 1, cols, _p(feats), _p(rope_out), _p(idx))
     return feats, rope_out, idx
+
+
+def preprocess_rgba(rgba):
+    """f32 RGBA [..., 4] in [0, 1] -> fp16 RGB [..., 3], ImageNet-normalised
+    (SAM3Predictor.swift:332-341)."""
+    rgba = _c(rgba, np.float32)
+    out = np.empty(rgba.shape[:-1] + (3,), np.float16)
+    lib().so_preprocess_rgba(_p(rgba), rgba.size // 4, _p(out))
+    return out
 
 
 def patch_embed(image, w, bias, patch=14):

@@ -420,6 +420,21 @@ void so_prune(const uint16_t* x, int batch, int64_t seq, int64_t d,
     }
 }
 
+// Camera-frame normalisation of SAM3Predictor.setImage: slice the RGB
+// channels of the f32 RGBA frame, subtract the ImageNet mean and divide by the
+// ImageNet std per channel (SAM3Predictor.swift:332-341), here rounded to fp16
+// for the fp16 encoder input.
+void so_preprocess_rgba(const float* rgba, int64_t pixels, uint16_t* rgb) {
+  static const float mean[3] = {0.485f, 0.456f, 0.406f};
+  static const float stdv[3] = {0.229f, 0.224f, 0.225f};
+#pragma omp parallel for schedule(static)
+  for (int64_t i = 0; i < pixels; ++i)
+    for (int c = 0; c < 3; ++c) {
+      const float x = rgba[4 * i + c];
+      rgb[3 * i + c] = f2h((x - mean[c]) / stdv[c]);
+    }
+}
+
 // conv(patch x patch, stride patch) on an NHWC fp16 image, tokens row-major
 // h*gw + w. Reference: ViTEncoder.swift:218-263 (MPSCNN conv) and
 // Metal/ViTUtils.metal:53-76 (flatten to [S, D], index h*W + w).

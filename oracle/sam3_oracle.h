@@ -96,6 +96,10 @@ void so_prune(const uint16_t* x, int batch, int64_t seq, int64_t d,
               int64_t rope_period, int rope_cols, uint16_t* feats,
               float* rope_out, int32_t* idx);
 
+/* f32 RGBA [pixels, 4] in [0, 1] -> fp16 RGB [pixels, 3]: (x - mean) / std
+ * per channel with the ImageNet statistics, fp32 arithmetic, IEEE division. */
+void so_preprocess_rgba(const float* rgba, int64_t pixels, uint16_t* rgb);
+
 /* NHWC fp16 image -> [b*gh*gw, dim] tokens, conv(patch x patch, stride patch)
  * with weights [dim, 3, patch, patch] and bias [dim]. */
 void so_patch_embed(const uint16_t* image, int batch, int height, int width,

@@ -436,6 +436,65 @@ def test_patch_embed_full_size(ctx_full, sam3, oracle):
     assert max_rel_err(got, oracle.patch_embed(img, w, b, 14)) < 2e-3
 
 
+# ------------------------------------------------------------------ camera-frame preprocessing
+def _rgba_frames(batch, size, seed=41):
+    rng = np.random.default_rng(seed)
+    return rng.random((batch, size, size, 4), dtype=np.float32)
+
+
+def test_preprocess_rgba_bit_exact(ctx, sam3, oracle):
+    rgba = _rgba_frames(2, 112)
+    out = ctx.alloc(2 * 112 * 112 * 3 * 2)
+    ctx.preprocess_rgba(ctx.upload(rgba), 2, 112, 112, out)
+    ctx.sync()
+    got = ctx.download(out, (2, 112, 112, 3), F16)
+    assert np.array_equal(got.view(np.uint16), oracle.preprocess_rgba(rgba).view(np.uint16))
+
+
+def test_patch_embed_rgba_equals_preprocess_then_patch_embed(ctx, sam3, oracle):
+    # the fused normalisation must give the same fp16 patches as the two-pass
+    # path: bit-identical outputs, and the oracle within the GEMM tolerance
+    rgba = _rgba_frames(2, 112, seed=42)
+    w = oracle.gen_normal(43, 2, (256, 3, 14, 14), 0.0, 0.02)
+    b = oracle.gen_normal(43, 3, (256,), 0.0, 0.02)
+    dw, db = ctx.upload(w), ctx.upload(b)
+    fused, twopass, rgb = ctx.alloc(128 * 256 * 2), ctx.alloc(128 * 256 * 2), ctx.alloc(2 * 112 * 112 * 6)
+    drgba = ctx.upload(rgba)
+    ctx.patch_embed_rgba(drgba, 2, 112, 112, dw, db, 14, 256, fused)
+    ctx.preprocess_rgba(drgba, 2, 112, 112, rgb)
+    ctx.patch_embed(rgb, 2, 112, 112, dw, db, 14, 256, twopass)
+    ctx.sync()
+    f = ctx.download(fused, (128, 256), F16)
+    assert np.array_equal(f.view(np.uint16), ctx.download(twopass, (128, 256), F16).view(np.uint16))
+    ref = oracle.patch_embed(oracle.preprocess_rgba(rgba), w, b, 14)
+    assert max_rel_err(f, ref) < 2e-3
+
+
+def test_encoder_rgba_equals_encoder_on_preprocessed(ctx, sam3, oracle):
+    blocks, pw, pb = _small_encoder(oracle, seed=44)
+    w = _upload_encoder(ctx, sam3, blocks, pw, pb)
+    rgba = _rgba_frames(2, 112, seed=45)
+    f1, i1 = ctx.alloc(2 * 32 * 256 * 2), ctx.alloc(2 * 32 * 4)
+    f2, i2 = ctx.alloc(2 * 32 * 256 * 2), ctx.alloc(2 * 32 * 4)
+    ctx.encoder_forward_rgba(ctx.upload(rgba), 2, w, f1, i1)
+    ctx.encoder_forward(ctx.upload(oracle.preprocess_rgba(rgba)), 2, w, f2, i2)
+    ctx.sync()
+    a, b = ctx.download(f1, (2, 32, 256), F16), ctx.download(f2, (2, 32, 256), F16)
+    assert np.array_equal(ctx.download(i1, (2, 32), np.int32), ctx.download(i2, (2, 32), np.int32))
+    assert np.array_equal(a.view(np.uint16), b.view(np.uint16))
+    ref_f, ref_i = oracle.encoder_forward(oracle.preprocess_rgba(rgba), blocks, pw, pb, heads=4,
+                                          prune_after=1, keep=32)
+    assert max_rel_err(a, ref_f) < SPEC_TOL
+
+
+def test_preprocess_rgba_rejects_bad_arguments(ctx, sam3):
+    out = ctx.alloc(64)
+    with pytest.raises(sam3.SAM3Error):
+        ctx.preprocess_rgba(None, 1, 4, 4, out)
+    with pytest.raises(sam3.SAM3Error):
+        ctx.preprocess_rgba(ctx.alloc(1024), 0, 4, 4, out)
+
+
 # ------------------------------------------------------------------ blocks
 def test_mlp_block_c1_full_size(ctx_full, sam3, oracle):
     ctx = ctx_full

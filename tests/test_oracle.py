@@ -157,3 +157,24 @@ def test_encoder_small_end_to_end(oracle):
     assert (np.diff(i1[0]) > 0).all() and i1.min() >= 0 and i1.max() < 64
     assert np.array_equal(f1.view(np.uint16), f2.view(np.uint16)) and np.array_equal(i1, i2)
     assert np.isfinite(f1.astype(np.float32)).all()
+
+
+def test_preprocess_rgba_matches_numpy_float32(oracle):
+    # (x - mean) / std in float32 with IEEE division, rounded to fp16; alpha
+    # dropped; exact values at mean, mean + std, mean - 2 std
+    rng = np.random.default_rng(3)
+    rgba = rng.random((3, 17, 19, 4), dtype=np.float32)
+    mean = np.array([0.485, 0.456, 0.406], np.float32)
+    std = np.array([0.229, 0.224, 0.225], np.float32)
+    ref = ((rgba[..., :3] - mean) / std).astype(np.float16)
+    got = oracle.preprocess_rgba(rgba)
+    assert got.shape == (3, 17, 19, 3)
+    assert np.array_equal(got.view(np.uint16), ref.view(np.uint16))
+    known = np.zeros((1, 1, 3, 4), np.float32)
+    known[0, 0, 0, :3] = mean
+    known[0, 0, 1, :3] = mean + std
+    known[0, 0, 2, :3] = mean - 2 * std
+    known[..., 3] = 0.5
+    k = oracle.preprocess_rgba(known).astype(np.float32)[0, 0]
+    assert np.allclose(k[0], 0.0, atol=1e-6) and np.allclose(k[1], 1.0, atol=2e-3)
+    assert np.allclose(k[2], -2.0, atol=2e-3)
