@@ -106,6 +106,18 @@ typedef struct {
   int32_t num_blocks;
 } sam3_encoder_weights_t;
 
+/* Neck weights (fp16, device pointers): conv1 1x1 [out_dim, in_dim] (OIHW
+ * with 1x1 kernels) + bias [out_dim]; conv2 3x3 [out_dim, out_dim, 3, 3] OIHW
+ * + bias [out_dim]. Reference: NeckLayer.loadWeights, ViTEncoder.swift:47-52. */
+typedef struct {
+  const uint16_t* conv1_w;
+  const uint16_t* conv1_b;
+  const uint16_t* conv2_w;
+  const uint16_t* conv2_b;
+  int32_t in_dim;
+  int32_t out_dim;
+} sam3_neck_weights_t;
+
 /* ---- context ------------------------------------------------------------ */
 /* Fill *cfg with the benchmark defaults listed above. */
 sam3_status_t sam3_config_default(sam3_encoder_config_t* cfg);
@@ -300,6 +312,24 @@ sam3_status_t sam3_encoder_forward_rgba(sam3_ctx_t* ctx, const float* rgba, int3
 sam3_status_t sam3_encoder_forward_host(sam3_ctx_t* ctx, const uint16_t* host_image,
                                         int32_t batch, const sam3_encoder_weights_t* w,
                                         uint16_t* host_feats, int32_t* host_idx);
+
+/* Pruned rows back to their grid positions: out [batch, seq, dim] fp16 is
+ * zero except out[b, idx[b, k], :] = pruned[b, k, :] (idx int32 [batch, keep],
+ * unique per image, as sam3_prune writes them). An index outside [0, seq) is
+ * skipped and reported by the next sam3_sync as SAM3_ERR_INVALID_ARG. dim % 8
+ * == 0. Reference: TokenPruner.restoreSpatial, TokenPruner.swift:130-196. */
+sam3_status_t sam3_restore_spatial(sam3_ctx_t* ctx, const uint16_t* pruned, const int32_t* idx,
+                                   int32_t batch, int32_t keep, int32_t seq, int32_t dim,
+                                   uint16_t* out);
+
+/* FPN-style neck on x fp16 [batch, height*width, in_dim] (row-major grid):
+ * conv 1x1 in_dim -> out_dim + bias, then conv 3x3 (padding 1) out_dim ->
+ * out_dim + bias, NHWC fp16 out [batch, height, width, out_dim]; fp16 between
+ * the convs, fp32 accumulation. in_dim % 64 == 0, out_dim % 128 == 0, and the
+ * grid must fit the context workspace (batch*height*width <= max_batch *
+ * tokens per image). Reference: NeckLayer.forward, ViTEncoder.swift:54-140. */
+sam3_status_t sam3_neck(sam3_ctx_t* ctx, const uint16_t* x, int32_t batch, int32_t height,
+                        int32_t width, const sam3_neck_weights_t* w, uint16_t* out);
 
 /* ---- device-side stage timing ---------------------------------------------
  * When enabled, the context brackets each of its kernel launches with CUDA

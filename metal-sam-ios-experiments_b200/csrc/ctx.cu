@@ -287,6 +287,9 @@ sam3_status_t sam3_sync(sam3_ctx_t* ctx) {
   if (st != SAM3_OK) return st;
   if (err) {
     cudaMemset(ctx->dev_err, 0, sizeof(int));
+    if ((err & 0xF00) == 0x200)  // a kernel met an invalid index in its input and skipped it
+      return set_error(ctx, SAM3_ERR_INVALID_ARG, "index out of range in a kernel input (code 0x%x)",
+                       err);
     return set_error(ctx, SAM3_ERR_TIMEOUT, "kernel bounded wait expired (code 0x%x)", err);
   }
   return SAM3_OK;

@@ -1226,7 +1226,7 @@ sam3_status_t gemm_palette(sam3_ctx_t* ctx, const uint16_t* x, int m, int k, con
 }
 
 sam3_status_t gemm_dense(sam3_ctx_t* ctx, const uint16_t* x, int m, int k, const uint16_t* w,
-                         const uint16_t* bias, int n, uint16_t* y) {
+                         const uint16_t* bias, int n, uint16_t* y, int prof_class) {
   sam3_status_t st = validate(ctx, x, m, k, n, y);
   if (st != SAM3_OK) return st;
   if (!w || !aligned16(w) || (bias && !aligned16(bias)))
@@ -1249,7 +1249,7 @@ sam3_status_t gemm_dense(sam3_ctx_t* ctx, const uint16_t* x, int m, int k, const
   a.rope_rows = 1;
   a.m_tiles = (m + BM - 1) / BM;
   a.total_tiles = a.m_tiles * (n / BN);
-  ProfScope prof(ctx, SAM3_PROF_PATCH, 2.0 * m * n * k, 2.0 * (m * k + n * k + m * n));
+  ProfScope prof(ctx, prof_class, 2.0 * m * n * k, 2.0 * (m * k + n * k + m * n));
   return launch<kDense>(ctx, ma, mb, a);
 }
 

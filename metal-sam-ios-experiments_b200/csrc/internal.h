@@ -77,7 +77,8 @@ sam3_status_t gemm_palette(sam3_ctx_t* ctx, const uint16_t* x, int m, int k,
                            int n, int epi, const uint16_t* residual, const float* rope,
                            int rope_rows, uint16_t* y);
 sam3_status_t gemm_dense(sam3_ctx_t* ctx, const uint16_t* x, int m, int k, const uint16_t* w,
-                         const uint16_t* bias, int n, uint16_t* y);
+                         const uint16_t* bias, int n, uint16_t* y,
+                         int prof_class = SAM3_PROF_PATCH);
 sam3_status_t layernorm(sam3_ctx_t* ctx, const uint16_t* x, int m, int d, const uint16_t* g,
                         const uint16_t* b, float eps, uint16_t* y);
 sam3_status_t attention(sam3_ctx_t* ctx, const uint16_t* qkv, int batch, int seq, int heads,

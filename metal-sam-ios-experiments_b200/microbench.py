@@ -6,6 +6,7 @@
     python microbench.py layernorm --m 41472
     python microbench.py patch --batch 8 [--rgba]
     python microbench.py preprocess --batch 8
+    python microbench.py neck --batch 8          (restoreSpatial + neck, 72x72, 1024 -> 256)
 
 Inputs are synthetic device tensors (torch is used only to allocate and fill
 them); each iteration calls the operator through the C ABI; timings are CUDA
@@ -40,7 +41,7 @@ def main():
 
     ap = argparse.ArgumentParser()
     ap.add_argument("op", choices=("gemm", "attention", "layernorm", "dequant", "patch",
-                                   "preprocess"))
+                                   "preprocess", "neck"))
     ap.add_argument("--rgba", action="store_true",
                     help="patch: f32 RGBA frames, normalisation fused into the patch gather")
     ap.add_argument("--m", type=int, default=41472)
@@ -109,6 +110,34 @@ def main():
         tf = prof["flops"] / prof["launches"] / (ms * 1e-3) / 1e12
         print(json.dumps({"op": "attention", "batch": a.batch, "seq": a.seq, "heads": a.heads,
                           "us": ms * 1e3, "tflops": tf, "frac_burst_peak": tf / tf_peak}))
+    elif a.op == "neck":
+        ctx.close()
+        ctx = sam3.Context(0, max_batch=a.batch)
+        grid, keep, din, dout = 72, 2592, 1024, 256
+        seq = grid * grid
+        pruned = torch.randn((a.batch, keep, din), generator=g, device=dev).half()
+        idx = torch.stack([torch.randperm(seq, generator=torch.Generator().manual_seed(b))[:keep]
+                           .sort().values for b in range(a.batch)]).int().to(dev)
+        spatial = torch.empty((a.batch, seq, din), dtype=torch.float16, device=dev)
+        w1 = (torch.randn((dout, din), generator=g, device=dev) * 0.03).half()
+        b1 = (torch.randn((dout,), generator=g, device=dev) * 0.01).half()
+        w2 = (torch.randn((dout, dout, 3, 3), generator=g, device=dev) * 0.03).half()
+        b2 = (torch.randn((dout,), generator=g, device=dev) * 0.01).half()
+        nw = sam3.neck_weights(w1, b1, w2, b2, din, dout)
+        out = torch.empty((a.batch, grid, grid, dout), dtype=torch.float16, device=dev)
+
+        def call():
+            ctx.restore_spatial(pruned, idx, a.batch, keep, seq, din, spatial)
+            ctx.neck(spatial, a.batch, grid, grid, nw, out)
+
+        prof = run(call)["other"]
+        calls = a.iters
+        flops = 2.0 * a.batch * seq * dout * (din + 9 * dout)
+        ms = prof["ms"] / calls
+        print(json.dumps({"op": "neck", "batch": a.batch, "us_per_call": ms * 1e3,
+                          "tflops_convs": flops / (ms * 1e-3) / 1e12}))
+        ctx.close()
+        return
     elif a.op in ("patch", "preprocess"):
         size = 1008
         ctx.close()

@@ -57,6 +57,11 @@ class EncoderWeights(C.Structure):
                 ("blocks", C.POINTER(BlockWeights)), ("num_blocks", C.c_int32)]
 
 
+class NeckWeights(C.Structure):
+    _fields_ = [("conv1_w", C.c_void_p), ("conv1_b", C.c_void_p), ("conv2_w", C.c_void_p),
+                ("conv2_b", C.c_void_p), ("in_dim", C.c_int32), ("out_dim", C.c_int32)]
+
+
 PROF_CLASSES = ("gemm", "attention", "layernorm", "prune", "patch", "other")
 
 
@@ -102,6 +107,8 @@ SIGNATURES = {
     "sam3_vit_block": (_S, [_P, _P, _I, _I, C.POINTER(BlockWeights), _P, _I]),
     "sam3_encoder_forward": (_S, [_P, _P, _I, C.POINTER(EncoderWeights), _P, _P]),
     "sam3_encoder_forward_rgba": (_S, [_P, _P, _I, C.POINTER(EncoderWeights), _P, _P]),
+    "sam3_restore_spatial": (_S, [_P, _P, _P, _I, _I, _I, _I, _P]),
+    "sam3_neck": (_S, [_P, _P, _I, _I, _I, C.POINTER(NeckWeights), _P]),
     "sam3_encoder_forward_host": (_S, [_P, _P, _I, C.POINTER(EncoderWeights), _P, _P]),
     "sam3_encoder_out_tokens": (C.c_int32, [_P]),
     "sam3_profile_enable": (_S, [_P, _I]),
@@ -295,6 +302,13 @@ class Context:
         self._check(lib.sam3_vit_block(self.handle, ptr(x), batch, seq, C.byref(w), ptr(rope),
                                        rope_rows))
 
+    def restore_spatial(self, pruned, idx, batch, keep, seq, dim, out):
+        self._check(lib.sam3_restore_spatial(self.handle, ptr(pruned), ptr(idx), batch, keep, seq,
+                                             dim, ptr(out)))
+
+    def neck(self, x, batch, height, width, w: NeckWeights, out):
+        self._check(lib.sam3_neck(self.handle, ptr(x), batch, height, width, C.byref(w), ptr(out)))
+
     def preprocess_rgba(self, rgba, batch, height, width, rgb):
         self._check(lib.sam3_preprocess_rgba(self.handle, ptr(rgba), batch, height, width,
                                              ptr(rgb)))
@@ -331,6 +345,10 @@ def palette_linear(idx, palette, bias, n, k) -> PaletteLinear:
 def block_weights(ln1_gamma, ln1_beta, qkv, proj, ln2_gamma, ln2_beta, fc1, fc2) -> BlockWeights:
     return BlockWeights(ptr(ln1_gamma), ptr(ln1_beta), qkv, proj, ptr(ln2_gamma), ptr(ln2_beta),
                         fc1, fc2)
+
+
+def neck_weights(conv1_w, conv1_b, conv2_w, conv2_b, in_dim, out_dim) -> NeckWeights:
+    return NeckWeights(ptr(conv1_w), ptr(conv1_b), ptr(conv2_w), ptr(conv2_b), in_dim, out_dim)
 
 
 def encoder_weights(patch_w, patch_b, blocks) -> EncoderWeights:

@@ -76,6 +76,8 @@ def _declare(L):
         "so_prune": [P, I, I64, I64, I64, I, I, P, I64, I, P, P, P],
         "so_patch_embed": [P, I, I, I, P, P, I, I, P],
         "so_preprocess_rgba": [P, I64, P],
+        "so_restore_spatial": [P, P, I, I64, I64, I64, P],
+        "so_neck": [P, I, I, I, I, I, P, P, P, P, P],
         "so_vit_block": [P, I, I64, I, I, F, P, P, I64],
         "so_encoder_forward": [P, I, I, I, I, I, I, I, I64, I, I, F, F, P, P, P, P, P],
     }
@@ -244,6 +246,29 @@ def preprocess_rgba(rgba):
     rgba = _c(rgba, np.float32)
     out = np.empty(rgba.shape[:-1] + (3,), np.float16)
     lib().so_preprocess_rgba(_p(rgba), rgba.size // 4, _p(out))
+    return out
+
+
+def restore_spatial(pruned, idx, seq):
+    """pruned [B, keep, D] + idx [B, keep] -> [B, seq, D], zeros elsewhere
+    (TokenPruner.swift:130-196)."""
+    pruned = _c(pruned, np.float16)
+    idx = _c(idx, np.int32)
+    b, keep, d = pruned.shape
+    out = np.empty((b, seq, d), np.float16)
+    lib().so_restore_spatial(_p(pruned), _p(idx), b, keep, seq, d, _p(out))
+    return out
+
+
+def neck(x, batch, h, w, w1, b1, w2, b2):
+    """x [B, h*w, din] -> conv1x1 + b1 -> conv3x3 (pad 1) + b2 -> [B, h, w, dout]
+    (ViTEncoder.swift:54-140)."""
+    x = _c(x, np.float16)
+    w1, w2 = _c(w1, np.float16), _c(w2, np.float16)
+    b1, b2 = _c(b1, np.float16), _c(b2, np.float16)
+    dout, din = w1.shape[0], w1.shape[1]
+    out = np.empty((batch, h, w, dout), np.float16)
+    lib().so_neck(_p(x), batch, h, w, din, dout, _p(w1), _p(b1), _p(w2), _p(b2), _p(out))
     return out
 
 

@@ -420,6 +420,64 @@ void so_prune(const uint16_t* x, int batch, int64_t seq, int64_t d,
     }
 }
 
+// TokenPruner.restoreSpatial (TokenPruner.swift:130-196): scatterND of the
+// kept rows, mode .add, into zeros; indices are unique per image.
+void so_restore_spatial(const uint16_t* pruned, const int32_t* idx, int batch, int64_t keep,
+                        int64_t seq, int64_t dim, uint16_t* out) {
+  std::fill(out, out + (size_t)batch * seq * dim, (uint16_t)0);
+  for (int b = 0; b < batch; ++b)
+    for (int64_t k = 0; k < keep; ++k) {
+      const int64_t s = idx[(size_t)b * keep + k];
+      std::copy(pruned + ((size_t)b * keep + k) * dim, pruned + ((size_t)b * keep + k + 1) * dim,
+                out + ((size_t)b * seq + s) * dim);
+    }
+}
+
+// NeckLayer.forward (ViTEncoder.swift:54-140): conv1 1x1 + bias, conv2 3x3
+// (padding 1) + bias, NHWC, both in fp16 tensors with fp32 accumulation.
+void so_neck(const uint16_t* x, int batch, int h, int w, int din, int dout,
+             const uint16_t* w1, const uint16_t* b1, const uint16_t* w2, const uint16_t* b2,
+             uint16_t* out) {
+  const int64_t pix = (int64_t)batch * h * w;
+  std::vector<float> w1f((size_t)dout * din), w2f((size_t)dout * dout * 9);
+  for (size_t i = 0; i < w1f.size(); ++i) w1f[i] = h2f(w1[i]);
+  // w2 [o][c][ky][kx] -> [o][tap][c] so the inner loop runs over channels
+  for (int o = 0; o < dout; ++o)
+    for (int c = 0; c < dout; ++c)
+      for (int t = 0; t < 9; ++t)
+        w2f[((size_t)o * 9 + t) * dout + c] = h2f(w2[((size_t)o * dout + c) * 9 + t]);
+  std::vector<uint16_t> mid((size_t)pix * dout);
+#pragma omp parallel for schedule(static)
+  for (int64_t p = 0; p < pix; ++p) {
+    std::vector<float> xr(din);
+    for (int c = 0; c < din; ++c) xr[c] = h2f(x[(size_t)p * din + c]);
+    for (int o = 0; o < dout; ++o) {
+      float acc = 0.f;
+      const float* wr = &w1f[(size_t)o * din];
+      for (int c = 0; c < din; ++c) acc += xr[c] * wr[c];
+      mid[(size_t)p * dout + o] = f2h(acc + (b1 ? h2f(b1[o]) : 0.f));
+    }
+  }
+#pragma omp parallel for schedule(static)
+  for (int64_t p = 0; p < pix; ++p) {
+    const int64_t b = p / ((int64_t)h * w);
+    const int py = (int)((p / w) % h), px = (int)(p % w);
+    std::vector<float> patch((size_t)9 * dout, 0.f);
+    for (int t = 0; t < 9; ++t) {
+      const int yy = py + t / 3 - 1, xx = px + t % 3 - 1;
+      if (yy < 0 || yy >= h || xx < 0 || xx >= w) continue;
+      const uint16_t* src = &mid[((size_t)(b * h + yy) * w + xx) * dout];
+      for (int c = 0; c < dout; ++c) patch[(size_t)t * dout + c] = h2f(src[c]);
+    }
+    for (int o = 0; o < dout; ++o) {
+      float acc = 0.f;
+      const float* wr = &w2f[(size_t)o * 9 * dout];
+      for (int i = 0; i < 9 * dout; ++i) acc += patch[i] * wr[i];
+      out[(size_t)p * dout + o] = f2h(acc + (b2 ? h2f(b2[o]) : 0.f));
+    }
+  }
+}
+
 // Camera-frame normalisation of SAM3Predictor.setImage: slice the RGB
 // channels of the f32 RGBA frame, subtract the ImageNet mean and divide by the
 // ImageNet std per channel (SAM3Predictor.swift:332-341), here rounded to fp16

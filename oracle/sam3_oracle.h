@@ -96,6 +96,17 @@ void so_prune(const uint16_t* x, int batch, int64_t seq, int64_t d,
               int64_t rope_period, int rope_cols, uint16_t* feats,
               float* rope_out, int32_t* idx);
 
+/* out [batch, seq, dim] = 0 except out[b, idx[b, k]] = pruned[b, k]. */
+void so_restore_spatial(const uint16_t* pruned, const int32_t* idx, int batch, int64_t keep,
+                        int64_t seq, int64_t dim, uint16_t* out);
+
+/* Neck: x [batch, h*w, din] -> conv 1x1 (din -> dout) + b1, rounded to fp16,
+ * -> conv 3x3 pad 1 (dout -> dout) + b2 -> out [batch, h, w, dout] fp16.
+ * Weights OIHW: w1 [dout, din], w2 [dout, dout, 3, 3]; fp32 accumulation. */
+void so_neck(const uint16_t* x, int batch, int h, int w, int din, int dout,
+             const uint16_t* w1, const uint16_t* b1, const uint16_t* w2, const uint16_t* b2,
+             uint16_t* out);
+
 /* f32 RGBA [pixels, 4] in [0, 1] -> fp16 RGB [pixels, 3]: (x - mean) / std
  * per channel with the ImageNet statistics, fp32 arithmetic, IEEE division. */
 void so_preprocess_rgba(const float* rgba, int64_t pixels, uint16_t* rgb);

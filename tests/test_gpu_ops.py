@@ -495,6 +495,72 @@ def test_preprocess_rgba_rejects_bad_arguments(ctx, sam3):
         ctx.preprocess_rgba(ctx.alloc(1024), 0, 4, 4, out)
 
 
+# ------------------------------------------------------------------ restore + neck
+def test_restore_spatial_bit_exact(ctx, sam3, oracle):
+    rng = np.random.default_rng(46)
+    batch, seq, keep, d = 2, 196, 98, 256
+    pruned = rng.standard_normal((batch, keep, d)).astype(F16)
+    idx = np.stack([np.sort(rng.permutation(seq)[:keep]) for _ in range(batch)]).astype(np.int32)
+    out = ctx.alloc(batch * seq * d * 2)
+    ctx.restore_spatial(ctx.upload(pruned), ctx.upload(idx), batch, keep, seq, d, out)
+    ctx.sync()
+    got = ctx.download(out, (batch, seq, d), F16)
+    assert np.array_equal(got.view(np.uint16), oracle.restore_spatial(pruned, idx, seq).view(np.uint16))
+
+
+def test_restore_spatial_reports_out_of_range_index(ctx, sam3):
+    pruned = np.ones((1, 2, 8), F16)
+    idx = np.array([[1, 50]], np.int32)  # 50 >= seq
+    out = ctx.alloc(1 * 10 * 8 * 2)
+    ctx.restore_spatial(ctx.upload(pruned), ctx.upload(idx), 1, 2, 10, 8, out)
+    with pytest.raises(sam3.SAM3Error) as e:
+        ctx.sync()
+    assert e.value.status == sam3.ERR_INVALID_ARG
+    ctx.sync()  # the error word was cleared: the context is usable again
+
+
+def _neck_weights(oracle, seed, din, dout):
+    w1 = oracle.gen_normal(seed, 1, (dout, din), 0.0, 0.03)
+    b1 = oracle.gen_normal(seed, 2, (dout,), 0.0, 0.01)
+    w2 = oracle.gen_normal(seed, 3, (dout, dout, 3, 3), 0.0, 0.03)
+    b2 = oracle.gen_normal(seed, 4, (dout,), 0.0, 0.01)
+    return w1, b1, w2, b2
+
+
+def test_neck_small_chunked(ctx, sam3, oracle):
+    # 64 pixels, 256 -> 128: the 3x3 gather runs in several row chunks of the
+    # small context's workspace
+    batch, h, w, din, dout = 1, 8, 8, 256, 128
+    x = oracle.gen_normal(47, 5, (batch, h * w, din))
+    w1, b1, w2, b2 = _neck_weights(oracle, 48, din, dout)
+    nw = sam3.neck_weights(ctx.upload(w1), ctx.upload(b1), ctx.upload(w2), ctx.upload(b2), din, dout)
+    out = ctx.alloc(batch * h * w * dout * 2)
+    ctx.neck(ctx.upload(x), batch, h, w, nw, out)
+    ctx.sync()
+    got = ctx.download(out, (batch, h, w, dout), F16)
+    assert max_rel_err(got, oracle.neck(x, batch, h, w, w1, b1, w2, b2)) < 2e-3
+
+
+def test_neck_full_size_72x72(ctx_full, sam3, oracle):
+    ctx = ctx_full
+    batch, h, w, din, dout = 1, 72, 72, 1024, 256
+    x = oracle.gen_normal(49, 5, (batch, h * w, din))
+    w1, b1, w2, b2 = _neck_weights(oracle, 50, din, dout)
+    nw = sam3.neck_weights(ctx.upload(w1), ctx.upload(b1), ctx.upload(w2), ctx.upload(b2), din, dout)
+    out = ctx.alloc(batch * h * w * dout * 2)
+    ctx.neck(ctx.upload(x), batch, h, w, nw, out)
+    ctx.sync()
+    got = ctx.download(out, (batch, h, w, dout), F16)
+    assert max_rel_err(got, oracle.neck(x, batch, h, w, w1, b1, w2, b2)) < 2e-3
+
+
+def test_neck_rejects_bad_dims(ctx, sam3, oracle):
+    w1, b1, w2, b2 = _neck_weights(oracle, 51, 256, 96)
+    nw = sam3.neck_weights(ctx.upload(w1), ctx.upload(b1), ctx.upload(w2), ctx.upload(b2), 256, 96)
+    with pytest.raises(sam3.SAM3Error):
+        ctx.neck(ctx.alloc(64 * 256 * 2), 1, 8, 8, nw, ctx.alloc(64 * 96 * 2))
+
+
 # ------------------------------------------------------------------ blocks
 def test_mlp_block_c1_full_size(ctx_full, sam3, oracle):
     ctx = ctx_full

@@ -178,3 +178,45 @@ def test_preprocess_rgba_matches_numpy_float32(oracle):
     k = oracle.preprocess_rgba(known).astype(np.float32)[0, 0]
     assert np.allclose(k[0], 0.0, atol=1e-6) and np.allclose(k[1], 1.0, atol=2e-3)
     assert np.allclose(k[2], -2.0, atol=2e-3)
+
+
+def test_restore_spatial_places_rows_and_zeros(oracle):
+    rng = np.random.default_rng(4)
+    pruned = rng.standard_normal((2, 5, 8)).astype(np.float16)
+    idx = np.stack([rng.permutation(12)[:5] for _ in range(2)]).astype(np.int32)
+    out = oracle.restore_spatial(pruned, idx, 12)
+    assert out.shape == (2, 12, 8)
+    for b in range(2):
+        assert np.array_equal(out[b, idx[b]].view(np.uint16), pruned[b].view(np.uint16))
+        rest = np.setdiff1d(np.arange(12), idx[b])
+        assert not np.any(out[b, rest].astype(np.float32))
+
+
+def _conv_neck_f64(x, batch, h, w, w1, b1, w2, b2):
+    # independent restatement: float64 convolutions, the conv1 output rounded
+    # to fp16 as the reference keeps it in an fp16 tensor
+    din = x.shape[-1]
+    xs = x.astype(np.float64).reshape(batch, h, w, din)
+    mid = (np.einsum("bhwc,oc->bhwo", xs, w1.astype(np.float64)) + b1.astype(np.float64))
+    mid = mid.astype(np.float16).astype(np.float64)
+    pad = np.pad(mid, ((0, 0), (1, 1), (1, 1), (0, 0)))
+    out = np.zeros((batch, h, w, w2.shape[0]))
+    for ky in range(3):
+        for kx in range(3):
+            out += np.einsum("bhwc,oc->bhwo", pad[:, ky:ky + h, kx:kx + w],
+                             w2[:, :, ky, kx].astype(np.float64))
+    return out + b2.astype(np.float64)
+
+
+def test_neck_matches_float64_convolution(oracle):
+    rng = np.random.default_rng(5)
+    batch, h, w, din, dout = 2, 5, 6, 64, 32
+    x = rng.standard_normal((batch, h * w, din)).astype(np.float16)
+    w1 = (rng.standard_normal((dout, din)) * 0.05).astype(np.float16)
+    b1 = (rng.standard_normal(dout) * 0.01).astype(np.float16)
+    w2 = (rng.standard_normal((dout, dout, 3, 3)) * 0.05).astype(np.float16)
+    b2 = (rng.standard_normal(dout) * 0.01).astype(np.float16)
+    got = oracle.neck(x, batch, h, w, w1, b1, w2, b2)
+    ref = _conv_neck_f64(x, batch, h, w, w1, b1, w2, b2)
+    assert got.shape == (batch, h, w, dout)
+    assert max_rel_err(got, ref) < 2e-3
