@@ -561,6 +561,64 @@ def test_neck_rejects_bad_dims(ctx, sam3, oracle):
         ctx.neck(ctx.alloc(64 * 256 * 2), 1, 8, 8, nw, ctx.alloc(64 * 96 * 2))
 
 
+# ------------------------------------------------------------------ palettized .wts weights
+def test_encoder_from_palettized_wts_file(ctx, sam3, oracle, tmp_path):
+    # dense fp16 weights under the reference's keys -> SAM3WTS1 file ->
+    # `wts.py palettize` -> load into device memory -> encoder; the oracle runs
+    # the same palettized weights
+    import wts
+    rng = np.random.default_rng(52)
+    dim, hidden, nblocks = 256, 512, 2
+
+    def dense(*shape, std=0.02):
+        return (rng.standard_normal(shape) * std).astype(F16)
+
+    src = {"patch_embed.proj.weight": dense(dim, 3, 14, 14),
+           "patch_embed.proj.bias": dense(dim, std=0.02)}
+    for i in range(nblocks):
+        p = f"blocks.{i}"
+        src.update({f"{p}.norm1.weight": np.ones(dim, F16), f"{p}.norm1.bias": np.zeros(dim, F16),
+                    f"{p}.attn.qkv.weight": dense(3 * dim, dim), f"{p}.attn.qkv.bias": dense(3 * dim, std=0.01),
+                    f"{p}.attn.proj.weight": dense(dim, dim), f"{p}.attn.proj.bias": dense(dim, std=0.01),
+                    f"{p}.norm2.weight": np.ones(dim, F16), f"{p}.norm2.bias": np.zeros(dim, F16),
+                    f"{p}.mlp.lin1.weight": dense(hidden, dim), f"{p}.mlp.lin1.bias": dense(hidden, std=0.01),
+                    f"{p}.mlp.lin2.weight": dense(dim, hidden), f"{p}.mlp.lin2.bias": dense(dim, std=0.01)})
+    a, b = tmp_path / "dense.wts", tmp_path / "pal.wts"
+    wts.write_wts(str(a), src)
+    assert wts.main(["palettize", "--src", str(a), "--dst", str(b), "--iters", "6"]) == 0
+    entries = wts.read_wts(str(b))
+    enc, neck = wts.load_encoder_weights(ctx, entries, nblocks, sam3)
+    assert neck is None
+
+    blocks = []
+    for i in range(nblocks):
+        blk = object.__new__(oracle.SyntheticBlock)
+        p = f"blocks.{i}"
+        blk.dim, blk.hidden = dim, hidden
+        blk.ln1_gamma, blk.ln1_beta = entries[f"{p}.norm1.weight"], entries[f"{p}.norm1.bias"]
+        blk.ln2_gamma, blk.ln2_beta = entries[f"{p}.norm2.weight"], entries[f"{p}.norm2.bias"]
+        for name, key in (("qkv", "attn.qkv"), ("proj", "attn.proj"), ("fc1", "mlp.lin1"),
+                          ("fc2", "mlp.lin2")):
+            setattr(blk, name, {"idx": np.ascontiguousarray(entries[f"{p}.{key}.weight"]),
+                                "palette": np.ascontiguousarray(entries[f"{p}.{key}.weight.palette"]),
+                                "bias": np.ascontiguousarray(entries[f"{p}.{key}.bias"])})
+        blocks.append(blk)
+    img = oracle.gen_uniform(53, 77, (2, 112, 112, 3), -1.0, 1.0)
+    feats, idx = ctx.alloc(2 * 32 * dim * 2), ctx.alloc(2 * 32 * 4)
+    ctx.encoder_forward(ctx.upload(img), 2, enc, feats, idx)
+    ctx.sync()
+    ref_f, ref_i = oracle.encoder_forward(img, blocks, src["patch_embed.proj.weight"],
+                                          src["patch_embed.proj.bias"], heads=4, prune_after=1,
+                                          keep=32)
+    gi = ctx.download(idx, (2, 32), np.int32)
+    gf = ctx.download(feats, (2, 32, dim), F16)
+    for b in range(2):
+        common = np.intersect1d(gi[b], ref_i[b])
+        assert common.size >= 30  # kept sets agree up to near-ties at the cut
+        gpos, rpos = np.searchsorted(gi[b], common), np.searchsorted(ref_i[b], common)
+        assert max_rel_err(gf[b][gpos], ref_f[b][rpos]) < SPEC_TOL
+
+
 # ------------------------------------------------------------------ blocks
 def test_mlp_block_c1_full_size(ctx_full, sam3, oracle):
     ctx = ctx_full
