@@ -118,6 +118,24 @@ typedef struct {
   int32_t out_dim;
 } sam3_neck_weights_t;
 
+/* Weights of the checkpoint-faithful SAM3 encoder variant (device pointers,
+ * fp16): patch_w [dim, 3, patch, patch] + patch_b [dim]; cls_token [dim] or
+ * NULL (zeros, as the reference when the checkpoint has none); pos_embed
+ * [1 + pos_grid^2, dim] (class position first); blocks as in
+ * sam3_encoder_weights_t, any count. window: side of the attention windows in
+ * tokens; the reference uses window = pos_grid (SAM3EncoderConfig.swift:45).
+ * Reference: SAM3Encoder.buildGraph, SAM3Encoder.swift:280-366. */
+typedef struct {
+  const uint16_t* patch_w;
+  const uint16_t* patch_b;
+  const uint16_t* cls_token;
+  const uint16_t* pos_embed;
+  int32_t pos_grid;
+  int32_t window;
+  const sam3_block_weights_t* blocks;
+  int32_t num_blocks;
+} sam3_windowed_encoder_weights_t;
+
 /* ---- context ------------------------------------------------------------ */
 /* Fill *cfg with the benchmark defaults listed above. */
 sam3_status_t sam3_config_default(sam3_encoder_config_t* cfg);
@@ -330,6 +348,23 @@ sam3_status_t sam3_restore_spatial(sam3_ctx_t* ctx, const uint16_t* pruned, cons
  * tokens per image). Reference: NeckLayer.forward, ViTEncoder.swift:54-140. */
 sam3_status_t sam3_neck(sam3_ctx_t* ctx, const uint16_t* x, int32_t batch, int32_t height,
                         int32_t width, const sam3_neck_weights_t* w, uint16_t* out);
+
+/* Checkpoint-faithful SAM3 encoder on fp16 RGB images [batch, S, S, 3] (S =
+ * image_size of the config; embed_dim, num_heads, mlp_hidden, ln_eps and
+ * rope_theta from the config too): patch embedding, class token prepended,
+ * pos_embed added (class position, then the pos_grid^2 table resized to the
+ * token grid by bilinear interpolation with half-pixel centres), then the
+ * blocks: block i attends globally when i % stride == stride - 1 (stride =
+ * max(1, num_blocks / 4)), else inside window x window token windows without
+ * the class token (whose attention output is zero); RoPE (the grid table)
+ * rotates the patch tokens only. out fp16 [batch, grid*grid, dim], grid
+ * order, class token dropped, no pruning. window must divide the grid.
+ * Reference: SAM3Encoder.buildGraph / buildTransformerBlock /
+ * buildFusedQKVAttention, SAM3Encoder.swift:280-366, 368-460, 545-720. */
+sam3_status_t sam3_windowed_encoder_forward(sam3_ctx_t* ctx, const uint16_t* image,
+                                            int32_t batch,
+                                            const sam3_windowed_encoder_weights_t* w,
+                                            uint16_t* out);
 
 /* ---- device-side stage timing ---------------------------------------------
  * When enabled, the context brackets each of its kernel launches with CUDA

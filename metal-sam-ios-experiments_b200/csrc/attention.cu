@@ -14,21 +14,30 @@
 namespace sam3 {
 
 sam3_status_t attention_tc(sam3_ctx_t* ctx, const uint16_t* qkv, int batch, int seq, int heads,
-                           float scale, uint16_t* o);
+                           float scale, uint16_t* o, int groups, int img_rows, int first_row);
 
-sam3_status_t attention(sam3_ctx_t* ctx, const uint16_t* qkv, int batch, int seq, int heads,
-                        int head_dim, float scale, uint16_t* o) {
+sam3_status_t attention_grouped(sam3_ctx_t* ctx, const uint16_t* qkv, int images, int groups,
+                                int seq, int img_rows, int first_row, int heads, int head_dim,
+                                float scale, uint16_t* o) {
   constexpr int kHeadDim = 64;
   if (!qkv || !o) return set_error(ctx, SAM3_ERR_INVALID_ARG, "attention: null pointer");
   if (head_dim != kHeadDim)
     return set_error(ctx, SAM3_ERR_SHAPE, "attention: head_dim must be 64 (got %d)", head_dim);
-  if (batch <= 0 || seq <= 0 || heads <= 0 || heads > 65535 || batch > 65535)
+  if (images <= 0 || groups <= 0 || seq <= 0 || heads <= 0 || heads > 65535 ||
+      (long long)images * groups > 65535 || first_row < 0 ||
+      (long long)first_row + (long long)groups * seq > img_rows)
     return set_error(ctx, SAM3_ERR_SHAPE, "attention: bad shape");
   if (!aligned16(qkv) || !aligned16(o))
     return set_error(ctx, SAM3_ERR_INVALID_ARG, "attention: pointers must be 16-byte aligned");
-  ProfScope prof(ctx, SAM3_PROF_ATTENTION, 4.0 * batch * heads * (double)seq * seq * kHeadDim,
-                 8.0 * batch * seq * heads * kHeadDim);
-  return attention_tc(ctx, qkv, batch, seq, heads, scale, o);
+  ProfScope prof(ctx, SAM3_PROF_ATTENTION,
+                 4.0 * images * groups * heads * (double)seq * seq * kHeadDim,
+                 8.0 * images * groups * seq * heads * kHeadDim);
+  return attention_tc(ctx, qkv, images, seq, heads, scale, o, groups, img_rows, first_row);
+}
+
+sam3_status_t attention(sam3_ctx_t* ctx, const uint16_t* qkv, int batch, int seq, int heads,
+                        int head_dim, float scale, uint16_t* o) {
+  return attention_grouped(ctx, qkv, batch, 1, seq, seq, 0, heads, head_dim, scale, o);
 }
 
 }  // namespace sam3

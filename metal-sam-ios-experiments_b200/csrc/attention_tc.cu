@@ -56,6 +56,10 @@ struct AttnArgs {
   __half* out;
   int* err;
   int seq, heads, dim;
+  // grid.z item z attends over rows [row0, row0 + seq) of the packed QKV:
+  // row0 = (z / groups) * img_rows + first_row + (z % groups) * seq (one
+  // group per image for plain attention; windows of an image otherwise)
+  int groups, img_rows, first_row;
   float scale_log2;
   int kv3d;  // 1: tmap_kv is the 3-D K|V map (one request per stage), 0: use 2-D boxes
 };
@@ -91,7 +95,7 @@ __global__ void __launch_bounds__(THREADS, 2)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int qt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int seq = args.seq, dim = args.dim;
-  const int row0 = b * seq;  // first packed row of this image
+  const int row0 = (b / args.groups) * args.img_rows + args.first_row + (b % args.groups) * seq;
   const int q0 = qt * BQ;
   const int ntiles = (seq + BKV - 1) / BKV;
 
@@ -339,10 +343,10 @@ __global__ void __launch_bounds__(THREADS, 2)
 }  // namespace
 
 sam3_status_t attention_tc(sam3_ctx_t* ctx, const uint16_t* qkv, int batch, int seq, int heads,
-                           float scale, uint16_t* o) {
+                           float scale, uint16_t* o, int groups, int img_rows, int first_row) {
   const int dim = heads * HD;
   CUtensorMap map;
-  cuuint64_t dims[2] = {(cuuint64_t)(3 * dim), (cuuint64_t)batch * seq};
+  cuuint64_t dims[2] = {(cuuint64_t)(3 * dim), (cuuint64_t)batch * img_rows};
   cuuint64_t strides[1] = {(cuuint64_t)(3 * dim) * 2};
   cuuint32_t box[2] = {HD, BKV};
   cuuint32_t es[2] = {1, 1};
@@ -355,7 +359,7 @@ sam3_status_t attention_tc(sam3_ctx_t* ctx, const uint16_t* qkv, int batch, int 
   // K and V of all heads as a 3-D tensor (dim columns, B*S rows, {k, v}): the
   // box {64, BKV, 2} is one head's K tile followed by its V tile.
   CUtensorMap map_kv;
-  cuuint64_t dims3[3] = {(cuuint64_t)dim, (cuuint64_t)batch * seq, 2};
+  cuuint64_t dims3[3] = {(cuuint64_t)dim, (cuuint64_t)batch * img_rows, 2};
   cuuint64_t strides3[2] = {(cuuint64_t)(3 * dim) * 2, (cuuint64_t)dim * 2};
   cuuint32_t box3[3] = {HD, BKV, 2};
   cuuint32_t es3[3] = {1, 1, 1};
@@ -375,11 +379,14 @@ sam3_status_t attention_tc(sam3_ctx_t* ctx, const uint16_t* qkv, int batch, int 
   a.out = reinterpret_cast<__half*>(o);
   a.err = ctx->dev_err;
   a.seq = seq;
+  a.groups = groups;
+  a.img_rows = img_rows;
+  a.first_row = first_row;
   a.heads = heads;
   a.dim = dim;
   a.scale_log2 = scale * 1.4426950408889634f;
   a.kv3d = kv3d ? 1 : 0;
-  dim3 grid((seq + BQ - 1) / BQ, heads, batch);
+  dim3 grid((seq + BQ - 1) / BQ, heads, batch * groups);
   attn_tc_kernel<<<grid, THREADS, SMEM_BYTES, ctx->stream>>>(map, kv3d ? map_kv : map, a);
   return check_launch(ctx, "attn_tc_kernel");
 }

@@ -122,21 +122,26 @@ size_t carve(sam3_ctx_t* ctx, char* base) {
   const size_t keep = (size_t)std::min<int64_t>(c.keep_tokens, (int64_t)S);
   const size_t hd = D / (size_t)c.num_heads;
   const size_t kp = align_up(3u * c.patch * c.patch, 64);
+  // activation rows per image: the S patch tokens plus one class token
+  // (the windowed encoder variant); the plain encoder uses the first S
+  const size_t R = S + 1;
   Carver cv{base};
-  ctx->x = cv.take<uint16_t>(B * S * D);
+  ctx->x = cv.take<uint16_t>(B * R * D);
   ctx->xp = cv.take<uint16_t>(B * keep * D);
-  ctx->ln = cv.take<uint16_t>(B * S * D);
-  ctx->qkv = cv.take<uint16_t>(B * S * 3 * D);
-  ctx->attn = cv.take<uint16_t>(B * S * D);
-  ctx->hidden = cv.take<uint16_t>(B * S * F);
+  ctx->ln = cv.take<uint16_t>(B * R * D);
+  ctx->qkv = cv.take<uint16_t>(B * R * 3 * D);
+  ctx->attn = cv.take<uint16_t>(B * R * D);
+  ctx->hidden = cv.take<uint16_t>(B * R * F);
   ctx->cols = cv.take<uint16_t>(B * S * kp);
   ctx->patch_wp = cv.take<uint16_t>(D * kp);
   ctx->scores = cv.take<float>(B * S);
   ctx->rope = cv.take<float>(S * hd);
+  ctx->rope_win = cv.take<float>(R * hd);
   ctx->rope_pruned = cv.take<float>(B * keep * hd);
   ctx->idx = cv.take<int32_t>(B * S);
   ctx->image = cv.take<uint16_t>(B * (size_t)c.image_size * c.image_size * 3);
   ctx->block_rows = B * S;
+  ctx->token_rows = B * R;
   return align_up(cv.off, 256);
 }
 

@@ -37,12 +37,15 @@ struct sam3_ctx {
   float* scores = nullptr;      // [B*S]
   float* rope = nullptr;        // [S, 32, 2]
   float* rope_pruned = nullptr; // [B*keep, 32, 2]
+  float* rope_win = nullptr;    // [S+1, 32, 2] window-major table of the windowed encoder
+  int rope_win_key = 0;         // window size the table was built for (0: none)
   int32_t* idx = nullptr;       // [B*keep]
   uint16_t* image = nullptr;    // [B, H, W, 3] staging for the host API
   uint16_t* feats = nullptr;    // [B*keep, D] staging for the host API
   int rope_ready = 0;
   // Block-level scratch used by sam3_vit_block & co. outside the encoder.
-  size_t block_rows = 0;        // rows the block scratch can hold
+  size_t block_rows = 0;        // rows the block scratch can hold (plain encoder)
+  size_t token_rows = 0;        // rows with a class token per image (windowed encoder)
 
   // Device-side stage timing (sam3_profile_enable / sam3_profile_read).
   struct ProfRecord {
@@ -83,6 +86,11 @@ sam3_status_t layernorm(sam3_ctx_t* ctx, const uint16_t* x, int m, int d, const 
                         const uint16_t* b, float eps, uint16_t* y);
 sam3_status_t attention(sam3_ctx_t* ctx, const uint16_t* qkv, int batch, int seq, int heads,
                         int head_dim, float scale, uint16_t* o);
+// Attention over `groups` row groups of `seq` rows per image: group g of image
+// i is rows i*img_rows + first_row + g*seq ... (windowed attention).
+sam3_status_t attention_grouped(sam3_ctx_t* ctx, const uint16_t* qkv, int images, int groups,
+                                int seq, int img_rows, int first_row, int heads, int head_dim,
+                                float scale, uint16_t* o);
 sam3_status_t rope_table(sam3_ctx_t* ctx, int gh, int gw, int hd, float theta, float* t);
 sam3_status_t prune(sam3_ctx_t* ctx, const uint16_t* x, int batch, int seq, int d, int keep,
                     int norm, int order, const float* rope_in, int rope_rows, int rope_cols,

@@ -7,6 +7,7 @@
     python microbench.py patch --batch 8 [--rgba]
     python microbench.py preprocess --batch 8
     python microbench.py neck --batch 8          (restoreSpatial + neck, 72x72, 1024 -> 256)
+    python microbench.py windowed --batch 8      (checkpoint-faithful encoder, 32 blocks, 1008^2)
 
 Inputs are synthetic device tensors (torch is used only to allocate and fill
 them); each iteration calls the operator through the C ABI; timings are CUDA
@@ -41,7 +42,7 @@ def main():
 
     ap = argparse.ArgumentParser()
     ap.add_argument("op", choices=("gemm", "attention", "layernorm", "dequant", "patch",
-                                   "preprocess", "neck"))
+                                   "preprocess", "neck", "windowed"))
     ap.add_argument("--rgba", action="store_true",
                     help="patch: f32 RGBA frames, normalisation fused into the patch gather")
     ap.add_argument("--m", type=int, default=41472)
@@ -136,6 +137,58 @@ def main():
         ms = prof["ms"] / calls
         print(json.dumps({"op": "neck", "batch": a.batch, "us_per_call": ms * 1e3,
                           "tflops_convs": flops / (ms * 1e-3) / 1e12}))
+        ctx.close()
+        return
+    elif a.op == "windowed":
+        ctx.close()
+        ctx = sam3.Context(0, max_batch=a.batch)
+        dim, hidden, nblocks, pg, size = 1024, 4096, 32, 24, 1008
+        keep = []
+
+        def t(x):
+            keep.append(x)
+            return x
+
+        def lin(n, k):
+            idx = t(torch.randint(0, 256, (n, k), generator=g, device=dev, dtype=torch.uint8))
+            pal = t((torch.randn((n, 256), generator=g, device=dev) * 0.02).half().sort(dim=1)
+                    .values.contiguous())
+            bias = t((torch.randn((n,), generator=g, device=dev) * 0.01).half())
+            return sam3.palette_linear(idx, pal, bias, n, k)
+
+        ones = t(torch.ones(dim, dtype=torch.float16, device=dev))
+        zeros = t(torch.zeros(dim, dtype=torch.float16, device=dev))
+        blocks = [sam3.block_weights(ones, zeros, lin(3 * dim, dim), lin(dim, dim), ones, zeros,
+                                     lin(hidden, dim), lin(dim, hidden)) for _ in range(nblocks)]
+        pw = t((torch.randn((dim, 3, 14, 14), generator=g, device=dev) * 0.02).half())
+        pb = t((torch.randn((dim,), generator=g, device=dev) * 0.02).half())
+        cls = t((torch.randn((dim,), generator=g, device=dev) * 0.02).half())
+        pos = t((torch.randn((1 + pg * pg, dim), generator=g, device=dev) * 0.02).half())
+        w = sam3.windowed_encoder_weights(pw, pb, cls, pos, pg, blocks)
+        img = (torch.rand((a.batch, size, size, 3), generator=g, device=dev) * 2 - 1).half()
+        out = torch.empty((a.batch, 5184, dim), dtype=torch.float16, device=dev)
+        fn = lambda: ctx.windowed_encoder_forward(img, a.batch, w, out)
+        prof = run(fn)
+        stream = torch.cuda.ExternalStream(ctx.stream, device=dev)
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ctx.sync()
+        ev0.record(stream)
+        for _ in range(a.iters):
+            fn()
+        ev1.record(stream)
+        ev1.synchronize()
+        ms = ev0.elapsed_time(ev1) / a.iters
+        T = 5185
+        win_att = 4.0 * 9 * 576 * 576 * 64 * 16
+        glob_att = 4.0 * T * T * 64 * 16
+        flops = a.batch * (nblocks * 2.0 * T * dim * (4 * dim + 2 * hidden)
+                           + 24 * win_att + 8 * glob_att)
+        print(json.dumps({
+            "op": "windowed", "batch": a.batch, "ms_per_call": ms, "images_per_s": a.batch / (ms * 1e-3),
+            "tflops": flops / (ms * 1e-3) / 1e12,
+            "classes_ms_per_call": {k: v["ms"] / a.iters for k, v in prof.items() if v["launches"]},
+            "gemm_tflops": prof["gemm"]["flops"] / (prof["gemm"]["ms"] * 1e-3) / 1e12,
+            "attention_tflops": prof["attention"]["flops"] / (prof["attention"]["ms"] * 1e-3) / 1e12}))
         ctx.close()
         return
     elif a.op in ("patch", "preprocess"):

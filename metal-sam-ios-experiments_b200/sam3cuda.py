@@ -62,6 +62,12 @@ class NeckWeights(C.Structure):
                 ("conv2_b", C.c_void_p), ("in_dim", C.c_int32), ("out_dim", C.c_int32)]
 
 
+class WindowedEncoderWeights(C.Structure):
+    _fields_ = [("patch_w", C.c_void_p), ("patch_b", C.c_void_p), ("cls_token", C.c_void_p),
+                ("pos_embed", C.c_void_p), ("pos_grid", C.c_int32), ("window", C.c_int32),
+                ("blocks", C.POINTER(BlockWeights)), ("num_blocks", C.c_int32)]
+
+
 PROF_CLASSES = ("gemm", "attention", "layernorm", "prune", "patch", "other")
 
 
@@ -109,6 +115,7 @@ SIGNATURES = {
     "sam3_encoder_forward_rgba": (_S, [_P, _P, _I, C.POINTER(EncoderWeights), _P, _P]),
     "sam3_restore_spatial": (_S, [_P, _P, _P, _I, _I, _I, _I, _P]),
     "sam3_neck": (_S, [_P, _P, _I, _I, _I, C.POINTER(NeckWeights), _P]),
+    "sam3_windowed_encoder_forward": (_S, [_P, _P, _I, C.POINTER(WindowedEncoderWeights), _P]),
     "sam3_encoder_forward_host": (_S, [_P, _P, _I, C.POINTER(EncoderWeights), _P, _P]),
     "sam3_encoder_out_tokens": (C.c_int32, [_P]),
     "sam3_profile_enable": (_S, [_P, _I]),
@@ -325,6 +332,10 @@ class Context:
         self._check(lib.sam3_encoder_forward(self.handle, ptr(image), batch, C.byref(w),
                                              ptr(feats), ptr(idx)))
 
+    def windowed_encoder_forward(self, image, batch, w: WindowedEncoderWeights, out):
+        self._check(lib.sam3_windowed_encoder_forward(self.handle, ptr(image), batch, C.byref(w),
+                                                      ptr(out)))
+
     def encoder_forward_host(self, image_host: np.ndarray, batch, w: EncoderWeights,
                              feats_host: np.ndarray, idx_host: np.ndarray):
         """Host buffers in and out (numpy arrays or anything with a ctypes data pointer)."""
@@ -356,4 +367,15 @@ def encoder_weights(patch_w, patch_b, blocks) -> EncoderWeights:
     w = EncoderWeights(ptr(patch_w), ptr(patch_b), C.cast(arr, C.POINTER(BlockWeights)),
                        len(blocks))
     w._keepalive = arr  # the C struct points into this array
+    return w
+
+
+def windowed_encoder_weights(patch_w, patch_b, cls_token, pos_embed, pos_grid, blocks,
+                             window=None) -> WindowedEncoderWeights:
+    """window defaults to pos_grid, as in the reference (SAM3EncoderConfig.swift:45)."""
+    arr = (BlockWeights * max(1, len(blocks)))(*blocks)
+    w = WindowedEncoderWeights(ptr(patch_w), ptr(patch_b), ptr(cls_token), ptr(pos_embed),
+                               pos_grid, pos_grid if window is None else window,
+                               C.cast(arr, C.POINTER(BlockWeights)), len(blocks))
+    w._keepalive = arr
     return w

@@ -80,6 +80,7 @@ def _declare(L):
         "so_neck": [P, I, I, I, I, I, P, P, P, P, P],
         "so_vit_block": [P, I, I64, I, I, F, P, P, I64],
         "so_encoder_forward": [P, I, I, I, I, I, I, I, I64, I, I, F, F, P, P, P, P, P],
+        "so_windowed_encoder_forward": [P, I, I, I, I, I, I, I, I, F, F, P, P, P, P, P, P],
     }
     for name, args in sig.items():
         fn = getattr(L, name)
@@ -349,3 +350,31 @@ def encoder_forward(image, blocks, patch_w, patch_b, heads=16, patch=14,
                              prune_after, keep, norm, order, ln_eps, theta,
                              _p(patch_w), _p(patch_b), arr, _p(feats), _p(idx))
     return feats, idx
+
+
+def windowed_encoder_forward(image, blocks, patch_w, patch_b, cls_token, pos_embed, heads=16,
+                             patch=14, window=None, ln_eps=1e-6, theta=10000.0):
+    """Checkpoint-faithful SAM3 encoder (class token, resized positions,
+    windowed/global blocks); returns [batch, grid^2, dim] in grid order.
+    cls_token may be None (zeros); pos_embed [1 + pos_grid^2, dim]; window
+    defaults to pos_grid, as in the reference."""
+    image = _c(image, np.float16)
+    b, size, _, _ = image.shape
+    grid = size // patch
+    dim = patch_w.shape[0]
+    pos_embed = _c(pos_embed, np.float16).reshape(-1, dim)
+    pos_grid = int(round((pos_embed.shape[0] - 1) ** 0.5))
+    if pos_grid * pos_grid + 1 != pos_embed.shape[0]:
+        raise ValueError("pos_embed must hold 1 + pos_grid^2 rows")
+    window = pos_grid if window is None else window
+    if grid % window:
+        raise ValueError("window must divide the token grid")
+    arr = (BlockWeights * max(1, len(blocks)))(*[blk.as_struct() for blk in blocks])
+    out = np.empty((b, grid * grid, dim), np.float16)
+    patch_w = _c(patch_w, np.float16)
+    patch_b = _c(patch_b, np.float16)
+    cls = None if cls_token is None else _c(cls_token, np.float16)
+    lib().so_windowed_encoder_forward(_p(image), b, size, patch, dim, heads, len(blocks), window,
+                                      pos_grid, ln_eps, theta, _p(patch_w), _p(patch_b), _p(cls),
+                                      _p(pos_embed), arr, _p(out))
+    return out

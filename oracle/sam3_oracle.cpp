@@ -587,4 +587,110 @@ void so_encoder_forward(const uint16_t* image, int batch, int image_size,
   std::memcpy(feats, x.data(), (size_t)(batch * cur * dim) * 2);
 }
 
+
+// Bilinear sample (half-pixel centres, edge clamp) of the pg x pg positional
+// grid at token (gy, gx) of a grid x grid token grid, channel c; rounded to
+// fp16. Reference: the bilinear resize with centerResult = true, alignCorners
+// = false of SAM3Encoder.swift:314-322. Interpolation a + f*(b - a) with
+// explicit fused multiply-adds, so the value is a defined function of the
+// inputs.
+static float upsampled_pos(const uint16_t* grid_pos, int pg, int grid, int gy, int gx, int c,
+                           int dim) {
+  const float ratio = (float)pg / (float)grid;
+  const float sy = std::max(std::fma((float)gy + 0.5f, ratio, -0.5f), 0.f);
+  const float sx = std::max(std::fma((float)gx + 0.5f, ratio, -0.5f), 0.f);
+  const int y0 = std::min((int)std::floor(sy), pg - 1), x0 = std::min((int)std::floor(sx), pg - 1);
+  const int y1 = std::min(y0 + 1, pg - 1), x1 = std::min(x0 + 1, pg - 1);
+  const float fy = sy - (float)y0, fx = sx - (float)x0;
+  auto at = [&](int y, int x) { return h2f(grid_pos[(size_t)(y * pg + x) * dim + c]); };
+  const float a = at(y0, x0), b = at(y0, x1), d = at(y1, x0), e = at(y1, x1);
+  const float top = std::fma(fx, b - a, a);
+  const float bot = std::fma(fx, e - d, d);
+  return h2f(f2h(std::fma(fy, bot - top, top)));
+}
+
+// Checkpoint-faithful SAM3 encoder, in grid order with explicit windows.
+// Reference: SAM3Encoder.buildGraph (SAM3Encoder.swift:259-366): patch
+// embedding, class token prepended (:288-298), class position + resized grid
+// positions added (:300-329), global blocks at i % stride == stride - 1 with
+// stride = max(1, num_blocks / 4) (:331-357); buildFusedQKVAttention
+// (:545-720): RoPE on the patch tokens only (:598-641), windowed blocks
+// partition the patch tokens into window x window windows (:651-663, window
+// partition :462-505) and give the class token a zero attention output
+// (:701-712); output = patch tokens in grid order (:363-366).
+void so_windowed_encoder_forward(const uint16_t* image, int batch, int image_size, int patch,
+                                 int dim, int heads, int num_blocks, int window, int pos_grid,
+                                 float ln_eps, float rope_theta, const uint16_t* patch_w,
+                                 const uint16_t* patch_b, const uint16_t* cls_token,
+                                 const uint16_t* pos_embed, const so_block_weights_t* blocks,
+                                 uint16_t* out) {
+  const int grid = image_size / patch;
+  const int64_t S = (int64_t)grid * grid, T = S + 1;
+  const int hd = dim / heads, per = window * window, wpr = grid / window;
+  const int64_t m = (int64_t)batch * T;
+  std::vector<uint16_t> tok((size_t)(batch * S * dim));
+  so_patch_embed(image, batch, image_size, image_size, patch_w, patch_b, patch, dim, tok.data());
+  std::vector<uint16_t> x((size_t)(m * dim));
+  for (int b = 0; b < batch; ++b) {
+    uint16_t* row = &x[(size_t)(b * T) * dim];
+    for (int c = 0; c < dim; ++c)
+      row[c] = f2h((cls_token ? h2f(cls_token[c]) : 0.f) + h2f(pos_embed[c]));
+    for (int64_t g = 0; g < S; ++g) {
+      const int gy = (int)(g / grid), gx = (int)(g % grid);
+      uint16_t* r = &x[(size_t)(b * T + 1 + g) * dim];
+      const uint16_t* t = &tok[(size_t)(b * S + g) * dim];
+      for (int c = 0; c < dim; ++c)
+        r[c] = f2h(h2f(t[c]) + upsampled_pos(pos_embed + dim, pos_grid, grid, gy, gx, c, dim));
+    }
+  }
+  // RoPE rows per token of an image: identity for the class token
+  std::vector<float> table((size_t)(T * hd));
+  for (int j = 0; j < hd / 2; ++j) {
+    table[2 * j] = 1.f;
+    table[2 * j + 1] = 0.f;
+  }
+  so_rope_table(grid, grid, hd, rope_theta, table.data() + hd);
+  std::vector<uint16_t> ln((size_t)(m * dim)), qkv((size_t)(m * 3 * dim)), att((size_t)(m * dim));
+  std::vector<uint16_t> wq((size_t)per * 3 * dim), wo((size_t)per * dim);
+  const int stride = std::max(1, num_blocks / 4);
+  const float scale = 1.0f / std::sqrt((float)hd);
+  for (int blk = 0; blk < num_blocks; ++blk) {
+    const so_block_weights_t* w = &blocks[blk];
+    const int64_t hidden = w->fc1.n;
+    so_layernorm(x.data(), m, dim, w->ln1_gamma, w->ln1_beta, ln_eps, ln.data());
+    so_linear(ln.data(), m, w->qkv.idx, w->qkv.palette, w->qkv.bias, 3LL * dim, dim,
+              SO_EPI_BIAS_ROPE_QKV, nullptr, table.data(), T, heads, hd, qkv.data());
+    if (blk % stride == stride - 1) {
+      so_attention(qkv.data(), batch, T, heads, hd, scale, att.data());
+    } else {
+      for (int b = 0; b < batch; ++b) {
+        std::fill(att.begin() + (size_t)(b * T) * dim, att.begin() + (size_t)(b * T + 1) * dim, 0);
+        for (int wi = 0; wi < wpr * wpr; ++wi) {
+          const int wy = wi / wpr, wx = wi % wpr;
+          for (int r = 0; r < per; ++r) {
+            const int64_t g = (int64_t)(wy * window + r / window) * grid + wx * window + r % window;
+            std::memcpy(&wq[(size_t)r * 3 * dim], &qkv[(size_t)(b * T + 1 + g) * 3 * dim],
+                        (size_t)3 * dim * 2);
+          }
+          so_attention(wq.data(), 1, per, heads, hd, scale, wo.data());
+          for (int r = 0; r < per; ++r) {
+            const int64_t g = (int64_t)(wy * window + r / window) * grid + wx * window + r % window;
+            std::memcpy(&att[(size_t)(b * T + 1 + g) * dim], &wo[(size_t)r * dim], (size_t)dim * 2);
+          }
+        }
+      }
+    }
+    so_linear(att.data(), m, w->proj.idx, w->proj.palette, w->proj.bias, dim, dim,
+              SO_EPI_BIAS_RESIDUAL, x.data(), nullptr, 1, heads, hd, x.data());
+    std::vector<uint16_t> hbuf((size_t)(m * hidden));
+    so_layernorm(x.data(), m, dim, w->ln2_gamma, w->ln2_beta, ln_eps, ln.data());
+    so_linear(ln.data(), m, w->fc1.idx, w->fc1.palette, w->fc1.bias, hidden, dim,
+              SO_EPI_BIAS_GELU, nullptr, nullptr, 1, heads, hd, hbuf.data());
+    so_linear(hbuf.data(), m, w->fc2.idx, w->fc2.palette, w->fc2.bias, dim, hidden,
+              SO_EPI_BIAS_RESIDUAL, x.data(), nullptr, 1, heads, hd, x.data());
+  }
+  for (int b = 0; b < batch; ++b)
+    std::memcpy(out + (size_t)(b * S) * dim, &x[(size_t)(b * T + 1) * dim], (size_t)(S * dim) * 2);
+}
+
 }  // extern "C"

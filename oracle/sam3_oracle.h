@@ -151,6 +151,18 @@ void so_encoder_forward(const uint16_t* image, int batch, int image_size,
                         const so_block_weights_t* blocks, uint16_t* feats,
                         int32_t* idx);
 
+/* Checkpoint-faithful SAM3 encoder: class token (NULL: zeros) + positional
+ * table [1 + pos_grid^2, dim] resized to the token grid (bilinear, half-pixel
+ * centres), blocks global at i % stride == stride - 1 (stride = max(1,
+ * num_blocks / 4)), windowed (window x window, class token excluded, zero
+ * attention output for it) otherwise; out [batch, grid^2, dim] grid order. */
+void so_windowed_encoder_forward(const uint16_t* image, int batch, int image_size, int patch,
+                                 int dim, int heads, int num_blocks, int window, int pos_grid,
+                                 float ln_eps, float rope_theta, const uint16_t* patch_w,
+                                 const uint16_t* patch_b, const uint16_t* cls_token,
+                                 const uint16_t* pos_embed, const so_block_weights_t* blocks,
+                                 uint16_t* out);
+
 /* fp16 helpers exposed for tests. */
 float so_half_to_float(uint16_t h);
 uint16_t so_float_to_half(float f);

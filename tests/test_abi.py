@@ -46,6 +46,7 @@ def test_struct_layouts(sam3):
     assert C.sizeof(sam3.BlockWeights) == 2 * 8 + 2 * 32 + 2 * 8 + 2 * 32
     assert C.sizeof(sam3.EncoderWeights) == 3 * 8 + 8
     assert C.sizeof(sam3.NeckWeights) == 4 * 8 + 2 * 4
+    assert C.sizeof(sam3.WindowedEncoderWeights) == 4 * 8 + 2 * 4 + 8 + 8
 
 
 def test_default_config_matches_benchmark_spec(sam3):

@@ -755,3 +755,67 @@ def test_encoder_full_32_blocks_properties(ctx_full, sam3, oracle):
     assert (np.diff(i1[0]) > 0).all() and i1.min() >= 0 and i1.max() < 5184
     assert np.isfinite(f1.astype(np.float32)).all()
     assert np.array_equal(i1, i2) and np.array_equal(f1.view(np.uint16), f2.view(np.uint16))
+
+
+# ------------------------------------------------------------------ windowed encoder variant
+def _windowed_setup(ctx, sam3, oracle, seed, dim, hidden, nblocks, pos_grid, image, batch,
+                    window=None, with_cls=True):
+    blocks = [oracle.SyntheticBlock(seed, i, dim, hidden) for i in range(nblocks)]
+    pw = oracle.gen_normal(seed, 900, (dim, 3, 14, 14), 0.0, 0.02)
+    pb = oracle.gen_normal(seed, 901, (dim,), 0.0, 0.02)
+    cls = oracle.gen_normal(seed, 902, (dim,), 0.0, 0.5) if with_cls else None
+    pos = oracle.gen_normal(seed, 903, (1 + pos_grid * pos_grid, dim), 0.0, 0.5)
+    img = oracle.gen_uniform(seed, 904, (batch, image, image, 3), -1.0, 1.0)
+    w = sam3.windowed_encoder_weights(ctx.upload(pw), ctx.upload(pb),
+                                      None if cls is None else ctx.upload(cls), ctx.upload(pos),
+                                      pos_grid, [upload_block(ctx, sam3, b) for b in blocks],
+                                      window=window)
+    return blocks, pw, pb, cls, pos, img, w
+
+
+@pytest.mark.parametrize("pos_grid,window,with_cls", [(4, None, True), (3, 2, False), (4, 8, True)])
+def test_windowed_encoder_small_matches_oracle(ctx, sam3, oracle, pos_grid, window, with_cls):
+    # 8x8 token grid, 8 blocks (1, 3, 5, 7 global), batch 2: 4x4 windows from a
+    # 4x4 position table; 2x2 windows from a 3x3 table without class token;
+    # one 8x8 window (windowed blocks see every patch token but not the class
+    # token)
+    blocks, pw, pb, cls, pos, img, w = _windowed_setup(ctx, sam3, oracle, 71, 256, 512, 8,
+                                                       pos_grid, 112, 2, window, with_cls)
+    out = ctx.alloc(2 * 64 * 256 * 2)
+    ctx.windowed_encoder_forward(ctx.upload(img), 2, w, out)
+    ctx.sync()
+    got = ctx.download(out, (2, 64, 256), F16)
+    ref = oracle.windowed_encoder_forward(img, blocks, pw, pb, cls, pos, heads=4, window=window)
+    assert max_rel_err(got, ref) < SPEC_TOL
+    # the second image does not depend on the first (per-image windows)
+    out1 = ctx.alloc(64 * 256 * 2)
+    ctx.windowed_encoder_forward(ctx.upload(np.ascontiguousarray(img[1:])), 1, w, out1)
+    ctx.sync()
+    one = ctx.download(out1, (1, 64, 256), F16)
+    assert max_rel_err(one[0], got[1]) < 1e-3
+
+
+def test_windowed_encoder_rejects_bad_windows(ctx, sam3, oracle):
+    _, _, _, _, _, img, w = _windowed_setup(ctx, sam3, oracle, 72, 256, 512, 2, 3, 112, 1,
+                                            window=3)
+    out = ctx.alloc(64 * 256 * 2)
+    with pytest.raises(sam3.SAM3Error):  # 3 does not divide the 8-token grid
+        ctx.windowed_encoder_forward(ctx.upload(img), 1, w, out)
+    w.window = 4
+    with pytest.raises(sam3.SAM3Error):  # batch above max_batch
+        ctx.windowed_encoder_forward(ctx.alloc(3 * 112 * 112 * 3 * 2), 3, w, out)
+
+
+def test_windowed_encoder_full_size_matches_oracle(sam3, oracle):
+    # 1008^2 image, dim 1024, 16 heads, 4096 hidden, 24x24 position table ->
+    # 72x72 grid in nine 24x24 windows; 8 blocks, 1, 3, 5, 7 global (5185 rows)
+    with sam3.Context(0, max_batch=1) as ctx:
+        blocks, pw, pb, cls, pos, img, w = _windowed_setup(ctx, sam3, oracle, 73, 1024, 4096, 8,
+                                                           24, 1008, 1)
+        out = ctx.alloc(5184 * 1024 * 2)
+        ctx.windowed_encoder_forward(ctx.upload(img), 1, w, out)
+        ctx.sync()
+        got = ctx.download(out, (1, 5184, 1024), F16)
+    ref = oracle.windowed_encoder_forward(img, blocks, pw, pb, cls, pos)
+    assert np.isfinite(got.astype(np.float32)).all()
+    assert max_rel_err(got, ref) < SPEC_TOL

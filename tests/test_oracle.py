@@ -220,3 +220,97 @@ def test_neck_matches_float64_convolution(oracle):
     ref = _conv_neck_f64(x, batch, h, w, w1, b1, w2, b2)
     assert got.shape == (batch, h, w, dout)
     assert max_rel_err(got, ref) < 2e-3
+
+
+# ------------------------------------------------------------------ windowed encoder variant
+def _bilinear_weights(n_out, n_in):
+    # half-pixel centres, source clamped at 0 and at n_in - 1 (float64)
+    w = np.zeros((n_out, n_in))
+    for i in range(n_out):
+        s = max((i + 0.5) * n_in / n_out - 0.5, 0.0)
+        i0 = min(int(np.floor(s)), n_in - 1)
+        i1 = min(i0 + 1, n_in - 1)
+        f = s - i0
+        w[i, i0] += 1.0 - f
+        w[i, i1] += f
+    return w
+
+
+def _windowed_inputs(oracle, seed, dim, hidden, nblocks, pos_grid, image=112, batch=1):
+    blocks = [oracle.SyntheticBlock(seed, i, dim, hidden) for i in range(nblocks)]
+    pw = oracle.gen_normal(seed, 900, (dim, 3, 14, 14), 0.0, 0.02)
+    pb = oracle.gen_normal(seed, 901, (dim,), 0.0, 0.02)
+    cls = oracle.gen_normal(seed, 902, (dim,), 0.0, 0.5)
+    pos = oracle.gen_normal(seed, 903, (1 + pos_grid * pos_grid, dim), 0.0, 0.5)
+    img = oracle.gen_uniform(seed, 904, (batch, image, image, 3), -1.0, 1.0)
+    return blocks, pw, pb, cls, pos, img
+
+
+def test_windowed_encoder_embedding_matches_float64_resize(oracle):
+    # no blocks: out = fp16(patch token + fp16(bilinear resize of the grid
+    # positions)); the resize against a float64 separable restatement
+    dim, grid, pg = 64, 8, 3
+    _, pw, pb, cls, pos, img = _windowed_inputs(oracle, 61, dim, 128, 0, pg, batch=2)
+    out = oracle.windowed_encoder_forward(img, [], pw, pb, cls, pos, heads=1, window=4)
+    tok = oracle.patch_embed(img, pw, pb).astype(np.float64).reshape(2, grid * grid, dim)
+    wy = _bilinear_weights(grid, pg)
+    up = np.einsum("yi,xj,ijc->yxc", wy, wy, pos[1:].astype(np.float64).reshape(pg, pg, dim))
+    up16 = up.reshape(grid * grid, dim).astype(np.float16).astype(np.float64)
+    ref = (tok + up16[None]).astype(np.float16)
+    assert out.shape == (2, grid * grid, dim)
+    assert f16_ulps(out, ref) <= 1
+    # pos_grid == grid: the resize is the identity, the sum exact
+    pos8 = oracle.gen_normal(62, 1, (1 + grid * grid, dim), 0.0, 0.5)
+    out8 = oracle.windowed_encoder_forward(img, [], pw, pb, None, pos8, heads=1, window=4)
+    ref8 = (tok + pos8[1:].astype(np.float64)[None]).astype(np.float16)
+    assert np.array_equal(out8.view(np.uint16), ref8.view(np.uint16))
+
+
+def test_windowed_encoder_matches_window_partition_composition(oracle):
+    # 8 blocks on an 8x8 grid with 4x4 windows: blocks 1, 3, 5, 7 global, the
+    # others windowed. Independent composition from the oracle's operators with
+    # the reference's reshape/transpose window partition; bit-identical.
+    dim, heads, hidden, nb, pg, grid = 128, 2, 256, 8, 4, 8
+    blocks, pw, pb, cls, pos, img = _windowed_inputs(oracle, 63, dim, hidden, nb, pg)
+    got = oracle.windowed_encoder_forward(img, blocks, pw, pb, cls, pos, heads=heads)
+
+    S, T, win = grid * grid, grid * grid + 1, pg
+    zero = oracle.windowed_encoder_forward(img, [], pw, pb, cls, pos, heads=heads)[0]
+    x = np.concatenate([(cls.astype(np.float32) + pos[0].astype(np.float32)).astype(np.float16)[None],
+                        zero], axis=0)
+    table = np.concatenate([np.stack([np.ones(32), np.zeros(32)], -1)[None].astype(np.float32),
+                            oracle.rope_table(grid, grid)], axis=0)
+    stride = max(1, nb // 4)
+    global_blocks = set(range(stride - 1, nb, stride))
+    assert global_blocks == {1, 3, 5, 7}
+    P = grid // win
+
+    def partition(a):  # [S, C] grid order -> [P*P*win*win, C] window-major
+        c = a.shape[-1]
+        return a.reshape(P, win, P, win, c).transpose(0, 2, 1, 3, 4).reshape(S, c)
+
+    def reverse(a):
+        c = a.shape[-1]
+        return a.reshape(P, P, win, win, c).transpose(0, 2, 1, 3, 4).reshape(S, c)
+
+    for i, blk in enumerate(blocks):
+        ln = oracle.layernorm(x)
+        qkv = oracle.linear(ln, **_lin(blk.qkv), epilogue=oracle.EPI_BIAS_ROPE_QKV, rope=table,
+                            rope_period=T, heads=heads)
+        if i in global_blocks:
+            att = oracle.attention(qkv, 1, T, heads, 64)
+        else:
+            wins = oracle.attention(partition(qkv[1:]), P * P, win * win, heads, 64)
+            att = np.concatenate([np.zeros((1, dim), np.float16), reverse(wins)], axis=0)
+        x = oracle.linear(att, **_lin(blk.proj), epilogue=oracle.EPI_BIAS_RESIDUAL, residual=x,
+                          heads=heads)
+        h = oracle.linear(oracle.layernorm(x), **_lin(blk.fc1), epilogue=oracle.EPI_BIAS_GELU,
+                          heads=heads)
+        x = oracle.linear(h, **_lin(blk.fc2), epilogue=oracle.EPI_BIAS_RESIDUAL, residual=x,
+                          heads=heads)
+    assert got.shape == (1, S, dim)
+    assert np.array_equal(got[0].view(np.uint16), x[1:].view(np.uint16))
+
+
+def _lin(d):
+    return {"idx": d["idx"], "palette": d["palette"], "bias": d["bias"]}
