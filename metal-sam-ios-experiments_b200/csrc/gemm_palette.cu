@@ -743,7 +743,8 @@ static_assert(WSC_SMEM_BYTES <= 232448, "shared memory budget");
 struct WscArgs {
   GemmArgs g;
   const uint8_t* idx;
-  int chunks;   // K / 512
+  int chunks;   // ceil(K / 512); the last chunk may hold fewer k-blocks
+  int kblocks;  // K / 64 (even)
   int m_tiles;  // 256-row pair tiles
   int groups;   // ceil(m_tiles / 2)
   int n_tiles;  // n / 128
@@ -818,7 +819,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(WS_THREADS, 1)
         for (int c = 0; c < chunks && ok; ++c)
           for (int t = 0; t < WSC_GROUP && ok; ++t) {
             const int row = (g * WSC_GROUP + t) * 2 * WS_BM + (int)rank * WS_BM;
-            for (int ks = 0; ks < WSC_KB_PER_CHUNK / WS_KSPLIT; ++ks) {
+            const int steps = min(WSC_KB_PER_CHUNK, wa.kblocks - c * WSC_KB_PER_CHUNK) / WS_KSPLIT;
+            for (int ks = 0; ks < steps; ++ks) {
               if (!mbar_wait_cluster(bar_a_empty + 8 * s, ph ^ 1, abort_flag, args.err,
                                      kDevErrTimeoutProducer)) {
                 ok = false;
@@ -862,9 +864,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(WS_THREADS, 1)
             break;
           }
           tc_fence_after();
+          const int steps = min(WSC_KB_PER_CHUNK, wa.kblocks - c * WSC_KB_PER_CHUNK) / WS_KSPLIT;
           for (int t = 0; t < WSC_GROUP && ok; ++t) {
             const uint32_t d_tmem = tmem + (uint32_t)((2 * gp + t) * WS_ACC_COLS);
-            for (int ks = 0; ks < WSC_KB_PER_CHUNK / WS_KSPLIT; ++ks) {
+            for (int ks = 0; ks < steps; ++ks) {
               if (!mbar_wait_cluster(bar_a_full + 8 * s, ph, abort_flag, args.err,
                                      kDevErrTimeoutMma)) {
                 ok = false;
@@ -985,9 +988,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(WS_THREADS, 1)
                                             abort_flag, args.err, kDevErrTimeoutDequant));
           if (!ok) break;
         }
-        const int k0 = c * WSC_KC + exp_q * (WSC_KC / 4);
-        ws_expand_range<WSC_KC / 4 / 16>(irow, pal, smem + WSC_OFF_SLAB + b * WSC_BUF, exp_row,
-                                         k0, c * WSC_KC);
+        const int kb_c = min(WSC_KB_PER_CHUNK, wa.kblocks - c * WSC_KB_PER_CHUNK);
+        if (kb_c == WSC_KB_PER_CHUNK) {
+          ws_expand_range<WSC_KC / 4 / 16>(irow, pal, smem + WSC_OFF_SLAB + b * WSC_BUF, exp_row,
+                                           c * WSC_KC + exp_q * (WSC_KC / 4), c * WSC_KC);
+        } else {  // short last chunk: kb_c * 16 indices per quarter, 32 at a time
+          const int k0 = c * WSC_KC + exp_q * kb_c * 16;
+          for (int k = k0; k < k0 + kb_c * 16; k += 32)
+            ws_expand_range<2>(irow, pal, smem + WSC_OFF_SLAB + b * WSC_BUF, exp_row, k,
+                               c * WSC_KC);
+        }
         fence_proxy_async_smem();
         mbar_arrive_cluster(mapa_shared(bar_slab_full + 8 * b, 0));
         if (c == 0 && pend_it >= 0) {
@@ -1204,12 +1214,14 @@ sam3_status_t gemm_palette(sam3_ctx_t* ctx, const uint16_t* x, int m, int k, con
     wa.a3d = make_map_a3d(&ma3, x, k, m) ? 1 : 0;
     return launch_ws(ctx, wa.a3d ? ma3 : ma, wa);
   }
-  if (k % WSC_KC == 0 && n / (2 * WS_BN) <= ctx->num_sms / 2) {
-    // chunked weight-stationary pair kernel
+  if (k % (WS_KSPLIT * WS_BK) == 0 && n / (2 * WS_BN) <= ctx->num_sms / 2) {
+    // chunked weight-stationary pair kernel (K > 1024; 512-wide chunks, the
+    // last one shorter when K % 512 != 0)
     WscArgs wa;
     wa.g = a;
     wa.idx = idx;
-    wa.chunks = k / WSC_KC;
+    wa.kblocks = k / WS_BK;
+    wa.chunks = (k + WSC_KC - 1) / WSC_KC;
     wa.m_tiles = (m + 2 * WS_BM - 1) / (2 * WS_BM);
     wa.groups = (wa.m_tiles + WSC_GROUP - 1) / WSC_GROUP;
     wa.n_tiles = n / (2 * WS_BN);

@@ -52,6 +52,7 @@ def main():
     ap.add_argument("--batch", type=int, default=8)
     ap.add_argument("--seq", type=int, default=5184)
     ap.add_argument("--heads", type=int, default=16)
+    ap.add_argument("--hidden", type=int, default=4096, help="windowed: MLP width (checkpoint 4736)")
     ap.add_argument("--iters", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     a = ap.parse_args()
@@ -141,8 +142,8 @@ def main():
         return
     elif a.op == "windowed":
         ctx.close()
-        ctx = sam3.Context(0, max_batch=a.batch)
-        dim, hidden, nblocks, pg, size = 1024, 4096, 32, 24, 1008
+        ctx = sam3.Context(0, max_batch=a.batch, mlp_hidden=a.hidden)
+        dim, hidden, nblocks, pg, size = 1024, a.hidden, 32, 24, 1008
         keep = []
 
         def t(x):
@@ -184,7 +185,7 @@ def main():
         flops = a.batch * (nblocks * 2.0 * T * dim * (4 * dim + 2 * hidden)
                            + 24 * win_att + 8 * glob_att)
         print(json.dumps({
-            "op": "windowed", "batch": a.batch, "ms_per_call": ms, "images_per_s": a.batch / (ms * 1e-3),
+            "op": "windowed", "batch": a.batch, "hidden": hidden, "ms_per_call": ms, "images_per_s": a.batch / (ms * 1e-3),
             "tflops": flops / (ms * 1e-3) / 1e12,
             "classes_ms_per_call": {k: v["ms"] / a.iters for k, v in prof.items() if v["launches"]},
             "gemm_tflops": prof["gemm"]["flops"] / (prof["gemm"]["ms"] * 1e-3) / 1e12,

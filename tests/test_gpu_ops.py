@@ -103,6 +103,21 @@ def test_linear_ragged_rows(ctx, sam3, oracle, m):
     assert max_rel_err(y, ref) < 2e-3
 
 
+@pytest.mark.parametrize("m,n,k", [(5185, 1024, 4736), (300, 256, 1152), (512, 256, 1536)])
+def test_linear_k_chunks_with_short_tail(ctx, sam3, oracle, m, n, k):
+    # K > 1024 in 512-wide chunks, the last one shorter (K % 512 = 128, 128)
+    # or whole (1536): the fc2 shape of the checkpoint (hidden 4736) over one
+    # image with a class token, and ragged rows
+    x = oracle.gen_normal(8, k, (m, k))
+    idx = oracle.gen_u8(8, 2, (n, k))
+    pal = oracle.gen_palette(8, 3, n)
+    bias = oracle.gen_normal(8, 4, (n,), 0.0, 0.01)
+    res = oracle.gen_normal(8, 5, (m, n))
+    y = run_linear(ctx, sam3, x, idx, pal, bias, sam3.EPI_BIAS_RESIDUAL, residual=res)
+    ref = oracle.linear(x, idx, pal, bias, epilogue=oracle.EPI_BIAS_RESIDUAL, residual=res)
+    assert max_rel_err(y, ref) < 2e-3
+
+
 def test_linear_many_tiles_gelu_and_rope(ctx, sam3, oracle):
     # more tiles than SMs, several n-tiles per CTA (palette reloads), K=4096
     m = 1000
@@ -806,11 +821,13 @@ def test_windowed_encoder_rejects_bad_windows(ctx, sam3, oracle):
         ctx.windowed_encoder_forward(ctx.alloc(3 * 112 * 112 * 3 * 2), 3, w, out)
 
 
-def test_windowed_encoder_full_size_matches_oracle(sam3, oracle):
-    # 1008^2 image, dim 1024, 16 heads, 4096 hidden, 24x24 position table ->
-    # 72x72 grid in nine 24x24 windows; 8 blocks, 1, 3, 5, 7 global (5185 rows)
-    with sam3.Context(0, max_batch=1) as ctx:
-        blocks, pw, pb, cls, pos, img, w = _windowed_setup(ctx, sam3, oracle, 73, 1024, 4096, 8,
+@pytest.mark.parametrize("hidden", [4096, 4736])
+def test_windowed_encoder_full_size_matches_oracle(sam3, oracle, hidden):
+    # 1008^2 image, dim 1024, 16 heads, 24x24 position table -> 72x72 grid in
+    # nine 24x24 windows; 8 blocks, 1, 3, 5, 7 global (5185 rows); MLP hidden
+    # 4096 (benchmark) or 4736 (the checkpoint's)
+    with sam3.Context(0, max_batch=1, mlp_hidden=hidden) as ctx:
+        blocks, pw, pb, cls, pos, img, w = _windowed_setup(ctx, sam3, oracle, 73, 1024, hidden, 8,
                                                            24, 1008, 1)
         out = ctx.alloc(5184 * 1024 * 2)
         ctx.windowed_encoder_forward(ctx.upload(img), 1, w, out)
