@@ -147,10 +147,12 @@ __global__ void __launch_bounds__(THREADS, 2)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  griddep_launch_dependents();
 
   if (warp == 0) {
     // ------------------------------------------------------------- producer
     if (lane == 0) {
+      griddep_wait();  // Q/K/V are the previous kernel's output
       uint32_t issued = 0, issued_par = 0;
       mbar_arrive_expect_tx(bar_q, Q_BYTES);
       tma_load_2d(sbase + OFF_Q, &tmap_qkv, bar_q, h * HD, row0 + q0);
@@ -244,6 +246,7 @@ __global__ void __launch_bounds__(THREADS, 2)
     const float c = args.scale_log2;
     float m_run = -INFINITY;
     bool ok = true;
+    griddep_wait();  // before this grid's output rows are written
     for (int j = 0; j < ntiles && ok; ++j) {
       ok = __all_sync(0xffffffffu, mbar_wait(bar_s_full + 8 * (j & 1), (uint32_t)(j >> 1) & 1u,
                                              abort_flag, args.err, kDevErrTimeoutAttn));
@@ -387,8 +390,9 @@ sam3_status_t attention_tc(sam3_ctx_t* ctx, const uint16_t* qkv, int batch, int 
   a.scale_log2 = scale * 1.4426950408889634f;
   a.kv3d = kv3d ? 1 : 0;
   dim3 grid((seq + BQ - 1) / BQ, heads, batch * groups);
-  attn_tc_kernel<<<grid, THREADS, SMEM_BYTES, ctx->stream>>>(map, kv3d ? map_kv : map, a);
-  return check_launch(ctx, "attn_tc_kernel");
+  const cudaError_t e = launch_pdl(attn_tc_kernel, grid, dim3(THREADS), SMEM_BYTES, ctx->stream,
+                                   map, kv3d ? map_kv : map, a);
+  return check_launch_ret(ctx, e, "attn_tc_kernel");
 }
 
 }  // namespace sam3

@@ -103,6 +103,17 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
+// Programmatic dependent launch. launch_dependents lets the next kernel in
+// the stream (launched with launch_pdl) start its CTAs once every CTA of this
+// grid has executed it; wait blocks until the grids this one depends on have
+// completed and their memory is visible (immediately when launched normally).
+// Every thread that touches activations written by an earlier kernel runs
+// griddep_wait first.
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }

@@ -40,6 +40,12 @@ sam3_status_t check_launch(sam3_ctx_t* ctx, const char* what) {
   return check_cuda(ctx, cudaGetLastError(), what);
 }
 
+sam3_status_t check_launch_ret(sam3_ctx_t* ctx, cudaError_t e, const char* what) {
+  const cudaError_t last = cudaGetLastError();  // clears a launch error recorded twice
+  ctx->launches++;
+  return check_cuda(ctx, e != cudaSuccess ? e : last, what);
+}
+
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 EncodeTiledFn encode_tiled() {

@@ -538,6 +538,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(WS_THREADS, 1)
   cluster_sync_all();  // both CTAs' barriers initialised before any remote arrive
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  griddep_launch_dependents();
 
   const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
   const int kblocks = wa.kblocks;
@@ -545,6 +546,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(WS_THREADS, 1)
   if (warp == 0) {
     // ------------------------------------------------------------- producer
     if (lane == 0) {
+      griddep_wait();  // X is the previous kernel's output
       const uint64_t policy = l2_policy_evict_last();
       int s = 0;
       uint32_t ph = 0, gen = 0;
@@ -644,7 +646,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(WS_THREADS, 1)
     const int colhalf = ew >> 2;                 // accumulator columns [64*colhalf, +64)
     uint32_t sync_ph = 0;
     int cur_n = -1, it = 0;
-    bool ok = true;
+    bool ok = true, dep_waited = false;
     int n_tile, m_tile;
     for (int k = 0; ok && ws_unit(wa, pair, npairs, k, n_tile, m_tile); ++k, ++it) {
       if (n_tile != cur_n) {
@@ -673,7 +675,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(WS_THREADS, 1)
         if (!ok) break;
         const int kq = args.k / 4;
         const uint8_t* irow = wa.idx + (size_t)wrow * args.k;
-        for (int k = exp_q * kq; k < (exp_q + 1) * kq; k += 32)
+        // 128 indices per batch of loads (one L2 round trip), 32 for the rest
+        int k = exp_q * kq;
+        for (; k + 128 <= (exp_q + 1) * kq; k += 128)
+          ws_expand_range<8>(irow, pal, smem + WS_OFF_SLAB, exp_row, k, 0);
+        for (; k < (exp_q + 1) * kq; k += 32)
           ws_expand_range<2>(irow, pal, smem + WS_OFF_SLAB, exp_row, k, 0);
         fence_proxy_async_smem();
         mbar_arrive(bar_slab_local);
@@ -687,6 +693,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(WS_THREADS, 1)
       const uint32_t use = (uint32_t)(it / WS_NUM_ACC) & 1u;
       const int row = m_tile * 2 * WS_BM + (int)rank * WS_BM + quad * 32 + lane;
       const int col0 = n_tile * 2 * WS_BN + colhalf * 64;
+      if (!dep_waited) {  // the slab is weights only; the residual is not
+        griddep_wait();
+        dep_waited = true;
+      }
       epilogue_prefetch(args, row, col0);
       ok = __all_sync(0xffffffffu, mbar_wait_cluster(bar_tfull + 8 * acc, use, abort_flag,
                                                      args.err, kDevErrTimeoutEpilogue));
@@ -800,6 +810,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(WS_THREADS, 1)
   cluster_sync_all();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  griddep_launch_dependents();
 
   // Pair p owns N tile p % n_tiles and M groups p / n_tiles + k * sets: the
   // n_tiles pairs of a set sweep the same A groups together (one DRAM read,
@@ -811,6 +822,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(WS_THREADS, 1)
   if (warp == 0) {
     // ------------------------------------------------------------- producer
     if (lane == 0) {
+      griddep_wait();  // X is the previous kernel's output
       const uint64_t policy = l2_policy_evict_last();
       int s = 0;
       uint32_t ph = 0;
@@ -914,7 +926,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(WS_THREADS, 1)
     uint32_t pal_ph = 0;
     int cur_n = -1, it = 0, q = 0;
     int pend_it = -1, pend_g = -1;  // group whose epilogue is still to do
-    bool ok = true;
+    bool ok = true, dep_waited = false;
     // Epilogue of a group: per M tile, its 64 columns of this row go from
     // tensor memory to registers (the accumulator pair is handed back to the
     // MMA issuer as soon as the last tile's values are out), then the math
@@ -923,6 +935,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(WS_THREADS, 1)
       const int gp = e_it & 1;
       const int col0 = my_n * 2 * WS_BN + colhalf * 64;
       const int row0 = g * WSC_GROUP * 2 * WS_BM + (int)rank * WS_BM + quad * 32 + lane;
+      if (!dep_waited) {  // the slab chunks are weights only; the residual is not
+        griddep_wait();
+        dep_waited = true;
+      }
 #pragma unroll
       for (int t = 0; t < WSC_GROUP; ++t) epilogue_prefetch(args, row0 + t * 2 * WS_BM, col0);
       const bool w = __all_sync(0xffffffffu,
@@ -1100,8 +1116,9 @@ sam3_status_t launch_ws(sam3_ctx_t* ctx, const CUtensorMap& ma, const WsArgs& wa
   const int max_pairs = ctx->num_sms / 2;
   const int pairs = wa.sets > 0 ? wa.sets * wa.n_tiles
                                 : (wa.units < max_pairs ? wa.units : max_pairs);
-  gemm_ws_kernel<<<2 * pairs, WS_THREADS, WS_SMEM_BYTES, ctx->stream>>>(ma, wa);
-  return check_launch(ctx, "gemm_ws_kernel");
+  return check_launch_ret(ctx, launch_pdl(gemm_ws_kernel, dim3(2 * pairs), dim3(WS_THREADS),
+                                         WS_SMEM_BYTES, ctx->stream, ma, wa),
+                          "gemm_ws_kernel");
 }
 
 sam3_status_t launch_wsc(sam3_ctx_t* ctx, const CUtensorMap& ma, const WscArgs& wa) {
@@ -1113,8 +1130,9 @@ sam3_status_t launch_wsc(sam3_ctx_t* ctx, const CUtensorMap& ma, const WscArgs& 
     attr_set = true;
   }
   const int pairs = wa.sets * wa.n_tiles;
-  gemm_wsc_kernel<<<2 * pairs, WS_THREADS, WSC_SMEM_BYTES, ctx->stream>>>(ma, wa);
-  return check_launch(ctx, "gemm_wsc_kernel");
+  return check_launch_ret(ctx, launch_pdl(gemm_wsc_kernel, dim3(2 * pairs), dim3(WS_THREADS),
+                                         WSC_SMEM_BYTES, ctx->stream, ma, wa),
+                          "gemm_wsc_kernel");
 }
 
 template <int MODE>

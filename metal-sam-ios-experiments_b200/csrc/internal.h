@@ -63,6 +63,8 @@ namespace sam3 {
 
 sam3_status_t set_error(sam3_ctx_t* ctx, sam3_status_t code, const char* fmt, ...);
 sam3_status_t check_launch(sam3_ctx_t* ctx, const char* what);
+// For launches that return their error (cudaLaunchKernelEx).
+sam3_status_t check_launch_ret(sam3_ctx_t* ctx, cudaError_t e, const char* what);
 sam3_status_t check_cuda(sam3_ctx_t* ctx, cudaError_t e, const char* what);
 sam3_status_t ensure_workspace(sam3_ctx_t* ctx);
 bool aligned16(const void* p);
@@ -100,6 +102,26 @@ sam3_status_t prune(sam3_ctx_t* ctx, const uint16_t* x, int batch, int seq, int 
 sam3_status_t patch_embed(sam3_ctx_t* ctx, const void* image, bool rgba, int batch, int h, int w,
                           const uint16_t* pw, const uint16_t* pb, int patch, int dim,
                           uint16_t* out, uint16_t* cols_scratch, uint16_t* wpad_scratch);
+
+// Launch with programmatic stream serialization: the kernel may start while
+// the previous kernel in the stream finishes (its prologue overlapping that
+// kernel's tail) and must call griddep_wait before touching that kernel's
+// outputs (or any buffer a preceding kernel reads or writes).
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                       cudaStream_t stream, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
 
 // Brackets one launch with CUDA events when the context is profiling.
 class ProfScope {

@@ -27,6 +27,8 @@ __global__ void __launch_bounds__(256) layernorm_kernel(const __half* __restrict
                                                         const __half* __restrict__ b, float eps,
                                                         __half* __restrict__ y) {
   constexpr int D = NCH * 256;
+  griddep_launch_dependents();
+  griddep_wait();  // x is the previous kernel's output
   const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= m) return;
@@ -385,18 +387,21 @@ sam3_status_t layernorm(sam3_ctx_t* ctx, const uint16_t* x, int m, int d, const 
   __half* hy = reinterpret_cast<__half*>(y);
   const int grid = blocks_for(m, 8);
   ProfScope prof(ctx, SAM3_PROF_LAYERNORM, 0.0, 4.0 * m * d);
+  void (*kern)(const __half*, int, const __half*, const __half*, float, __half*) = nullptr;
   switch (d) {
-    case 256: layernorm_kernel<1><<<grid, 256, 0, ctx->stream>>>(hx, m, hg, hb, eps, hy); break;
-    case 512: layernorm_kernel<2><<<grid, 256, 0, ctx->stream>>>(hx, m, hg, hb, eps, hy); break;
-    case 768: layernorm_kernel<3><<<grid, 256, 0, ctx->stream>>>(hx, m, hg, hb, eps, hy); break;
-    case 1024: layernorm_kernel<4><<<grid, 256, 0, ctx->stream>>>(hx, m, hg, hb, eps, hy); break;
-    case 1280: layernorm_kernel<5><<<grid, 256, 0, ctx->stream>>>(hx, m, hg, hb, eps, hy); break;
-    case 1536: layernorm_kernel<6><<<grid, 256, 0, ctx->stream>>>(hx, m, hg, hb, eps, hy); break;
-    case 2048: layernorm_kernel<8><<<grid, 256, 0, ctx->stream>>>(hx, m, hg, hb, eps, hy); break;
+    case 256: kern = layernorm_kernel<1>; break;
+    case 512: kern = layernorm_kernel<2>; break;
+    case 768: kern = layernorm_kernel<3>; break;
+    case 1024: kern = layernorm_kernel<4>; break;
+    case 1280: kern = layernorm_kernel<5>; break;
+    case 1536: kern = layernorm_kernel<6>; break;
+    case 2048: kern = layernorm_kernel<8>; break;
     default:
       return set_error(ctx, SAM3_ERR_SHAPE, "layernorm: d=%d unsupported (256..2048, step 256)", d);
   }
-  return check_launch(ctx, "layernorm_kernel");
+  return check_launch_ret(ctx, launch_pdl(kern, dim3(grid), dim3(256), 0, ctx->stream, hx, m, hg,
+                                          hb, eps, hy),
+                          "layernorm_kernel");
 }
 
 sam3_status_t rope_table(sam3_ctx_t* ctx, int gh, int gw, int hd, float theta, float* t) {

@@ -40,8 +40,13 @@ CODE_DTYPES = {v: k for k, v in DTYPE_CODES.items()}
 PALETTE_SUFFIX = ".palette"
 PALETTE_SIZE = 256
 
-# Linear weights of the encoder blocks (ViTEncoder.swift:693-721).
-LINEAR_KEY = re.compile(r"^blocks\.\d+\.(attn\.qkv|attn\.proj|mlp\.lin1|mlp\.lin2)\.weight$")
+# Linear weights of the encoder blocks: ViTEncoder's keys (ViTEncoder.swift:
+# 693-721) and the checkpoint's, under the trunk prefix with mlp.fc1 / mlp.fc2
+# (WeightMapper.swift:42-77).
+TRUNK = "backbone.vision_backbone.trunk"
+NECK = "backbone.vision_backbone.convs.3"
+LINEAR_KEY = re.compile(r"^(?:backbone\.vision_backbone\.trunk\.)?blocks\.\d+\."
+                        r"(attn\.qkv|attn\.proj|mlp\.lin1|mlp\.lin2|mlp\.fc1|mlp\.fc2)\.weight$")
 
 
 class WtsError(ValueError):
@@ -231,6 +236,74 @@ def load_encoder_weights(ctx, entries: dict, num_blocks: int, sam3):
         neck = sam3.neck_weights(ctx.upload(np.ascontiguousarray(w1.reshape(w1.shape[0], -1), np.float16)),
                                  f16("neck.0.bias"), f16("neck.2.weight"), f16("neck.2.bias"),
                                  w1.shape[1], w1.shape[0])
+    return enc, neck
+
+
+def load_windowed_encoder_weights(ctx, entries: dict, sam3, num_blocks=None, prefix=TRUNK,
+                                  window=None):
+    """Upload a palettized SAM3 checkpoint (the reference's keys,
+    WeightMapper.swift:42-110: `<trunk>.patch_embed.proj.*`, `<trunk>.cls_token`
+    (optional), `<trunk>.pos_embed` [1, 1 + g^2, dim], `<trunk>.blocks.N.norm1 /
+    attn.qkv / attn.proj / norm2 / mlp.fc1 / mlp.fc2`, neck `convs.3.conv_1x1 /
+    conv_3x3`) and return (WindowedEncoderWeights, NeckWeights or None).
+    num_blocks defaults to the number of blocks in the file; window to the
+    position grid (SAM3EncoderConfig.swift:45)."""
+
+    def f16(key):
+        a = entries.get(key)
+        return None if a is None else ctx.upload(np.ascontiguousarray(a, np.float16))
+
+    def linear(key):
+        w = entries.get(key + ".weight")
+        pal = entries.get(key + ".weight" + PALETTE_SUFFIX)
+        if w is None or pal is None or w.dtype != np.uint8:
+            raise WtsError(f"{key}.weight is not palettized (run `wts.py palettize`)")
+        n, k = w.shape
+        if pal.shape != (n, PALETTE_SIZE):
+            raise WtsError(f"{key}.weight.palette has shape {pal.shape}, expected {(n, 256)}")
+        return sam3.palette_linear(ctx.upload(np.ascontiguousarray(w)),
+                                   f16(key + ".weight" + PALETTE_SUFFIX), f16(key + ".bias"), n, k)
+
+    pw = entries.get(f"{prefix}.patch_embed.proj.weight")
+    pos = entries.get(f"{prefix}.pos_embed")
+    if pw is None or pos is None:
+        raise WtsError(f"{prefix}.patch_embed.proj.weight / {prefix}.pos_embed missing")
+    dim = pw.shape[0]
+    pos = np.ascontiguousarray(pos, np.float16).reshape(-1, dim)
+    pos_grid = int(round((pos.shape[0] - 1) ** 0.5))
+    if pos_grid * pos_grid + 1 != pos.shape[0]:
+        raise WtsError(f"{prefix}.pos_embed has {pos.shape[0]} rows, not 1 + g^2")
+    if num_blocks is None:
+        num_blocks = 0
+        while f"{prefix}.blocks.{num_blocks}.attn.qkv.weight" in entries:
+            num_blocks += 1
+
+    def ln(key):
+        g = entries.get(key + ".weight")
+        b = entries.get(key + ".bias")
+        g = np.ones(dim, np.float16) if g is None else g
+        b = np.zeros(dim, np.float16) if b is None else b
+        return (ctx.upload(np.ascontiguousarray(g, np.float16)),
+                ctx.upload(np.ascontiguousarray(b, np.float16)))
+
+    blocks = []
+    for i in range(num_blocks):
+        p = f"{prefix}.blocks.{i}"
+        g1, b1 = ln(p + ".norm1")
+        g2, b2 = ln(p + ".norm2")
+        blocks.append(sam3.block_weights(g1, b1, linear(p + ".attn.qkv"), linear(p + ".attn.proj"),
+                                         g2, b2, linear(p + ".mlp.fc1"), linear(p + ".mlp.fc2")))
+    cls = entries.get(f"{prefix}.cls_token")
+    enc = sam3.windowed_encoder_weights(
+        f16(f"{prefix}.patch_embed.proj.weight"), f16(f"{prefix}.patch_embed.proj.bias"),
+        None if cls is None else ctx.upload(np.ascontiguousarray(cls, np.float16).reshape(-1)),
+        ctx.upload(pos), pos_grid, blocks, window=window)
+    neck = None
+    if f"{NECK}.conv_1x1.weight" in entries and f"{NECK}.conv_3x3.weight" in entries:
+        w1 = entries[f"{NECK}.conv_1x1.weight"]
+        neck = sam3.neck_weights(ctx.upload(np.ascontiguousarray(w1.reshape(w1.shape[0], -1), np.float16)),
+                                 f16(f"{NECK}.conv_1x1.bias"), f16(f"{NECK}.conv_3x3.weight"),
+                                 f16(f"{NECK}.conv_3x3.bias"), w1.shape[1], w1.shape[0])
     return enc, neck
 
 

@@ -836,3 +836,59 @@ def test_windowed_encoder_full_size_matches_oracle(sam3, oracle, hidden):
     ref = oracle.windowed_encoder_forward(img, blocks, pw, pb, cls, pos)
     assert np.isfinite(got.astype(np.float32)).all()
     assert max_rel_err(got, ref) < SPEC_TOL
+
+
+def test_windowed_encoder_from_palettized_checkpoint_keys(ctx, sam3, oracle, tmp_path):
+    # a checkpoint laid out under the reference's keys (trunk prefix, mlp.fc1 /
+    # fc2, cls_token [1, 1, D], pos_embed [1, 1 + 4*4, D]) -> SAM3WTS1 ->
+    # palettize -> load_windowed_encoder_weights -> windowed encoder; the
+    # oracle runs the same palettized weights
+    import wts
+    rng = np.random.default_rng(81)
+    dim, hidden, nblocks, t = 256, 512, 4, wts.TRUNK
+
+    def dense(*shape, std=0.02):
+        return (rng.standard_normal(shape) * std).astype(F16)
+
+    src = {f"{t}.patch_embed.proj.weight": dense(dim, 3, 14, 14),
+           f"{t}.patch_embed.proj.bias": dense(dim),
+           f"{t}.cls_token": dense(1, 1, dim, std=0.5),
+           f"{t}.pos_embed": dense(1, 17, dim, std=0.5)}
+    for i in range(nblocks):
+        p = f"{t}.blocks.{i}"
+        src.update({f"{p}.norm1.weight": (1 + dense(dim, std=0.1)), f"{p}.norm1.bias": dense(dim),
+                    f"{p}.attn.qkv.weight": dense(3 * dim, dim), f"{p}.attn.qkv.bias": dense(3 * dim, std=0.01),
+                    f"{p}.attn.proj.weight": dense(dim, dim), f"{p}.attn.proj.bias": dense(dim, std=0.01),
+                    f"{p}.norm2.weight": (1 + dense(dim, std=0.1)), f"{p}.norm2.bias": dense(dim),
+                    f"{p}.mlp.fc1.weight": dense(hidden, dim), f"{p}.mlp.fc1.bias": dense(hidden, std=0.01),
+                    f"{p}.mlp.fc2.weight": dense(dim, hidden), f"{p}.mlp.fc2.bias": dense(dim, std=0.01)})
+    a, b = tmp_path / "ckpt.wts", tmp_path / "ckpt_pal.wts"
+    wts.write_wts(str(a), src)
+    assert wts.main(["palettize", "--src", str(a), "--dst", str(b), "--iters", "6"]) == 0
+    entries = wts.read_wts(str(b))
+    enc, neck = wts.load_windowed_encoder_weights(ctx, entries, sam3)
+    assert neck is None and enc.num_blocks == nblocks and enc.pos_grid == 4 and enc.window == 4
+
+    blocks = []
+    for i in range(nblocks):
+        blk = object.__new__(oracle.SyntheticBlock)
+        p = f"{t}.blocks.{i}"
+        blk.dim, blk.hidden = dim, hidden
+        blk.ln1_gamma, blk.ln1_beta = entries[f"{p}.norm1.weight"], entries[f"{p}.norm1.bias"]
+        blk.ln2_gamma, blk.ln2_beta = entries[f"{p}.norm2.weight"], entries[f"{p}.norm2.bias"]
+        for name, key in (("qkv", "attn.qkv"), ("proj", "attn.proj"), ("fc1", "mlp.fc1"),
+                          ("fc2", "mlp.fc2")):
+            setattr(blk, name, {"idx": np.ascontiguousarray(entries[f"{p}.{key}.weight"]),
+                                "palette": np.ascontiguousarray(entries[f"{p}.{key}.weight.palette"]),
+                                "bias": np.ascontiguousarray(entries[f"{p}.{key}.bias"])})
+        blocks.append(blk)
+    img = oracle.gen_uniform(82, 77, (2, 112, 112, 3), -1.0, 1.0)
+    out = ctx.alloc(2 * 64 * dim * 2)
+    ctx.windowed_encoder_forward(ctx.upload(img), 2, enc, out)
+    ctx.sync()
+    got = ctx.download(out, (2, 64, dim), F16)
+    ref = oracle.windowed_encoder_forward(img, blocks, src[f"{t}.patch_embed.proj.weight"],
+                                          src[f"{t}.patch_embed.proj.bias"],
+                                          src[f"{t}.cls_token"].reshape(-1),
+                                          src[f"{t}.pos_embed"].reshape(17, dim), heads=4)
+    assert max_rel_err(got, ref) < SPEC_TOL

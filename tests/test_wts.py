@@ -91,3 +91,21 @@ def test_palettize_entries_replaces_block_linears_only(tmp_path):
     back = wts.read_wts(str(q))
     assert set(back) == set(out)
     assert np.array_equal(back["blocks.0.attn.qkv.weight"], out["blocks.0.attn.qkv.weight"])
+
+
+def test_palettize_entries_matches_checkpoint_keys():
+    # the checkpoint's trunk prefix and mlp.fc1 / mlp.fc2 names
+    # (WeightMapper.swift:42-77); other modules' blocks stay dense
+    rng = np.random.default_rng(3)
+    t = wts.TRUNK
+    src = {f"{t}.blocks.3.mlp.fc1.weight": rng.standard_normal((8, 16)).astype(np.float16),
+           f"{t}.blocks.3.mlp.fc2.weight": rng.standard_normal((16, 8)).astype(np.float16),
+           f"{t}.blocks.3.attn.proj.weight": rng.standard_normal((16, 16)).astype(np.float16),
+           f"{t}.pos_embed": rng.standard_normal((1, 5, 16)).astype(np.float16),
+           "geometry_encoder.blocks.0.attn.qkv.weight": rng.standard_normal((6, 16)).astype(np.float16)}
+    out = wts.palettize_entries(src, iters=2)
+    for k in ("mlp.fc1", "mlp.fc2", "attn.proj"):
+        assert out[f"{t}.blocks.3.{k}.weight"].dtype == np.uint8
+        assert f"{t}.blocks.3.{k}.weight.palette" in out
+    assert out[f"{t}.pos_embed"] is src[f"{t}.pos_embed"]
+    assert out["geometry_encoder.blocks.0.attn.qkv.weight"].dtype == np.float16
