@@ -16,8 +16,10 @@ one JSON line:
   value   images/s of the whole job, device-timed (CUDA events on the library's
           stream, inputs resident in HBM), max over ranks;
   e2e     the same through the host-buffer C-ABI entry point
-          (sam3_encoder_forward_host: pinned host images in, pruned features and
-          indices out, copies inside the timed region);
+          (sam3_encoder_forward_host_pipelined over all of the rank's images:
+          pinned host images in, pruned features and indices out, every copy
+          inside the timed region, overlapped with the encoder of the
+          neighbouring call);
   roofline  the palette-dequant GEMM (dominant kernel): algorithmic FLOPs
           (2*M*N*K) / its summed CUDA-event launch time, measured in a second
           pass over the same steps with events around every launch (kept out
@@ -366,10 +368,11 @@ def run_ours(args):
     h_idx = torch.empty(idx.shape, dtype=torch.int32, pin_memory=True)
 
     def step_e2e():
-        for c0 in range(0, per_rank, batch):
-            n = min(batch, per_rank - c0)
-            ctx.encoder_forward_host(h_imgs[c0].data_ptr(), n, w, h_feats[c0].data_ptr(),
-                                     h_idx[c0].data_ptr())
+        # every image of this rank through the pipelined host entry point:
+        # uploads of the next call and downloads of the previous one overlap
+        # the encoder
+        ctx.encoder_forward_host_pipelined(h_imgs.data_ptr(), per_rank, w, h_feats.data_ptr(),
+                                           h_idx.data_ptr())
 
     step_e2e()
     barrier()

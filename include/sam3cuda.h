@@ -331,6 +331,22 @@ sam3_status_t sam3_encoder_forward_host(sam3_ctx_t* ctx, const uint16_t* host_im
                                         int32_t batch, const sam3_encoder_weights_t* w,
                                         uint16_t* host_feats, int32_t* host_idx);
 
+/* Any number of images from and to HOST buffers, in chunks of max_batch,
+ * with the copies overlapped: while the encoder runs on chunk c, a copy
+ * stream uploads chunk c+1's images and downloads chunk c-1's features and
+ * indices (double-buffered device staging, allocated on first use: about
+ * 2 x max_batch x (image + features) bytes). host_image [n_images, S, S, 3]
+ * fp16, host_feats [n_images, out_tokens, dim] fp16, host_idx
+ * [n_images, out_tokens] int32; the results equal sam3_encoder_forward_host's
+ * bit for bit. Returns when everything is on the host. Pinned host memory is
+ * needed for the copies to overlap (pageable memory works, serialised).
+ * Reference: the per-batch encode + host gather of SAM3MetalPipeline
+ * (SAM3MetalPipeline.swift:67-82), here overlapped with the next batch. */
+sam3_status_t sam3_encoder_forward_host_pipelined(sam3_ctx_t* ctx, const uint16_t* host_image,
+                                                  int32_t n_images,
+                                                  const sam3_encoder_weights_t* w,
+                                                  uint16_t* host_feats, int32_t* host_idx);
+
 /* Pruned rows back to their grid positions: out [batch, seq, dim] fp16 is
  * zero except out[b, idx[b, k], :] = pruned[b, k, :] (idx int32 [batch, keep],
  * unique per image, as sam3_prune writes them). An index outside [0, seq) is

@@ -266,6 +266,11 @@ sam3_status_t sam3_ctx_destroy(sam3_ctx_t* ctx) {
   if (ctx->stream) cudaStreamSynchronize(ctx->stream);
   resolve_profile(ctx);
   for (cudaEvent_t e : ctx->event_pool) cudaEventDestroy(e);
+  if (ctx->copy_stream) cudaStreamSynchronize(ctx->copy_stream);
+  for (cudaEvent_t e : ctx->pipe_ev)
+    if (e) cudaEventDestroy(e);
+  if (ctx->pipe_mem) cudaFree(ctx->pipe_mem);
+  if (ctx->copy_stream) cudaStreamDestroy(ctx->copy_stream);
   if (ctx->ws) cudaFree(ctx->ws);
   if (ctx->dev_err) cudaFree(ctx->dev_err);
   if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);

@@ -235,4 +235,114 @@ sam3_status_t sam3_encoder_forward_host(sam3_ctx_t* ctx, const uint16_t* host_im
   return sam3_sync(ctx);
 }
 
+sam3_status_t sam3_encoder_forward_host_pipelined(sam3_ctx_t* ctx, const uint16_t* host_image,
+                                                  int32_t n_images,
+                                                  const sam3_encoder_weights_t* w,
+                                                  uint16_t* host_feats, int32_t* host_idx) {
+  SAM3_CHECK_CTX(ctx);
+  if (!host_image || !host_feats || !host_idx)
+    return set_error(ctx, SAM3_ERR_INVALID_ARG, "encoder_host_pipelined: null pointer");
+  if (n_images <= 0)
+    return set_error(ctx, SAM3_ERR_SHAPE, "encoder_host_pipelined: n_images %d", n_images);
+  cudaSetDevice(ctx->device);
+  const sam3_encoder_config_t& c = ctx->cfg;
+  const int B = c.max_batch;
+  const int rows = sam3_encoder_out_tokens(ctx);
+  const size_t img_elems = (size_t)c.image_size * c.image_size * 3;
+  const size_t img_bytes = (size_t)B * img_elems * 2;
+  const size_t feat_bytes = (size_t)B * rows * c.embed_dim * 2;
+  const size_t idx_bytes = ((size_t)B * rows * 4 + 255) / 256 * 256;
+  const size_t set_bytes = img_bytes + feat_bytes + idx_bytes;
+  sam3_status_t st;
+  if (!ctx->copy_stream) {
+    if ((st = check_cuda(ctx, cudaStreamCreateWithFlags(&ctx->copy_stream, cudaStreamNonBlocking),
+                         "copy stream")) != SAM3_OK)
+      return st;
+    for (cudaEvent_t& e : ctx->pipe_ev)
+      if ((st = check_cuda(ctx, cudaEventCreateWithFlags(&e, cudaEventDisableTiming),
+                           "pipeline event")) != SAM3_OK)
+        return st;
+  }
+  if (ctx->pipe_bytes < 2 * set_bytes) {
+    if (ctx->pipe_mem) {
+      cudaStreamSynchronize(ctx->copy_stream);
+      cudaStreamSynchronize(ctx->stream);
+      cudaFree(ctx->pipe_mem);
+      ctx->pipe_mem = nullptr;
+      ctx->pipe_bytes = 0;
+    }
+    if (cudaMalloc(&ctx->pipe_mem, 2 * set_bytes) != cudaSuccess) {
+      cudaGetLastError();
+      return set_error(ctx, SAM3_ERR_OOM, "encoder_host_pipelined: %zu bytes of staging",
+                       2 * set_bytes);
+    }
+    ctx->pipe_bytes = 2 * set_bytes;
+  }
+  uint16_t* img[2];
+  uint16_t* feats[2];
+  int32_t* idx[2];
+  for (int b = 0; b < 2; ++b) {
+    char* base = ctx->pipe_mem + b * set_bytes;
+    img[b] = reinterpret_cast<uint16_t*>(base);
+    feats[b] = reinterpret_cast<uint16_t*>(base + img_bytes);
+    idx[b] = reinterpret_cast<int32_t*>(base + img_bytes + feat_bytes);
+  }
+  cudaEvent_t* in_done = ctx->pipe_ev;       // chunk's images are on the device
+  cudaEvent_t* img_free = ctx->pipe_ev + 2;  // the encoder has finished with them
+  cudaEvent_t* out_ready = ctx->pipe_ev + 4; // chunk's features are staged
+  cudaEvent_t* out_done = ctx->pipe_ev + 6;  // and copied to the host
+  const cudaStream_t cs = ctx->copy_stream;
+  const int chunks = (n_images + B - 1) / B;
+  auto count = [&](int ch) { return std::min(B, n_images - ch * B); };
+  // Issue order upload(c+1), encoder(c), download(c): on the copy stream the
+  // next chunk's images go ahead of this chunk's features, so both copies run
+  // under the encoder of chunk c+1 / c.
+  auto upload = [&](int ch) -> sam3_status_t {
+    const int b = ch & 1;
+    if (ch >= 2) cudaStreamWaitEvent(cs, img_free[b], 0);
+    sam3_status_t s = check_cuda(
+        ctx, cudaMemcpyAsync(img[b], host_image + (size_t)ch * B * img_elems,
+                             (size_t)count(ch) * img_elems * 2, cudaMemcpyHostToDevice, cs),
+        "pipelined image upload");
+    if (s == SAM3_OK) s = check_cuda(ctx, cudaEventRecord(in_done[b], cs), "event");
+    return s;
+  };
+  // on an error after the first copy, nothing may still be in flight against
+  // the caller's host buffers when this returns
+  auto drain = [&](sam3_status_t s) {
+    cudaStreamSynchronize(cs);
+    cudaStreamSynchronize(ctx->stream);
+    return s;
+  };
+  if ((st = upload(0)) != SAM3_OK) return drain(st);
+  for (int ch = 0; ch < chunks; ++ch) {
+    const int b = ch & 1, nb = count(ch);
+    if (ch + 1 < chunks && (st = upload(ch + 1)) != SAM3_OK) return drain(st);
+    cudaStreamWaitEvent(ctx->stream, in_done[b], 0);
+    if (ch >= 2) cudaStreamWaitEvent(ctx->stream, out_done[b], 0);
+    const uint16_t* out = nullptr;
+    int r = 0;
+    if ((st = encoder_run(ctx, img[b], false, nb, w, idx[b], &out, &r)) != SAM3_OK) return drain(st);
+    const size_t fb = (size_t)nb * r * c.embed_dim * 2;
+    if ((st = check_cuda(ctx, cudaEventRecord(img_free[b], ctx->stream), "event")) != SAM3_OK ||
+        (st = check_cuda(ctx, cudaMemcpyAsync(feats[b], out, fb, cudaMemcpyDeviceToDevice,
+                                              ctx->stream),
+                         "pipelined feats staging")) != SAM3_OK ||
+        (st = check_cuda(ctx, cudaEventRecord(out_ready[b], ctx->stream), "event")) != SAM3_OK)
+      return drain(st);
+    cudaStreamWaitEvent(cs, out_ready[b], 0);
+    if ((st = check_cuda(ctx, cudaMemcpyAsync(host_feats + (size_t)ch * B * r * c.embed_dim,
+                                              feats[b], fb, cudaMemcpyDeviceToHost, cs),
+                         "pipelined feats download")) != SAM3_OK ||
+        (st = check_cuda(ctx, cudaMemcpyAsync(host_idx + (size_t)ch * B * r, idx[b],
+                                              (size_t)nb * r * 4, cudaMemcpyDeviceToHost, cs),
+                         "pipelined idx download")) != SAM3_OK ||
+        (st = check_cuda(ctx, cudaEventRecord(out_done[b], cs), "event")) != SAM3_OK)
+      return drain(st);
+  }
+  if ((st = check_cuda(ctx, cudaStreamSynchronize(cs), "pipelined downloads")) != SAM3_OK)
+    return st;
+  return sam3_sync(ctx);
+}
+
 }  // extern "C"

@@ -47,6 +47,13 @@ struct sam3_ctx {
   size_t block_rows = 0;        // rows the block scratch can hold (plain encoder)
   size_t token_rows = 0;        // rows with a class token per image (windowed encoder)
 
+  // Double-buffered staging of sam3_encoder_forward_host_pipelined, made on
+  // first use: two sets of (images, features, indices) and a copy stream.
+  cudaStream_t copy_stream = nullptr;
+  char* pipe_mem = nullptr;
+  size_t pipe_bytes = 0;
+  cudaEvent_t pipe_ev[8] = {};  // in_done[2], img_free[2], out_ready[2], out_done[2]
+
   // Device-side stage timing (sam3_profile_enable / sam3_profile_read).
   struct ProfRecord {
     int cls;

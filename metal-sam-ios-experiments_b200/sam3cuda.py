@@ -116,6 +116,7 @@ SIGNATURES = {
     "sam3_restore_spatial": (_S, [_P, _P, _P, _I, _I, _I, _I, _P]),
     "sam3_neck": (_S, [_P, _P, _I, _I, _I, C.POINTER(NeckWeights), _P]),
     "sam3_windowed_encoder_forward": (_S, [_P, _P, _I, C.POINTER(WindowedEncoderWeights), _P]),
+    "sam3_encoder_forward_host_pipelined": (_S, [_P, _P, _I, C.POINTER(EncoderWeights), _P, _P]),
     "sam3_encoder_forward_host": (_S, [_P, _P, _I, C.POINTER(EncoderWeights), _P, _P]),
     "sam3_encoder_out_tokens": (C.c_int32, [_P]),
     "sam3_profile_enable": (_S, [_P, _I]),
@@ -343,6 +344,15 @@ class Context:
             return a.ctypes.data_as(C.c_void_p) if isinstance(a, np.ndarray) else ptr(a)
         self._check(lib.sam3_encoder_forward_host(self.handle, hp(image_host), batch, C.byref(w),
                                                   hp(feats_host), hp(idx_host)))
+
+    def encoder_forward_host_pipelined(self, image_host, n_images, w: EncoderWeights, feats_host,
+                                       idx_host):
+        """n_images from host buffers in chunks of max_batch, copies overlapped."""
+        def hp(a):
+            return a.ctypes.data_as(C.c_void_p) if isinstance(a, np.ndarray) else ptr(a)
+        self._check(lib.sam3_encoder_forward_host_pipelined(self.handle, hp(image_host), n_images,
+                                                            C.byref(w), hp(feats_host),
+                                                            hp(idx_host)))
 
     @property
     def out_tokens(self) -> int:

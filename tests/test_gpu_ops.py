@@ -718,6 +718,30 @@ def test_encoder_small_device_and_host_api(ctx, sam3, oracle):
     assert np.array_equal(hi, gi) and np.array_equal(hf.view(np.uint16), gf.view(np.uint16))
 
 
+def test_encoder_host_pipelined_equals_per_call(ctx, sam3, oracle):
+    # 5 images through max_batch 2: three chunks, the last one partial, with
+    # the uploads / downloads overlapped on the copy stream; bit-identical to
+    # one sam3_encoder_forward_host call per chunk
+    blocks, pw, pb = _small_encoder(oracle)
+    w = _upload_encoder(ctx, sam3, blocks, pw, pb)
+    img = oracle.gen_uniform(32, 77, (5, 112, 112, 3), -1.0, 1.0)
+    pf = np.full((5, 32, 256), np.nan, F16)
+    pi = np.full((5, 32), -1, np.int32)
+    ctx.encoder_forward_host_pipelined(img, 5, w, pf, pi)
+    for c0 in range(0, 5, 2):
+        n = min(2, 5 - c0)
+        hf = np.empty((n, 32, 256), F16)
+        hi = np.empty((n, 32), np.int32)
+        ctx.encoder_forward_host(np.ascontiguousarray(img[c0:c0 + n]), n, w, hf, hi)
+        assert np.array_equal(pi[c0:c0 + n], hi)
+        assert np.array_equal(pf[c0:c0 + n].view(np.uint16), hf.view(np.uint16))
+    # twice in a row (staging reused) gives the same bits
+    pf2 = np.empty_like(pf)
+    pi2 = np.empty_like(pi)
+    ctx.encoder_forward_host_pipelined(img, 5, w, pf2, pi2)
+    assert np.array_equal(pi2, pi) and np.array_equal(pf2.view(np.uint16), pf.view(np.uint16))
+
+
 def test_encoder_full_size_two_blocks_matches_oracle(sam3, oracle):
     # 1008^2 image, full width (1024, 16 heads, 4096), two blocks with the
     # prune (to 2592 tokens by L2 norm) between them. Upstream fp16 rounding
