@@ -5,7 +5,8 @@
 // Sam3Sensor): RoPE (RoPE.swift:9-121), LayerNorm (ViTEncoder.swift:751-888),
 // MLP (ViTEncoder.swift:892-1051), MPSAttentionLayer (MPSAttention.swift:
 // 13-244), TransformerBlock (ViTEncoder.swift:299-747), TokenPruner
-// (TokenPruner.swift:11-197) and ViTEncoder (ViTEncoder.swift:1056-1481).
+// (TokenPruner.swift:11-197), ViTEncoder (ViTEncoder.swift:1056-1481) and
+// the checkpoint-faithful SAM3Encoder (SAM3Encoder.swift:10-760).
 // The classes below keep their names, method names and argument meaning:
 //  - `forward(...)` returns a freshly allocated device buffer and appends it
 //    to `recycledBuffers`, as the reference does with BufferAllocator
@@ -243,10 +244,42 @@ class ViTEncoder {
     return feats;
   }
 
+  // Many images from and to host memory (SAM3MetalPipeline.encode,
+  // SAM3MetalPipeline.swift:67-82, over a whole set of frames): chunks of
+  // max_batch with the copies overlapped; returns when all are on the host.
+  void encodeHost(const uint16_t* hostImages, int nImages, uint16_t* hostFeats,
+                  int32_t* hostIndices) {
+    check(ctx_, sam3_encoder_forward_host_pipelined(ctx_, hostImages, nImages, &w_, hostFeats,
+                                                    hostIndices),
+          "ViTEncoder.encodeHost");
+  }
+
  private:
   sam3_ctx_t* ctx_;
   sam3_encoder_weights_t w_;
   int dim_;
+};
+
+// SAM3Encoder.swift:10-760: class token, resized positional embedding,
+// windowed blocks with global ones every num_blocks / 4; returns the patch
+// tokens [batch, grid*grid, dim] in grid order.
+class SAM3Encoder {
+ public:
+  SAM3Encoder(sam3_ctx_t* ctx, const sam3_windowed_encoder_weights_t& w, int embedDim = 1024,
+              int gridSize = 72)
+      : ctx_(ctx), w_(w), dim_(embedDim), grid_(gridSize) {}
+  uint16_t* forward(const uint16_t* image, int batch, BufferList& recycledBuffers) {
+    auto* out = static_cast<uint16_t*>(allocate(ctx_, (size_t)batch * grid_ * grid_ * dim_ * 2,
+                                                recycledBuffers, "SAM3Encoder output"));
+    check(ctx_, sam3_windowed_encoder_forward(ctx_, image, batch, &w_, out),
+          "SAM3Encoder.forward");
+    return out;
+  }
+
+ private:
+  sam3_ctx_t* ctx_;
+  sam3_windowed_encoder_weights_t w_;
+  int dim_, grid_;
 };
 
 }  // namespace sam3

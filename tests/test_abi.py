@@ -76,3 +76,24 @@ def test_null_context_is_an_error_not_a_crash(sam3):
     assert sam3.lib.sam3_ctx_destroy(None) == sam3.ERR_INVALID_ARG
     assert sam3.lib.sam3_last_error(None) == b"null context"
     assert sam3.lib.sam3_ctx_create(0, None, None) == sam3.ERR_INVALID_ARG
+
+
+def test_cpp_operator_mirror_compiles_and_throws(tmp_path):
+    # the header-only C++ mirror of the reference's operator classes, built
+    # against the library; errors come back as sam3::SAM3Error (no GPU used)
+    import shutil
+    gxx = shutil.which("g++")
+    if gxx is None:
+        pytest.skip("no g++")
+    pkg = PKG
+    exe = str(tmp_path / "mirror_check")
+    cmd = [gxx, "-std=c++17", "-O1", "-Wall", "-Werror",
+           "-I/usr/local/cuda/include", "-I" + os.path.join(pkg, "host"),
+           os.path.join(ROOT, "tests", "host_mirror_check.cpp"),
+           "-L" + pkg, "-lsam3cuda", "-L/usr/local/cuda/lib64", "-lcudart",
+           "-Wl,-rpath," + pkg, "-Wl,-rpath,/usr/local/cuda/lib64", "-o", exe]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+    r = subprocess.run([exe], capture_output=True, text=True, timeout=60)
+    assert r.returncode == 0, r.stdout + r.stderr
+    assert "caught 5 of 5" in r.stdout
