@@ -382,6 +382,29 @@ sam3_status_t sam3_windowed_encoder_forward(sam3_ctx_t* ctx, const uint16_t* ima
                                             const sam3_windowed_encoder_weights_t* w,
                                             uint16_t* out);
 
+/* ---- failure detection and fault injection ------------------------------
+ * Every wait inside a kernel (mbarriers of the TMA / MMA pipelines) is bounded
+ * (2 s); on expiry the kernel records a code in the context's device error
+ * word, drains its copies in flight and returns, and the next sam3_sync
+ * returns SAM3_ERR_TIMEOUT and clears the word: the context stays usable.
+ * Reference: errors surface as `throws SAM3Error`
+ * (SAM3MetalPipeline.swift:176-208); it has no device-side watchdog. */
+
+/* Launches a one-thread kernel whose bounded wait, on an mbarrier nothing
+ * arrives on, runs out: the following sam3_sync returns SAM3_ERR_TIMEOUT
+ * (after about 2 s) without any GPU fault. */
+sam3_status_t sam3_selftest_wait_timeout(sam3_ctx_t* ctx);
+
+/* Host-side fault injection for the error paths (no GPU fault is made):
+ * SAM3_FAULT_ALLOC makes sam3_alloc, sam3_host_alloc and the staging
+ * allocation of sam3_encoder_forward_host_pipelined fail with SAM3_ERR_OOM;
+ * SAM3_FAULT_LAUNCH makes every kernel-launch check report SAM3_ERR_CUDA
+ * (the kernel itself may have run). The environment variable SAM3_FAULT
+ * ("alloc", "launch", "alloc,launch") sets the flags of every new context. */
+typedef enum { SAM3_FAULT_NONE = 0, SAM3_FAULT_ALLOC = 1, SAM3_FAULT_LAUNCH = 2 } sam3_fault_t;
+sam3_status_t sam3_set_fault(sam3_ctx_t* ctx, int32_t flags);
+int32_t sam3_get_fault(const sam3_ctx_t* ctx);
+
 /* ---- device-side stage timing ---------------------------------------------
  * When enabled, the context brackets each of its kernel launches with CUDA
  * events on its stream and accumulates, per kernel class, the launch count,

@@ -26,6 +26,7 @@ enum DevErr : int {
   kDevErrTimeoutEpilogue = 0x104,
   kDevErrTimeoutDrain = 0x105,
   kDevErrTimeoutAttn = 0x106,
+  kDevErrTimeoutSelftest = 0x1FF,  // sam3_selftest_wait_timeout
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {

@@ -6,10 +6,13 @@
 // once at creation, so the encoder's hot loop never allocates.
 #include <stdarg.h>
 #include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
 
 #include <algorithm>
 #include <mutex>
 
+#include "common.cuh"
 #include "internal.h"
 
 namespace sam3 {
@@ -37,14 +40,49 @@ sam3_status_t check_cuda(sam3_ctx_t* ctx, cudaError_t e, const char* what) {
 
 sam3_status_t check_launch(sam3_ctx_t* ctx, const char* what) {
   ctx->launches++;
-  return check_cuda(ctx, cudaGetLastError(), what);
+  sam3_status_t st = check_cuda(ctx, cudaGetLastError(), what);
+  if (st == SAM3_OK && (ctx->fault & SAM3_FAULT_LAUNCH))
+    return set_error(ctx, SAM3_ERR_CUDA, "%s: injected launch failure", what);
+  return st;
 }
 
 sam3_status_t check_launch_ret(sam3_ctx_t* ctx, cudaError_t e, const char* what) {
   const cudaError_t last = cudaGetLastError();  // clears a launch error recorded twice
   ctx->launches++;
-  return check_cuda(ctx, e != cudaSuccess ? e : last, what);
+  sam3_status_t st = check_cuda(ctx, e != cudaSuccess ? e : last, what);
+  if (st == SAM3_OK && (ctx->fault & SAM3_FAULT_LAUNCH))
+    return set_error(ctx, SAM3_ERR_CUDA, "%s: injected launch failure", what);
+  return st;
 }
+
+namespace {
+
+// One thread waits, with the bounded wait every kernel uses, on an mbarrier
+// that nothing arrives on: the wait runs out after kWaitTimeoutNs, records
+// kDevErrTimeoutSelftest in the context's error word and the kernel returns.
+__global__ void selftest_wait_kernel(int* err) {
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    mbar_init(smem_u32(&bar), 1);
+    fence_mbar_init();
+    abort_flag = 0;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) mbar_wait(smem_u32(&bar), 0, &abort_flag, err, kDevErrTimeoutSelftest);
+}
+
+int fault_flags_from_env() {
+  const char* v = getenv("SAM3_FAULT");
+  int f = 0;
+  if (v) {
+    if (strstr(v, "alloc")) f |= SAM3_FAULT_ALLOC;
+    if (strstr(v, "launch")) f |= SAM3_FAULT_LAUNCH;
+  }
+  return f;
+}
+
+}  // namespace
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
@@ -256,8 +294,25 @@ sam3_status_t sam3_ctx_create(int device, const sam3_encoder_config_t* cfg, sam3
     return st;
   }
   cudaDeviceSynchronize();
+  ctx->fault = fault_flags_from_env();  // after the workspace: the context itself is made
   *out = ctx;
   return SAM3_OK;
+}
+
+sam3_status_t sam3_set_fault(sam3_ctx_t* ctx, int32_t flags) {
+  SAM3_CHECK_CTX(ctx);
+  if (flags & ~(SAM3_FAULT_ALLOC | SAM3_FAULT_LAUNCH)) return SAM3_ERR_INVALID_ARG;
+  ctx->fault = flags;
+  return SAM3_OK;
+}
+
+int32_t sam3_get_fault(const sam3_ctx_t* ctx) { return ctx ? ctx->fault : 0; }
+
+sam3_status_t sam3_selftest_wait_timeout(sam3_ctx_t* ctx) {
+  SAM3_CHECK_CTX(ctx);
+  cudaSetDevice(ctx->device);
+  selftest_wait_kernel<<<1, 32, 0, ctx->stream>>>(ctx->dev_err);
+  return check_launch(ctx, "selftest_wait_kernel");
 }
 
 sam3_status_t sam3_ctx_destroy(sam3_ctx_t* ctx) {
@@ -333,6 +388,10 @@ sam3_status_t sam3_alloc(sam3_ctx_t* ctx, size_t bytes, void** p) {
   SAM3_CHECK_CTX(ctx);
   if (!p) return SAM3_ERR_INVALID_ARG;
   cudaSetDevice(ctx->device);
+  if (ctx->fault & SAM3_FAULT_ALLOC) {
+    *p = nullptr;
+    return set_error(ctx, SAM3_ERR_OOM, "sam3_alloc: injected allocation failure");
+  }
   return check_cuda(ctx, cudaMalloc(p, bytes ? bytes : 1), "sam3_alloc");
 }
 sam3_status_t sam3_free(sam3_ctx_t* ctx, void* p) {
@@ -343,6 +402,10 @@ sam3_status_t sam3_free(sam3_ctx_t* ctx, void* p) {
 sam3_status_t sam3_host_alloc(sam3_ctx_t* ctx, size_t bytes, void** p) {
   SAM3_CHECK_CTX(ctx);
   if (!p) return SAM3_ERR_INVALID_ARG;
+  if (ctx->fault & SAM3_FAULT_ALLOC) {
+    *p = nullptr;
+    return set_error(ctx, SAM3_ERR_OOM, "sam3_host_alloc: injected allocation failure");
+  }
   return check_cuda(ctx, cudaMallocHost(p, bytes ? bytes : 1), "sam3_host_alloc");
 }
 sam3_status_t sam3_host_free(sam3_ctx_t* ctx, void* p) {

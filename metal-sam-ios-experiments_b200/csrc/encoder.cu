@@ -263,6 +263,8 @@ sam3_status_t sam3_encoder_forward_host_pipelined(sam3_ctx_t* ctx, const uint16_
                            "pipeline event")) != SAM3_OK)
         return st;
   }
+  if (ctx->pipe_bytes < 2 * set_bytes && (ctx->fault & SAM3_FAULT_ALLOC))
+    return set_error(ctx, SAM3_ERR_OOM, "encoder_host_pipelined: injected allocation failure");
   if (ctx->pipe_bytes < 2 * set_bytes) {
     if (ctx->pipe_mem) {
       cudaStreamSynchronize(ctx->copy_stream);

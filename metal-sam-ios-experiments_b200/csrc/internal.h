@@ -20,6 +20,7 @@ struct sam3_ctx {
   std::string last_error;
   int* dev_err = nullptr;  // device error word written by bounded waits
   uint64_t launches = 0;
+  int fault = 0;  // SAM3_FAULT_* flags: host-side fault injection for tests
 
   // Workspace arena (allocated at create, sized for cfg.max_batch images).
   char* ws = nullptr;

@@ -22,6 +22,7 @@ LIB_PATH = os.path.join(_HERE, "libsam3cuda.so")
 
 OK, ERR_INVALID_ARG, ERR_SHAPE, ERR_OOM, ERR_CUDA, ERR_TIMEOUT, ERR_UNSUPPORTED = range(7)
 EPI_BIAS, EPI_BIAS_GELU, EPI_BIAS_RESIDUAL, EPI_BIAS_ROPE_QKV = range(4)
+FAULT_NONE, FAULT_ALLOC, FAULT_LAUNCH = 0, 1, 2
 SCORE_L2, SCORE_L1 = 0, 1
 ORDER_INDEX, ORDER_SCORE = 0, 1
 
@@ -119,6 +120,9 @@ SIGNATURES = {
     "sam3_encoder_forward_host_pipelined": (_S, [_P, _P, _I, C.POINTER(EncoderWeights), _P, _P]),
     "sam3_encoder_forward_host": (_S, [_P, _P, _I, C.POINTER(EncoderWeights), _P, _P]),
     "sam3_encoder_out_tokens": (C.c_int32, [_P]),
+    "sam3_selftest_wait_timeout": (_S, [_P]),
+    "sam3_set_fault": (_S, [_P, _I]),
+    "sam3_get_fault": (C.c_int32, [_P]),
     "sam3_profile_enable": (_S, [_P, _I]),
     "sam3_profile_read": (_S, [_P, C.POINTER(Profile)]),
     "sam3_prune_noalloc": (_S, [_P, _P, _I, _I, _I, _I, _I, _I, _P, _I, _I, _P, _P, _P]),
@@ -236,6 +240,18 @@ class Context:
     @property
     def launches(self) -> int:
         return int(lib.sam3_launch_count(self.handle))
+
+    def selftest_wait_timeout(self):
+        """Launch the bounded-wait self-test; the next sync raises SAM3Error (TIMEOUT)."""
+        self._check(lib.sam3_selftest_wait_timeout(self.handle))
+
+    @property
+    def fault(self) -> int:
+        return int(lib.sam3_get_fault(self.handle))
+
+    @fault.setter
+    def fault(self, flags: int):
+        self._check(lib.sam3_set_fault(self.handle, flags))
 
     def profile_enable(self, on: bool = True):
         self._check(lib.sam3_profile_enable(self.handle, 1 if on else 0))

@@ -41,6 +41,11 @@ int main() {
   } catch (const sam3::SAM3Error& e) {
     caught += e.status == SAM3_ERR_INVALID_ARG;
   }
-  std::printf("caught %d of 5, embed_dim %d\n", caught, cfg.embed_dim);
-  return caught == 5 && recycled.empty() ? 0 : 1;
+  // fault injection and the wait self-test need a context too
+  const bool no_ctx = sam3_set_fault(nullptr, SAM3_FAULT_ALLOC) == SAM3_ERR_INVALID_ARG &&
+                      sam3_selftest_wait_timeout(nullptr) == SAM3_ERR_INVALID_ARG &&
+                      sam3_get_fault(nullptr) == 0;
+  std::printf("caught %d of 5, embed_dim %d, no-context checks %s\n", caught, cfg.embed_dim,
+              no_ctx ? "ok" : "failed");
+  return caught == 5 && recycled.empty() && no_ctx ? 0 : 1;
 }

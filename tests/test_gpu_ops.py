@@ -7,10 +7,12 @@ outputs within a normwise max relative error of 1e-2 in fp16
 sides differ only by fp32 summation order.
 """
 import ctypes as C
+import os
 
 import numpy as np
 import pytest
 
+from conftest import PKG
 from util import f16_ulps, max_rel_err
 
 pytestmark = pytest.mark.gpu
@@ -916,3 +918,77 @@ def test_windowed_encoder_from_palettized_checkpoint_keys(ctx, sam3, oracle, tmp
                                           src[f"{t}.cls_token"].reshape(-1),
                                           src[f"{t}.pos_embed"].reshape(17, dim), heads=4)
     assert max_rel_err(got, ref) < SPEC_TOL
+
+
+# ------------------------------------------------------------------ failure detection
+def test_bounded_wait_runs_out_reports_timeout_and_context_survives(ctx, sam3, oracle):
+    # a kernel waits, with the bounded wait every kernel uses, on an mbarrier
+    # that nothing arrives on: no fault, no hang — the wait runs out (2 s),
+    # sync reports SAM3_ERR_TIMEOUT once, and the context keeps working
+    x = oracle.gen_normal(91, 1, (64, 256))
+    dx = ctx.upload(x)
+    dy = ctx.alloc(x.nbytes)
+    ctx.sync()
+    ctx.selftest_wait_timeout()
+    with pytest.raises(sam3.SAM3Error) as e:
+        ctx.sync()
+    assert e.value.status == sam3.ERR_TIMEOUT and "0x1ff" in str(e.value)
+    ctx.sync()  # the error word was cleared
+    ctx.layernorm(dx, 64, 256, None, None, 1e-6, dy)
+    ctx.sync()
+    assert max_rel_err(ctx.download(dy, x.shape, F16), oracle.layernorm(x)) < 2e-3
+
+
+def test_injected_faults_propagate_and_clear(ctx, sam3, oracle):
+    blocks, pw, pb = _small_encoder(oracle)
+    w = _upload_encoder(ctx, sam3, blocks, pw, pb)
+    img = oracle.gen_uniform(31, 77, (2, 112, 112, 3), -1.0, 1.0)
+    dimg = ctx.upload(img)
+    feats, idx = ctx.alloc(2 * 32 * 256 * 2), ctx.alloc(2 * 32 * 4)
+    try:
+        ctx.fault = sam3.FAULT_ALLOC
+        with pytest.raises(sam3.SAM3Error) as e:
+            ctx.alloc(4096)
+        assert e.value.status == sam3.ERR_OOM and "injected" in str(e.value)
+        hf = np.empty((2, 32, 256), F16)
+        hi = np.empty((2, 32), np.int32)
+        ctx.fault = sam3.FAULT_LAUNCH
+        with pytest.raises(sam3.SAM3Error) as e:
+            ctx.encoder_forward(dimg, 2, w, feats, idx)
+        assert e.value.status == sam3.ERR_CUDA and "injected launch failure" in str(e.value)
+        with pytest.raises(sam3.SAM3Error):
+            ctx.encoder_forward_host(img, 2, w, hf, hi)
+    finally:
+        ctx.fault = sam3.FAULT_NONE
+    ctx.sync()
+    assert ctx.fault == 0
+    ctx.encoder_forward(dimg, 2, w, feats, idx)
+    ctx.sync()
+    ref_f, ref_i = oracle.encoder_forward(img, blocks, pw, pb, heads=4, prune_after=1, keep=32)
+    assert np.array_equal(ctx.download(idx, (2, 32), np.int32), ref_i)
+    assert max_rel_err(ctx.download(feats, (2, 32, 256), F16), ref_f) < SPEC_TOL
+
+
+def test_fault_environment_variable_sets_new_contexts(sam3, tmp_path):
+    # SAM3_FAULT is read when a context is made (subprocess: a clean environment)
+    import subprocess
+    import sys
+    code = (
+        "import sys; sys.path.insert(0, %r)\n"
+        "import sam3cuda as s\n"
+        "c = s.Context(0, embed_dim=256, num_heads=4, mlp_hidden=512, num_blocks=1,\n"
+        "              image_size=112, max_batch=1)\n"
+        "assert c.fault == s.FAULT_ALLOC | s.FAULT_LAUNCH, c.fault\n"
+        "try:\n"
+        "    c.alloc(64)\n"
+        "    raise SystemExit('alloc did not fail')\n"
+        "except s.SAM3Error as e:\n"
+        "    assert e.status == s.ERR_OOM\n"
+        "c.fault = 0\n"
+        "c.alloc(64)\n"
+        "c.close()\n"
+        "print('ok')\n") % PKG
+    env = dict(os.environ, SAM3_FAULT="alloc,launch")
+    r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, env=env,
+                       timeout=300)
+    assert r.returncode == 0 and "ok" in r.stdout, r.stdout + r.stderr
