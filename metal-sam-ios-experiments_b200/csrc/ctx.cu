@@ -180,7 +180,10 @@ size_t carve(sam3_ctx_t* ctx, char* base) {
   ctx->patch_wp = cv.take<uint16_t>(D * kp);
   ctx->scores = cv.take<float>(B * S);
   ctx->rope = cv.take<float>(S * hd);
-  ctx->rope_win = cv.take<float>(R * hd);
+  ctx->rope_axial = cv.take<float>(grid * 32);
+  ctx->rope_pos_grid = cv.take<int32_t>(B * S);
+  ctx->rope_pos_win = cv.take<int32_t>(B * R);
+  ctx->rope_pos_pruned = cv.take<int32_t>(B * keep);
   ctx->rope_pruned = cv.take<float>(B * keep * hd);
   ctx->idx = cv.take<int32_t>(B * S);
   ctx->image = cv.take<uint16_t>(B * (size_t)c.image_size * c.image_size * 3);
@@ -209,6 +212,7 @@ sam3_status_t ensure_workspace(sam3_ctx_t* ctx) {
   ctx->ws = static_cast<char*>(p);
   ctx->ws_bytes = need;
   ctx->rope_ready = 0;
+  ctx->rope_win_key = 0;
   carve(ctx, ctx->ws);
   return SAM3_OK;
 }

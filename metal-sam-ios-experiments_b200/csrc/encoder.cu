@@ -32,15 +32,19 @@ sam3_status_t check_block_weights(sam3_ctx_t* ctx, const sam3_block_weights_t* w
   return SAM3_OK;
 }
 
+// rope_pos null: rope is a table of rope_rows full rows (row r % rope_rows);
+// otherwise the axial table with per-row coordinates (gemm_palette).
 sam3_status_t attention_block(sam3_ctx_t* ctx, uint16_t* x, int batch, int seq,
-                              const sam3_block_weights_t* w, const float* rope, int rope_rows) {
+                              const sam3_block_weights_t* w, const float* rope, int rope_rows,
+                              const int32_t* rope_pos = nullptr) {
   const int D = ctx->cfg.embed_dim, H = ctx->cfg.num_heads;
   const int m = batch * seq;
   sam3_status_t st;
   if ((st = layernorm(ctx, x, m, D, w->ln1_gamma, w->ln1_beta, ctx->cfg.ln_eps, ctx->ln)) != SAM3_OK)
     return st;
   if ((st = gemm_palette(ctx, ctx->ln, m, D, w->qkv.idx, w->qkv.palette, w->qkv.bias, 3 * D,
-                         SAM3_EPI_BIAS_ROPE_QKV, nullptr, rope, rope_rows, ctx->qkv)) != SAM3_OK)
+                         SAM3_EPI_BIAS_ROPE_QKV, nullptr, rope, rope_rows, ctx->qkv,
+                         rope_pos)) != SAM3_OK)
     return st;
   if ((st = attention(ctx, ctx->qkv, batch, seq, H, 64, 0.125f, ctx->attn)) != SAM3_OK) return st;
   return gemm_palette(ctx, ctx->attn, m, D, w->proj.idx, w->proj.palette, w->proj.bias, D,
@@ -87,29 +91,28 @@ sam3_status_t encoder_run(sam3_ctx_t* ctx, const void* image, bool rgba, int bat
   const bool pruned = c.prune_after_block > 0 && c.prune_after_block <= c.num_blocks &&
                       c.keep_tokens < S;
   const int keep = pruned ? c.keep_tokens : S;
-  if (!ctx->rope_ready) {
-    if ((st = rope_table(ctx, grid, grid, 64, c.rope_theta, ctx->rope)) != SAM3_OK) return st;
-    ctx->rope_ready = 1;
-  }
+  if ((st = rope_setup(ctx)) != SAM3_OK) return st;
   if ((st = patch_embed(ctx, image, rgba, batch, c.image_size, c.image_size, w->patch_w,
                         w->patch_b, c.patch, D, ctx->x, ctx->cols, ctx->patch_wp)) != SAM3_OK)
     return st;
   uint16_t* cur = ctx->x;
   int rows = S;
-  const float* rope = ctx->rope;
-  int rope_rows = S;
+  // the QKV epilogue rotates by the axial table and each row's coordinates
+  const int32_t* rope_pos = ctx->rope_pos_grid;
   for (int blk = 0; blk <= c.num_blocks; ++blk) {
     if (pruned && blk == c.prune_after_block) {
       if ((st = prune(ctx, cur, batch, S, D, keep, c.score_norm, c.keep_order, ctx->rope, S, 64,
                       ctx->xp, ctx->rope_pruned, idx, ctx->scores)) != SAM3_OK)
         return st;
+      if ((st = rope_pos_from_idx(ctx, idx, batch * keep, grid, ctx->rope_pos_pruned)) != SAM3_OK)
+        return st;
       cur = ctx->xp;
       rows = keep;
-      rope = ctx->rope_pruned;
-      rope_rows = batch * keep;
+      rope_pos = ctx->rope_pos_pruned;
     }
     if (blk == c.num_blocks) break;
-    if ((st = attention_block(ctx, cur, batch, rows, &w->blocks[blk], rope, rope_rows)) != SAM3_OK)
+    if ((st = attention_block(ctx, cur, batch, rows, &w->blocks[blk], ctx->rope_axial, 0,
+                              rope_pos)) != SAM3_OK)
       return st;
     if ((st = mlp_block(ctx, cur, batch * rows, &w->blocks[blk])) != SAM3_OK) return st;
   }

@@ -54,6 +54,12 @@ struct GemmArgs {
   const __half* bias;
   const __half* residual;
   const float* rope;
+  // Axial RoPE: when set, rope points at A[c][16] (cos, sin) pairs with
+  // A[c][i] = rotation of pair i at coordinate c, and row r of the output
+  // takes its coordinates from rope_pos[r] = x | y << 16 (pairs 0-15 of a head
+  // rotate by x, pairs 16-31 by y; -1: no rotation). Otherwise rope is a
+  // table of rope_rows full rows (32 pairs) indexed by r % rope_rows.
+  const int32_t* rope_pos;
   const __half* palette;
   __half* y;
   int* err;
@@ -78,11 +84,19 @@ __device__ __forceinline__ void prefetch_l1(const void* p) {
   asm volatile("prefetch.global.L1 [%0];" ::"l"(p));
 }
 
+// Coordinates of an output row for the axial RoPE epilogue (loaded before
+// the accumulator is ready).
+__device__ __forceinline__ int rope_pos_of(const GemmArgs& a, int row) {
+  return (a.rope_pos && a.epi == SAM3_EPI_BIAS_ROPE_QKV && row < a.m) ? __ldg(a.rope_pos + row)
+                                                                       : 0;
+}
+
 // Warm L1 with an epilogue's inputs for 64 columns of one output row (bias,
 // RoPE table row, residual row) while the accumulator is still being computed.
+// (The axial RoPE table is a few KB and stays in L1 by itself.)
 __device__ __forceinline__ void epilogue_prefetch(const GemmArgs& a, int row, int col0) {
   if (a.bias) prefetch_l1(a.bias + col0);
-  if (a.epi == SAM3_EPI_BIAS_ROPE_QKV && col0 < a.qk_cols) {
+  if (a.epi == SAM3_EPI_BIAS_ROPE_QKV && col0 < a.qk_cols && !a.rope_pos) {
     const float* t = a.rope + (size_t)(row % a.rope_rows) * 64;
     prefetch_l1(t);
     prefetch_l1(t + 32);
@@ -93,7 +107,7 @@ __device__ __forceinline__ void epilogue_prefetch(const GemmArgs& a, int row, in
 
 // Epilogue for 32 consecutive accumulator columns of one output row.
 __device__ __forceinline__ void epilogue_chunk(const GemmArgs& a, int row, int col0,
-                                               const uint32_t (&v)[32]) {
+                                               const uint32_t (&v)[32], int rpos) {
   float f[32];
 #pragma unroll
   for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(v[j]);
@@ -107,11 +121,20 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs& a, int row, int c
     for (int j = 0; j < 32; ++j) f[j] = gelu_as(f[j]);
   } else if (a.epi == SAM3_EPI_BIAS_ROPE_QKV && col0 < a.qk_cols) {
     // 32 columns = 16 interleaved (even, odd) pairs of one 64-wide head;
-    // table row holds 32 (cos, sin) pairs, pair j at float offset 2j.
-    const float4* t = reinterpret_cast<const float4*>(
-        a.rope + (size_t)(row % a.rope_rows) * 64 + (col0 & 63));
+    // a full table row holds 32 (cos, sin) pairs, pair j at float offset 2j;
+    // the axial table holds the 16 pairs of one coordinate (x for the first
+    // 32 columns of the head, y for the last 32).
+    const float4* t;
+    bool rotate = true;
+    if (a.rope_pos) {
+      rotate = rpos >= 0;
+      const int c = (col0 & 32) ? (rpos >> 16) : (rpos & 0xFFFF);
+      t = reinterpret_cast<const float4*>(a.rope + (size_t)(rotate ? c : 0) * 32);
+    } else {
+      t = reinterpret_cast<const float4*>(a.rope + (size_t)(row % a.rope_rows) * 64 + (col0 & 63));
+    }
 #pragma unroll
-    for (int q = 0; q < 8; ++q) {
+    for (int q = 0; q < 8 && rotate; ++q) {
       const float4 cs = __ldg(t + q);
       float x0 = f[4 * q], x1 = f[4 * q + 1];
       f[4 * q] = x0 * cs.x - x1 * cs.y;
@@ -363,13 +386,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       tc_fence_after();
       const int m0 = (t % args.m_tiles) * BM, n0 = (t / args.m_tiles) * BN;
       const int row = m0 + quad * 32 + lane;
+      const int rpos = rope_pos_of(args, row);
       const uint32_t taddr = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * BN);
 #pragma unroll 1
       for (int c = 0; c < BN / 32; ++c) {
         uint32_t v[32];
         tmem_ld_32x32b_x32(taddr + (uint32_t)(c * 32), v);
         tmem_wait_ld();
-        epilogue_chunk(args, row, n0 + c * 32, v);
+        epilogue_chunk(args, row, n0 + c * 32, v, rpos);
       }
       tc_fence_before();
       mbar_arrive(bar_tempty + 8 * acc);
@@ -698,6 +722,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(WS_THREADS, 1)
         dep_waited = true;
       }
       epilogue_prefetch(args, row, col0);
+      const int rpos = rope_pos_of(args, row);
       ok = __all_sync(0xffffffffu, mbar_wait_cluster(bar_tfull + 8 * acc, use, abort_flag,
                                                      args.err, kDevErrTimeoutEpilogue));
       if (!ok) break;
@@ -711,8 +736,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(WS_THREADS, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(mapa_shared(bar_tempty + 8 * acc, 0));
-      epilogue_chunk(args, row, col0, *reinterpret_cast<const uint32_t(*)[32]>(v));
-      epilogue_chunk(args, row, col0 + 32, *reinterpret_cast<const uint32_t(*)[32]>(v + 32));
+      epilogue_chunk(args, row, col0, *reinterpret_cast<const uint32_t(*)[32]>(v), rpos);
+      epilogue_chunk(args, row, col0 + 32, *reinterpret_cast<const uint32_t(*)[32]>(v + 32), rpos);
     }
   }
 
@@ -939,8 +964,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(WS_THREADS, 1)
         griddep_wait();
         dep_waited = true;
       }
+      static_assert(WSC_GROUP == 2, "two M tiles per group");
 #pragma unroll
       for (int t = 0; t < WSC_GROUP; ++t) epilogue_prefetch(args, row0 + t * 2 * WS_BM, col0);
+      const int rpos0 = rope_pos_of(args, row0), rpos1 = rope_pos_of(args, row0 + 2 * WS_BM);
       const bool w = __all_sync(0xffffffffu,
                                 mbar_wait_cluster(bar_tfull + 8 * gp, (uint32_t)(e_it >> 1) & 1u,
                                                   abort_flag, args.err, kDevErrTimeoutEpilogue));
@@ -960,8 +987,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(WS_THREADS, 1)
           __syncwarp();
           if (lane == 0) mbar_arrive_cluster(mapa_shared(bar_tempty + 8 * gp, 0));
         }
-        epilogue_chunk(args, row, col0, *reinterpret_cast<const uint32_t(*)[32]>(v));
-        epilogue_chunk(args, row, col0 + 32, *reinterpret_cast<const uint32_t(*)[32]>(v + 32));
+        const int rpos = t == 0 ? rpos0 : rpos1;
+        epilogue_chunk(args, row, col0, *reinterpret_cast<const uint32_t(*)[32]>(v), rpos);
+        epilogue_chunk(args, row, col0 + 32, *reinterpret_cast<const uint32_t(*)[32]>(v + 32),
+                       rpos);
       }
       return true;
     };
@@ -1167,7 +1196,7 @@ sam3_status_t validate(sam3_ctx_t* ctx, const void* x, int m, int k, int n, cons
 sam3_status_t gemm_palette(sam3_ctx_t* ctx, const uint16_t* x, int m, int k, const uint8_t* idx,
                            const uint16_t* palette, const uint16_t* bias, int n, int epi,
                            const uint16_t* residual, const float* rope, int rope_rows,
-                           uint16_t* y) {
+                           uint16_t* y, const int32_t* rope_pos) {
   sam3_status_t st = validate(ctx, x, m, k, n, y);
   if (st != SAM3_OK) return st;
   if (!idx || !palette) return set_error(ctx, SAM3_ERR_INVALID_ARG, "linear: null idx/palette");
@@ -1179,7 +1208,7 @@ sam3_status_t gemm_palette(sam3_ctx_t* ctx, const uint16_t* x, int m, int k, con
     return set_error(ctx, SAM3_ERR_INVALID_ARG, "linear: residual epilogue needs aligned residual");
   int qk_cols = 0;
   if (epi == SAM3_EPI_BIAS_ROPE_QKV) {
-    if (!rope || rope_rows <= 0 || !aligned16(rope))
+    if (!rope || (rope_rows <= 0 && !rope_pos) || !aligned16(rope))
       return set_error(ctx, SAM3_ERR_INVALID_ARG, "linear: RoPE epilogue needs a table");
     if (n % (3 * 64))
       return set_error(ctx, SAM3_ERR_SHAPE, "linear: RoPE epilogue needs n = 3*heads*64");
@@ -1193,6 +1222,7 @@ sam3_status_t gemm_palette(sam3_ctx_t* ctx, const uint16_t* x, int m, int k, con
   a.bias = reinterpret_cast<const __half*>(bias);
   a.residual = reinterpret_cast<const __half*>(residual);
   a.rope = rope;
+  a.rope_pos = epi == SAM3_EPI_BIAS_ROPE_QKV ? rope_pos : nullptr;
   a.palette = reinterpret_cast<const __half*>(palette);
   a.y = reinterpret_cast<__half*>(y);
   a.err = ctx->dev_err;

@@ -38,8 +38,13 @@ struct sam3_ctx {
   float* scores = nullptr;      // [B*S]
   float* rope = nullptr;        // [S, 32, 2]
   float* rope_pruned = nullptr; // [B*keep, 32, 2]
-  float* rope_win = nullptr;    // [S+1, 32, 2] window-major table of the windowed encoder
-  int rope_win_key = 0;         // window size the table was built for (0: none)
+  // Axial form of the grid table for the QKV GEMM epilogue: rope_axial[c][i]
+  // = pair i (0..15) at coordinate c, and per row the coordinates x | y << 16.
+  float* rope_axial = nullptr;        // [grid, 16, 2]
+  int32_t* rope_pos_grid = nullptr;   // [B*S] grid order
+  int32_t* rope_pos_win = nullptr;    // [B*(S+1)] window-major, -1 for the class token
+  int32_t* rope_pos_pruned = nullptr; // [B*keep] the kept tokens
+  int rope_win_key = 0;               // window size rope_pos_win was built for (0: none)
   int32_t* idx = nullptr;       // [B*keep]
   uint16_t* image = nullptr;    // [B, H, W, 3] staging for the host API
   uint16_t* feats = nullptr;    // [B*keep, D] staging for the host API
@@ -88,7 +93,7 @@ EncodeTiledFn encode_tiled();
 sam3_status_t gemm_palette(sam3_ctx_t* ctx, const uint16_t* x, int m, int k,
                            const uint8_t* idx, const uint16_t* palette, const uint16_t* bias,
                            int n, int epi, const uint16_t* residual, const float* rope,
-                           int rope_rows, uint16_t* y);
+                           int rope_rows, uint16_t* y, const int32_t* rope_pos = nullptr);
 sam3_status_t gemm_dense(sam3_ctx_t* ctx, const uint16_t* x, int m, int k, const uint16_t* w,
                          const uint16_t* bias, int n, uint16_t* y,
                          int prof_class = SAM3_PROF_PATCH);
@@ -102,6 +107,11 @@ sam3_status_t attention_grouped(sam3_ctx_t* ctx, const uint16_t* qkv, int images
                                 int seq, int img_rows, int first_row, int heads, int head_dim,
                                 float scale, uint16_t* o);
 sam3_status_t rope_table(sam3_ctx_t* ctx, int gh, int gw, int hd, float theta, float* t);
+// Once per context: the grid table (ctx->rope), its axial form and the
+// grid-order row coordinates for max_batch images.
+sam3_status_t rope_setup(sam3_ctx_t* ctx);
+// out[i] = coordinates x | y << 16 of grid token idx[i] (grid width gw).
+sam3_status_t rope_pos_from_idx(sam3_ctx_t* ctx, const int32_t* idx, int n, int gw, int32_t* out);
 sam3_status_t prune(sam3_ctx_t* ctx, const uint16_t* x, int batch, int seq, int d, int keep,
                     int norm, int order, const float* rope_in, int rope_rows, int rope_cols,
                     uint16_t* feats, float* rope_out, int32_t* idx, float* scores_scratch);

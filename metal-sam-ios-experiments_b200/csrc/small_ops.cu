@@ -113,6 +113,31 @@ __global__ void rope_table_kernel(float* __restrict__ t, int gh, int gw, int hd,
   row[quarter + i] = make_float2(cosf(ay), sinf(ay));
 }
 
+// Axial form of the table: a[c][i] = pair i (i < 16) at coordinate c. The
+// row-index half of the table uses the same frequencies and formula as the
+// column-index half, so row c (h = 0, w = c) gives coordinate c for both
+// halves bit for bit; rows h*gw (w = 0) cover c >= gw on taller grids.
+__global__ void rope_axial_kernel(const float2* __restrict__ t, int gw, float2* __restrict__ a) {
+  const int c = blockIdx.x, i = threadIdx.x;
+  a[c * 16 + i] = c < gw ? t[(size_t)c * 32 + i] : t[(size_t)c * gw * 32 + 16 + i];
+}
+
+// pos[r] = coordinates of grid token r % per, x | y << 16.
+__global__ void rope_pos_grid_kernel(int32_t* __restrict__ pos, int rows, int per, int gw) {
+  const int r = blockIdx.x * blockDim.x + threadIdx.x;
+  if (r >= rows) return;
+  const int p = r % per;
+  pos[r] = (p % gw) | ((p / gw) << 16);
+}
+
+__global__ void rope_pos_idx_kernel(const int32_t* __restrict__ idx, int n, int gw,
+                                    int32_t* __restrict__ pos) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const int p = idx[i];
+  pos[i] = (p % gw) | ((p / gw) << 16);
+}
+
 // Reference: apply_rope_2d_batch, Metal/RoPE.metal:111-153 (packed QKV row,
 // q and k rotated, v untouched).
 __global__ void rope_apply_kernel(__half2* __restrict__ qkv, int m, int dim, int hd,
@@ -414,6 +439,34 @@ sam3_status_t rope_table(sam3_ctx_t* ctx, int gh, int gw, int hd, float theta, f
   rope_table_kernel<<<blocks_for((long long)gh * gw, per), dim3(quarter, per), 0, ctx->stream>>>(
       t, gh, gw, hd, theta);
   return check_launch(ctx, "rope_table_kernel");
+}
+
+sam3_status_t rope_setup(sam3_ctx_t* ctx) {
+  if (ctx->rope_ready) return SAM3_OK;
+  const sam3_encoder_config_t& c = ctx->cfg;
+  const int grid = c.image_size / c.patch, S = grid * grid;
+  const int hd = c.embed_dim / c.num_heads;
+  sam3_status_t st = rope_table(ctx, grid, grid, hd, c.rope_theta, ctx->rope);
+  if (st != SAM3_OK) return st;
+  if (hd == 64) {  // the axial form serves the QKV epilogue (head_dim 64)
+    ProfScope prof(ctx, SAM3_PROF_OTHER, 0.0, 2.0 * grid * 16 * 8);
+    rope_axial_kernel<<<grid, 16, 0, ctx->stream>>>(reinterpret_cast<const float2*>(ctx->rope),
+                                                     grid, reinterpret_cast<float2*>(ctx->rope_axial));
+    if ((st = check_launch(ctx, "rope_axial_kernel")) != SAM3_OK) return st;
+    const int rows = std::max(1, c.max_batch) * S;
+    rope_pos_grid_kernel<<<blocks_for(rows, 256), 256, 0, ctx->stream>>>(ctx->rope_pos_grid, rows,
+                                                                         S, grid);
+    if ((st = check_launch(ctx, "rope_pos_grid_kernel")) != SAM3_OK) return st;
+  }
+  ctx->rope_ready = 1;
+  return SAM3_OK;
+}
+
+sam3_status_t rope_pos_from_idx(sam3_ctx_t* ctx, const int32_t* idx, int n, int gw, int32_t* out) {
+  if (n <= 0) return SAM3_OK;
+  ProfScope prof(ctx, SAM3_PROF_PRUNE, 0.0, 8.0 * n);
+  rope_pos_idx_kernel<<<blocks_for(n, 256), 256, 0, ctx->stream>>>(idx, n, gw, out);
+  return check_launch(ctx, "rope_pos_idx_kernel");
 }
 
 sam3_status_t prune(sam3_ctx_t* ctx, const uint16_t* x, int batch, int seq, int d, int keep,

@@ -17,8 +17,9 @@
 // window), window 1's, ... Every per-token operator ignores the order; a
 // windowed block is attention over contiguous row groups (the grouped form of
 // the attention kernel), a global block plain attention over all rows, and the
-// RoPE table is permuted the same way once (identity row for the class
-// token). The grid order comes back in the last kernel.
+// QKV epilogue's per-row RoPE coordinates are laid out the same way once
+// (no rotation for the class token). The grid order comes back in the last
+// kernel.
 #include <algorithm>
 
 #include "common.cuh"
@@ -78,18 +79,18 @@ __global__ void __launch_bounds__(128) win_embed_kernel(
     dst[c] = __float2half_rn(__half2float(src[c]) + upsampled_pos(pos, pg, grid, g, c, dim));
 }
 
-// Window-major RoPE table: identity for the class token, the grid table's
-// row of each patch token otherwise. hd/2 (cos, sin) pairs per row.
-__global__ void win_rope_kernel(const float* __restrict__ rope, int grid, int window, int pairs,
-                                float* __restrict__ out) {
-  const int p = blockIdx.x;
-  float2* dst = reinterpret_cast<float2*>(out) + (size_t)p * pairs;
+// Row coordinates for the axial RoPE epilogue in window-major order:
+// -1 (no rotation) for the class token, x | y << 16 of the grid token otherwise.
+__global__ void win_rope_pos_kernel(int32_t* __restrict__ pos, int rows, int grid, int window) {
+  const int r = blockIdx.x * blockDim.x + threadIdx.x;
+  if (r >= rows) return;
+  const int T = grid * grid + 1, p = r % T;
   if (p == 0) {
-    for (int j = threadIdx.x; j < pairs; j += blockDim.x) dst[j] = make_float2(1.f, 0.f);
+    pos[r] = -1;
     return;
   }
-  const float2* src = reinterpret_cast<const float2*>(rope) + (size_t)grid_token(p, grid, window) * pairs;
-  for (int j = threadIdx.x; j < pairs; j += blockDim.x) dst[j] = src[j];
+  const int g = grid_token(p, grid, window);
+  pos[r] = (g % grid) | ((g / grid) << 16);
 }
 
 // out[b, g] (grid order, no class token) = x[b, p(g)].
@@ -142,13 +143,12 @@ sam3_status_t windowed_encoder_run(sam3_ctx_t* ctx, const uint16_t* image, int b
   const int rows = batch * T;
   if ((size_t)rows > ctx->token_rows)
     return set_error(ctx, SAM3_ERR_SHAPE, "windowed encoder: %d rows exceed the workspace", rows);
-  if (!ctx->rope_ready) {
-    if ((st = rope_table(ctx, grid, grid, hd, c.rope_theta, ctx->rope)) != SAM3_OK) return st;
-    ctx->rope_ready = 1;
-  }
+  if ((st = rope_setup(ctx)) != SAM3_OK) return st;
   if (ctx->rope_win_key != win) {
-    win_rope_kernel<<<T, 32, 0, ctx->stream>>>(ctx->rope, grid, win, hd / 2, ctx->rope_win);
-    if ((st = check_launch(ctx, "win_rope_kernel")) != SAM3_OK) return st;
+    const int prow = c.max_batch * T;
+    win_rope_pos_kernel<<<(prow + 255) / 256, 256, 0, ctx->stream>>>(ctx->rope_pos_win, prow, grid,
+                                                                     win);
+    if ((st = check_launch(ctx, "win_rope_pos_kernel")) != SAM3_OK) return st;
     ctx->rope_win_key = win;
   }
   // patch tokens (grid order) into the attention scratch, then the
@@ -172,8 +172,8 @@ sam3_status_t windowed_encoder_run(sam3_ctx_t* ctx, const uint16_t* image, int b
     if ((st = layernorm(ctx, x, rows, D, bw->ln1_gamma, bw->ln1_beta, c.ln_eps, ctx->ln)) != SAM3_OK)
       return st;
     if ((st = gemm_palette(ctx, ctx->ln, rows, D, bw->qkv.idx, bw->qkv.palette, bw->qkv.bias,
-                           3 * D, SAM3_EPI_BIAS_ROPE_QKV, nullptr, ctx->rope_win, T,
-                           ctx->qkv)) != SAM3_OK)
+                           3 * D, SAM3_EPI_BIAS_ROPE_QKV, nullptr, ctx->rope_axial, 0,
+                           ctx->qkv, ctx->rope_pos_win)) != SAM3_OK)
       return st;
     if (global) {
       st = attention_grouped(ctx, ctx->qkv, batch, 1, T, T, 0, H, hd, 0.125f, ctx->attn);

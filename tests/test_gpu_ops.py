@@ -845,6 +845,14 @@ def test_windowed_encoder_rejects_bad_windows(ctx, sam3, oracle):
     w.window = 4
     with pytest.raises(sam3.SAM3Error):  # batch above max_batch
         ctx.windowed_encoder_forward(ctx.alloc(3 * 112 * 112 * 3 * 2), 3, w, out)
+    pos = w.pos_embed
+    w.pos_embed = None
+    with pytest.raises(sam3.SAM3Error) as e:  # no positional table
+        ctx.windowed_encoder_forward(ctx.upload(img), 1, w, out)
+    assert e.value.status == sam3.ERR_INVALID_ARG
+    w.pos_embed = pos
+    ctx.windowed_encoder_forward(ctx.upload(img), 1, w, out)  # the context still works
+    ctx.sync()
 
 
 @pytest.mark.parametrize("hidden", [4096, 4736])
@@ -992,3 +1000,44 @@ def test_fault_environment_variable_sets_new_contexts(sam3, tmp_path):
     r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, env=env,
                        timeout=300)
     assert r.returncode == 0 and "ok" in r.stdout, r.stdout + r.stderr
+
+
+# ------------------------------------------------------------------ axial RoPE in the encoder
+@pytest.mark.parametrize("prune_after", [0, 1])
+def test_encoder_axial_rope_bit_exact_with_table_entry_points(sam3, oracle, prune_after):
+    # The encoders rotate q/k in the QKV epilogue from the axial form of the
+    # grid table and per-row coordinates (grid order; after pruning the kept
+    # tokens' coordinates). The public entry points take the full table (and
+    # the pruned rows' gathered table). Both must give the same bits.
+    cfg = sam3.default_config()
+    with sam3.Context(0, embed_dim=256, num_heads=4, mlp_hidden=512, num_blocks=2, patch=14,
+                      image_size=112, prune_after_block=prune_after, keep_tokens=32,
+                      max_batch=2) as c:
+        blocks, pw, pb = _small_encoder(oracle, seed=37)
+        w = _upload_encoder(c, sam3, blocks, pw, pb)
+        img = c.upload(oracle.gen_uniform(37, 77, (2, 112, 112, 3), -1.0, 1.0))
+        rows = 32 if prune_after else 64
+        feats, idx = c.alloc(2 * rows * 256 * 2), c.alloc(2 * rows * 4)
+        c.encoder_forward(img, 2, w, feats, idx)
+        x = c.alloc(2 * 64 * 256 * 2)
+        c.patch_embed(img, 2, 112, 112, c.upload(pw), c.upload(pb), 14, 256, x)
+        table = c.alloc(64 * 32 * 2 * 4)
+        c.rope_table(8, 8, 64, 10000.0, table)
+        bw = [upload_block(c, sam3, b) for b in blocks]
+        c.vit_block(x, 2, 64, bw[0], table, 64)
+        if prune_after:
+            xp, ip = c.alloc(2 * 32 * 256 * 2), c.alloc(2 * 32 * 4)
+            rp = c.alloc(2 * 32 * 32 * 2 * 4)
+            c.prune(x, 2, 64, 256, 32, cfg.score_norm, cfg.keep_order, xp, ip, table, 64, 64, rp)
+            c.vit_block(xp, 2, 32, bw[1], rp, 2 * 32)
+            ref, ref_idx = xp, ip
+        else:
+            c.vit_block(x, 2, 64, bw[1], table, 64)
+            ref, ref_idx = x, None
+        c.sync()
+        got = c.download(feats, (2, rows, 256), F16)
+        want = c.download(ref, (2, rows, 256), F16)
+        assert np.array_equal(got.view(np.uint16), want.view(np.uint16))
+        if ref_idx is not None:
+            assert np.array_equal(c.download(idx, (2, rows), np.int32),
+                                  c.download(ref_idx, (2, rows), np.int32))
