@@ -186,19 +186,18 @@ __global__ void __launch_bounds__(THREADS, 2)
     // once that PV has read P_j, S_(j%2) = Q K_(j+2)^T.
     if (lane == 0) {
       bool issued_any = false, ok = true;
-      const uint32_t q_addr = sbase + OFF_Q;
+      const uint64_t dq = umma_desc_sw128(sbase + OFF_Q);
       auto issue_qk = [&](int j) -> bool {
         const int s = j % STAGES;
         if (!mbar_wait(bar_kv_full + 8 * s, (uint32_t)(j / STAGES) & 1u, abort_flag, args.err,
                        kDevErrTimeoutAttn))
           return false;
         tc_fence_after();
-        const uint32_t k_addr = sbase + OFF_KV + s * KV_STAGE;
+        const uint64_t dk = umma_desc_sw128(sbase + OFF_KV + s * KV_STAGE);
         const uint32_t d = tmem + COL_S0 + (uint32_t)((j & 1) * BKV);
 #pragma unroll
         for (int kk = 0; kk < HD / 16; ++kk)
-          umma_f16_ss(d, umma_desc_sw128(q_addr + kk * 32), umma_desc_sw128(k_addr + kk * 32),
-                      IDESC_S, kk != 0);
+          umma_f16_ss(d, desc_advance(dq, kk * 32), desc_advance(dk, kk * 32), IDESC_S, kk != 0);
         umma_commit(bar_s_full + 8 * (j & 1));
         issued_any = true;
         return true;
@@ -212,12 +211,12 @@ __global__ void __launch_bounds__(THREADS, 2)
                        kDevErrTimeoutAttn))
           break;
         tc_fence_after();
-        const uint32_t v_addr = sbase + OFF_KV + s * KV_STAGE + KV_BYTES;
+        const uint64_t dv = desc_v_ones(sbase + OFF_KV + s * KV_STAGE + KV_BYTES);
         const uint32_t p_col = tmem + COL_S0 + (uint32_t)((j & 1) * BKV);
 #pragma unroll
         for (int kk = 0; kk < BKV / 16; ++kk)
-          umma_f16_ts(tmem + COL_O, p_col + kk * 8, desc_v_ones(v_addr + kk * 2048),
-                      IDESC_O, (j | kk) != 0);
+          umma_f16_ts(tmem + COL_O, p_col + kk * 8, desc_advance(dv, kk * 2048), IDESC_O,
+                      (j | kk) != 0);
         umma_commit(bar_o_full);
         umma_commit(bar_kv_empty + 8 * s);
         if (j == ntiles - 1) umma_commit(bar_o_done);

@@ -198,6 +198,15 @@ __device__ __forceinline__ uint64_t umma_desc_sw128_mn(uint32_t saddr) {
   return d;
 }
 
+// The same descriptor `bytes` further on in shared memory: the start address
+// sits in bits [0,14) as addr >> 4, and shared addresses stay below 256 KB,
+// so a 32-bit add on the low word never carries out of the field. (The MMA
+// issuing thread paces its kernel; one add per operand instead of a rebuild.)
+__device__ __forceinline__ uint64_t desc_advance(uint64_t d, uint32_t bytes) {
+  const uint32_t lo = static_cast<uint32_t>(d) + (bytes >> 4);
+  return (d & 0xFFFFFFFF00000000ull) | lo;
+}
+
 // Instruction descriptor, kind::f16: D f32, A/B f16, both K-major.
 __host__ __device__ constexpr uint32_t umma_idesc_f16(int m, int n, int b_mn_major = 0) {
   return (1u << 4) | (0u << 7) | (0u << 10) | (0u << 15) |

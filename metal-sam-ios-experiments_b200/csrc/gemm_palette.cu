@@ -636,15 +636,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(WS_THREADS, 1)
             break;
           }
           tc_fence_after();
+          const uint64_t da = umma_desc_sw128(sbase + WS_OFF_A + s * WS_A_STAGE);
+          const uint64_t db = umma_desc_sw128(sbase + WS_OFF_SLAB + ks * WS_KSPLIT * WS_SLAB_KB);
 #pragma unroll
           for (int h = 0; h < WS_KSPLIT; ++h) {
-            const int kb = ks * WS_KSPLIT + h;
-            const uint32_t a_addr = sbase + WS_OFF_A + s * WS_A_STAGE + h * WS_A_BOX;
-            const uint32_t b_addr = sbase + WS_OFF_SLAB + kb * WS_SLAB_KB;
 #pragma unroll
             for (int kk = 0; kk < WS_BK / 16; ++kk)
-              umma_f16_ss_cg2(d_tmem, umma_desc_sw128(a_addr + kk * 32),
-                              umma_desc_sw128(b_addr + kk * 32), WS_IDESC, (kb | kk) != 0);
+              umma_f16_ss_cg2(d_tmem, desc_advance(da, h * WS_A_BOX + kk * 32),
+                              desc_advance(db, h * WS_SLAB_KB + kk * 32), WS_IDESC,
+                              (ks | h | kk) != 0);
           }
           umma_commit_cg2_mc(bar_a_empty + 8 * s, 0x3);
           issued_any = true;
@@ -911,16 +911,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(WS_THREADS, 1)
                 break;
               }
               tc_fence_after();
+              const uint64_t da = umma_desc_sw128(sbase + WSC_OFF_A + s * WS_A_STAGE);
+              const uint64_t db = umma_desc_sw128(sbase + WSC_OFF_SLAB + b * WSC_BUF +
+                                                  ks * WS_KSPLIT * WS_SLAB_KB);
 #pragma unroll
               for (int h = 0; h < WS_KSPLIT; ++h) {
-                const int kb = ks * WS_KSPLIT + h;
-                const uint32_t a_addr = sbase + WSC_OFF_A + s * WS_A_STAGE + h * WS_A_BOX;
-                const uint32_t b_addr = sbase + WSC_OFF_SLAB + b * WSC_BUF + kb * WS_SLAB_KB;
 #pragma unroll
                 for (int kk = 0; kk < WS_BK / 16; ++kk)
-                  umma_f16_ss_cg2(d_tmem, umma_desc_sw128(a_addr + kk * 32),
-                                  umma_desc_sw128(b_addr + kk * 32), WS_IDESC,
-                                  (c | kb | kk) != 0);
+                  umma_f16_ss_cg2(d_tmem, desc_advance(da, h * WS_A_BOX + kk * 32),
+                                  desc_advance(db, h * WS_SLAB_KB + kk * 32), WS_IDESC,
+                                  (c | ks | h | kk) != 0);
               }
               umma_commit_cg2_mc(bar_a_empty + 8 * s, 0x3);
               issued_any = true;
