@@ -106,8 +106,11 @@ __device__ __forceinline__ void epilogue_prefetch(const GemmArgs& a, int row, in
 }
 
 // Epilogue for 32 consecutive accumulator columns of one output row.
+// res: the chunk's 32 residual values (4 x 16 bytes) already in registers,
+// or null to load them here.
 __device__ __forceinline__ void epilogue_chunk(const GemmArgs& a, int row, int col0,
-                                               const uint32_t (&v)[32], int rpos) {
+                                               const uint32_t (&v)[32], int rpos,
+                                               const uint4* res = nullptr) {
   float f[32];
 #pragma unroll
   for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(v[j]);
@@ -150,7 +153,7 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs& a, int row, int c
   if (a.epi == SAM3_EPI_BIAS_RESIDUAL) {
     const uint4* rp = reinterpret_cast<const uint4*>(a.residual + off);
 #pragma unroll
-    for (int q = 0; q < 4; ++q) add_half8(f + 8 * q, rp[q]);
+    for (int q = 0; q < 4; ++q) add_half8(f + 8 * q, res ? res[q] : rp[q]);
   }
   uint4* yp = reinterpret_cast<uint4*>(a.y + off);
 #pragma unroll
@@ -723,6 +726,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(WS_THREADS, 1)
       }
       epilogue_prefetch(args, row, col0);
       const int rpos = rope_pos_of(args, row);
+      // The residual row's 64 values go straight to registers while the
+      // accumulator is computed: 256 threads' lines (32 KB) would not stay in
+      // the L1 left beside this kernel's shared memory.
+      uint4 res[8];
+      const bool has_res = args.epi == SAM3_EPI_BIAS_RESIDUAL && row < args.m;
+      if (has_res) {
+        const uint4* rp = reinterpret_cast<const uint4*>(args.residual + (size_t)row * args.n + col0);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) res[q] = rp[q];
+      }
       ok = __all_sync(0xffffffffu, mbar_wait_cluster(bar_tfull + 8 * acc, use, abort_flag,
                                                      args.err, kDevErrTimeoutEpilogue));
       if (!ok) break;
@@ -736,8 +749,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(WS_THREADS, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(mapa_shared(bar_tempty + 8 * acc, 0));
-      epilogue_chunk(args, row, col0, *reinterpret_cast<const uint32_t(*)[32]>(v), rpos);
-      epilogue_chunk(args, row, col0 + 32, *reinterpret_cast<const uint32_t(*)[32]>(v + 32), rpos);
+      epilogue_chunk(args, row, col0, *reinterpret_cast<const uint32_t(*)[32]>(v), rpos,
+                     has_res ? res : nullptr);
+      epilogue_chunk(args, row, col0 + 32, *reinterpret_cast<const uint32_t(*)[32]>(v + 32), rpos,
+                     has_res ? res + 4 : nullptr);
     }
   }
 
