@@ -8,6 +8,7 @@
     python microbench.py preprocess --batch 8
     python microbench.py neck --batch 8          (restoreSpatial + neck, 72x72, 1024 -> 256)
     python microbench.py windowed --batch 8      (checkpoint-faithful encoder, 32 blocks, 1008^2)
+    python microbench.py encoder --batch 8 [--blocks 32]  (pruned encoder, device buffers)
 
 Inputs are synthetic device tensors (torch is used only to allocate and fill
 them); each iteration calls the operator through the C ABI; timings are CUDA
@@ -42,7 +43,7 @@ def main():
 
     ap = argparse.ArgumentParser()
     ap.add_argument("op", choices=("gemm", "attention", "layernorm", "dequant", "patch",
-                                   "preprocess", "neck", "windowed"))
+                                   "preprocess", "neck", "windowed", "encoder"))
     ap.add_argument("--rgba", action="store_true",
                     help="patch: f32 RGBA frames, normalisation fused into the patch gather")
     ap.add_argument("--m", type=int, default=41472)
@@ -53,6 +54,7 @@ def main():
     ap.add_argument("--seq", type=int, default=5184)
     ap.add_argument("--heads", type=int, default=16)
     ap.add_argument("--hidden", type=int, default=4096, help="windowed: MLP width (checkpoint 4736)")
+    ap.add_argument("--blocks", type=int, default=32, help="encoder: blocks (pruned after half)")
     ap.add_argument("--iters", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     a = ap.parse_args()
@@ -138,6 +140,37 @@ def main():
         ms = prof["ms"] / calls
         print(json.dumps({"op": "neck", "batch": a.batch, "us_per_call": ms * 1e3,
                           "tflops_convs": flops / (ms * 1e-3) / 1e12}))
+        ctx.close()
+        return
+    elif a.op == "encoder":
+        sys.path.insert(0, os.path.dirname(HERE))
+        import bench  # the benchmark's synthetic weights
+        ctx.close()
+        prune_after = a.blocks // 2 if a.blocks > 1 else 0
+        ctx = sam3.Context(0, max_batch=a.batch, num_blocks=a.blocks,
+                           prune_after_block=prune_after)
+        bench.BLOCKS = a.blocks
+        w = bench.make_weights(torch, sam3, dev, 1234)
+        img = (torch.rand((a.batch, 1008, 1008, 3), generator=g, device=dev) * 2 - 1).half()
+        keep = ctx.out_tokens
+        feats = torch.empty((a.batch, keep, 1024), dtype=torch.float16, device=dev)
+        idx = torch.empty((a.batch, keep), dtype=torch.int32, device=dev)
+        fn = lambda: ctx.encoder_forward(img, a.batch, w, feats, idx)
+        prof = run(fn)
+        stream = torch.cuda.ExternalStream(ctx.stream, device=dev)
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ctx.sync()
+        ev0.record(stream)
+        for _ in range(a.iters):
+            fn()
+        ev1.record(stream)
+        ev1.synchronize()
+        ms = ev0.elapsed_time(ev1) / a.iters
+        print(json.dumps({
+            "op": "encoder", "batch": a.batch, "blocks": a.blocks, "ms_per_call": ms,
+            "images_per_s": a.batch / (ms * 1e-3),
+            "gemm_tflops": prof["gemm"]["flops"] / (prof["gemm"]["ms"] * 1e-3) / 1e12,
+            "attention_tflops": prof["attention"]["flops"] / (prof["attention"]["ms"] * 1e-3) / 1e12}))
         ctx.close()
         return
     elif a.op == "windowed":
