@@ -382,6 +382,15 @@ sam3_status_t sam3_windowed_encoder_forward(sam3_ctx_t* ctx, const uint16_t* ima
                                             const sam3_windowed_encoder_weights_t* w,
                                             uint16_t* out);
 
+/* Same from f32 RGBA camera frames [batch, S, S, 4] in [0, 1] on the device,
+ * the ImageNet normalisation fused into the patch embedding (as
+ * sam3_encoder_forward_rgba). Reference: SAM3Predictor.setImage's
+ * preprocessing (SAM3Predictor.swift:332-341) feeding SAM3Encoder's graph
+ * (SAM3Encoder.swift:259-366). */
+sam3_status_t sam3_windowed_encoder_forward_rgba(sam3_ctx_t* ctx, const float* rgba, int32_t batch,
+                                                 const sam3_windowed_encoder_weights_t* w,
+                                                 uint16_t* out);
+
 /* ---- failure detection and fault injection ------------------------------
  * Every wait inside a kernel (mbarriers of the TMA / MMA pipelines) is bounded
  * (2 s); on expiry the kernel records a code in the context's device error

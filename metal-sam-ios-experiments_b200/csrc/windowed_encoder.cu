@@ -128,7 +128,9 @@ sam3_status_t check_windowed_weights(sam3_ctx_t* ctx, const sam3_windowed_encode
 
 }  // namespace
 
-sam3_status_t windowed_encoder_run(sam3_ctx_t* ctx, const uint16_t* image, int batch,
+// image: fp16 RGB NHWC, or f32 RGBA NHWC in [0, 1] normalised in the patch
+// gather (rgba = true).
+sam3_status_t windowed_encoder_run(sam3_ctx_t* ctx, const void* image, bool rgba, int batch,
                                    const sam3_windowed_encoder_weights_t* w, uint16_t* out) {
   const sam3_encoder_config_t& c = ctx->cfg;
   if (!image || !out) return set_error(ctx, SAM3_ERR_INVALID_ARG, "windowed encoder: null pointer");
@@ -153,7 +155,7 @@ sam3_status_t windowed_encoder_run(sam3_ctx_t* ctx, const uint16_t* image, int b
   }
   // patch tokens (grid order) into the attention scratch, then the
   // window-major residual stream with the class token and positions
-  if ((st = patch_embed(ctx, image, false, batch, c.image_size, c.image_size, w->patch_w,
+  if ((st = patch_embed(ctx, image, rgba, batch, c.image_size, c.image_size, w->patch_w,
                         w->patch_b, c.patch, D, ctx->attn, ctx->cols, ctx->patch_wp)) != SAM3_OK)
     return st;
   {
@@ -215,5 +217,16 @@ extern "C" sam3_status_t sam3_windowed_encoder_forward(sam3_ctx_t* ctx, const ui
   SAM3_CHECK_CTX(ctx);
   cudaSetDevice(ctx->device);
   if (!aligned16(out)) return set_error(ctx, SAM3_ERR_INVALID_ARG, "windowed encoder: out must be 16-byte aligned");
-  return windowed_encoder_run(ctx, image, batch, w, out);
+  return windowed_encoder_run(ctx, image, false, batch, w, out);
+}
+
+extern "C" sam3_status_t sam3_windowed_encoder_forward_rgba(
+    sam3_ctx_t* ctx, const float* rgba, int32_t batch, const sam3_windowed_encoder_weights_t* w,
+    uint16_t* out) {
+  SAM3_CHECK_CTX(ctx);
+  cudaSetDevice(ctx->device);
+  if (!aligned16(out) || !rgba || !aligned16(rgba))
+    return set_error(ctx, SAM3_ERR_INVALID_ARG,
+                     "windowed encoder: rgba and out must be 16-byte aligned pointers");
+  return windowed_encoder_run(ctx, rgba, true, batch, w, out);
 }

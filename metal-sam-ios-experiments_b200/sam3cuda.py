@@ -117,6 +117,7 @@ SIGNATURES = {
     "sam3_restore_spatial": (_S, [_P, _P, _P, _I, _I, _I, _I, _P]),
     "sam3_neck": (_S, [_P, _P, _I, _I, _I, C.POINTER(NeckWeights), _P]),
     "sam3_windowed_encoder_forward": (_S, [_P, _P, _I, C.POINTER(WindowedEncoderWeights), _P]),
+    "sam3_windowed_encoder_forward_rgba": (_S, [_P, _P, _I, C.POINTER(WindowedEncoderWeights), _P]),
     "sam3_encoder_forward_host_pipelined": (_S, [_P, _P, _I, C.POINTER(EncoderWeights), _P, _P]),
     "sam3_encoder_forward_host": (_S, [_P, _P, _I, C.POINTER(EncoderWeights), _P, _P]),
     "sam3_encoder_out_tokens": (C.c_int32, [_P]),
@@ -352,6 +353,10 @@ class Context:
     def windowed_encoder_forward(self, image, batch, w: WindowedEncoderWeights, out):
         self._check(lib.sam3_windowed_encoder_forward(self.handle, ptr(image), batch, C.byref(w),
                                                       ptr(out)))
+
+    def windowed_encoder_forward_rgba(self, rgba, batch, w: WindowedEncoderWeights, out):
+        self._check(lib.sam3_windowed_encoder_forward_rgba(self.handle, ptr(rgba), batch,
+                                                           C.byref(w), ptr(out)))
 
     def encoder_forward_host(self, image_host: np.ndarray, batch, w: EncoderWeights,
                              feats_host: np.ndarray, idx_host: np.ndarray):

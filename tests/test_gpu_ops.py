@@ -1041,3 +1041,25 @@ def test_encoder_axial_rope_bit_exact_with_table_entry_points(sam3, oracle, prun
         if ref_idx is not None:
             assert np.array_equal(c.download(idx, (2, rows), np.int32),
                                   c.download(ref_idx, (2, rows), np.int32))
+
+
+def test_windowed_encoder_rgba_equals_preprocess_then_rgb(ctx, sam3, oracle):
+    # camera frames: normalisation fused into the patch gather gives the same
+    # bits as sam3_preprocess_rgba followed by the fp16 entry point
+    blocks, pw, pb, cls, pos, img, w = _windowed_setup(ctx, sam3, oracle, 74, 256, 512, 8, 4,
+                                                       112, 2)
+    rgba = np.random.default_rng(74).random((2, 112, 112, 4), dtype=np.float32)
+    drgba = ctx.upload(rgba)
+    rgb = ctx.alloc(2 * 112 * 112 * 3 * 2)
+    ctx.preprocess_rgba(drgba, 2, 112, 112, rgb)
+    a, b = ctx.alloc(2 * 64 * 256 * 2), ctx.alloc(2 * 64 * 256 * 2)
+    ctx.windowed_encoder_forward(rgb, 2, w, a)
+    ctx.windowed_encoder_forward_rgba(drgba, 2, w, b)
+    ctx.sync()
+    ga = ctx.download(a, (2, 64, 256), F16)
+    gb = ctx.download(b, (2, 64, 256), F16)
+    assert np.array_equal(ga.view(np.uint16), gb.view(np.uint16))
+    # and against the oracle on the preprocessed frames
+    ref = oracle.windowed_encoder_forward(oracle.preprocess_rgba(rgba), blocks, pw, pb, cls, pos,
+                                          heads=4)
+    assert max_rel_err(gb, ref) < SPEC_TOL
