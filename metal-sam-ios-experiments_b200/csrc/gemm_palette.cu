@@ -68,7 +68,15 @@ struct GemmArgs {
   int rope_rows;
   int qk_cols;
   int m_tiles, total_tiles;
+  int y32;  // y is 32-byte aligned: 256-bit stores
 };
+
+// 32 bytes to global memory in one store (sm_100 256-bit access).
+__device__ __forceinline__ void st_global_v8(void* p, const uint32_t (&r)[8]) {
+  asm volatile("st.global.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(p), "r"(r[0]),
+               "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
+               : "memory");
+}
 
 __device__ __forceinline__ void add_half8(float* f, uint4 v) {
   const uint32_t w[4] = {v.x, v.y, v.z, v.w};
@@ -154,6 +162,18 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs& a, int row, int c
     const uint4* rp = reinterpret_cast<const uint4*>(a.residual + off);
 #pragma unroll
     for (int q = 0; q < 4; ++q) add_half8(f + 8 * q, res ? res[q] : rp[q]);
+  }
+  // Each lane writes its own row: 32-byte stores fill whole sectors and halve
+  // the store instructions (the epilogue's issue cost slows the whole GEMM).
+  if (a.y32) {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      uint32_t o[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) o[e] = pack_half2(f[16 * h + 2 * e], f[16 * h + 2 * e + 1]);
+      st_global_v8(a.y + off + 16 * h, o);
+    }
+    return;
   }
   uint4* yp = reinterpret_cast<uint4*>(a.y + off);
 #pragma unroll
@@ -1240,6 +1260,7 @@ sam3_status_t gemm_palette(sam3_ctx_t* ctx, const uint16_t* x, int m, int k, con
   a.rope_pos = epi == SAM3_EPI_BIAS_ROPE_QKV ? rope_pos : nullptr;
   a.palette = reinterpret_cast<const __half*>(palette);
   a.y = reinterpret_cast<__half*>(y);
+  a.y32 = (reinterpret_cast<uintptr_t>(y) & 31u) == 0;
   a.err = ctx->dev_err;
   a.m = m;
   a.n = n;
@@ -1316,6 +1337,7 @@ sam3_status_t gemm_dense(sam3_ctx_t* ctx, const uint16_t* x, int m, int k, const
   GemmArgs a{};
   a.bias = reinterpret_cast<const __half*>(bias);
   a.y = reinterpret_cast<__half*>(y);
+  a.y32 = (reinterpret_cast<uintptr_t>(y) & 31u) == 0;
   a.err = ctx->dev_err;
   a.m = m;
   a.n = n;

@@ -120,6 +120,30 @@ def test_linear_k_chunks_with_short_tail(ctx, sam3, oracle, m, n, k):
     assert max_rel_err(y, ref) < 2e-3
 
 
+@pytest.mark.parametrize("epi", [0, 1, 2])
+def test_linear_output_alignment_16_and_32_bytes(ctx, sam3, oracle, epi):
+    # a 32-byte aligned output takes 256-bit stores, a 16-byte aligned one the
+    # 128-bit path: the same bits either way
+    m, n, k = 300, 256, 256
+    x = oracle.gen_normal(9, 1, (m, k))
+    idx = oracle.gen_u8(9, 2, (n, k))
+    pal = oracle.gen_palette(9, 3, n)
+    bias = oracle.gen_normal(9, 4, (n,), 0.0, 0.01)
+    w = upload_linear(ctx, sam3, idx, pal, bias)
+    dx = ctx.upload(x)
+    dres = ctx.upload(oracle.gen_normal(9, 5, (m, n))) if epi == 2 else None
+    outs = []
+    for shift in (0, 16):
+        buf = ctx.alloc(m * n * 2 + 64)
+        ctx.linear_palette(dx, m, w, epi, buf.ptr + shift, dres, None, 0)
+        ctx.sync()
+        outs.append(ctx.download(buf.ptr + shift, (m, n), F16))
+    assert np.array_equal(outs[0].view(np.uint16), outs[1].view(np.uint16))
+    ref = oracle.linear(x, idx, pal, bias, epilogue=epi,
+                        residual=ctx.download(dres, (m, n), F16) if epi == 2 else None)
+    assert max_rel_err(outs[0], ref) < 2e-3
+
+
 def test_linear_many_tiles_gelu_and_rope(ctx, sam3, oracle):
     # more tiles than SMs, several n-tiles per CTA (palette reloads), K=4096
     m = 1000
