@@ -62,6 +62,7 @@ struct AttnArgs {
   int groups, img_rows, first_row;
   float scale_log2;
   int kv3d;  // 1: tmap_kv is the 3-D K|V map (one request per stage), 0: use 2-D boxes
+  int o32;   // out is 32-byte aligned (256-bit stores)
 };
 
 // B descriptor of the PV MMA: V (MN-major, 128B swizzle) with the ones block
@@ -320,15 +321,28 @@ __global__ void __launch_bounds__(THREADS, 2)
       const int q = q0 + r;
       if (q < seq) {
         const float inv = 1.f / __uint_as_float(o[HD]);  // sum of P, from the ones columns
-        uint4* dst = reinterpret_cast<uint4*>(args.out + (size_t)(row0 + q) * dim + h * HD);
+        __half* drow = args.out + (size_t)(row0 + q) * dim + h * HD;
+        if (args.o32) {  // 32-byte stores: whole sectors, half the instructions
 #pragma unroll
-        for (int c8 = 0; c8 < HD / 8; ++c8) {
-          uint4 w;
-          w.x = pack_half2(__uint_as_float(o[8 * c8 + 0]) * inv, __uint_as_float(o[8 * c8 + 1]) * inv);
-          w.y = pack_half2(__uint_as_float(o[8 * c8 + 2]) * inv, __uint_as_float(o[8 * c8 + 3]) * inv);
-          w.z = pack_half2(__uint_as_float(o[8 * c8 + 4]) * inv, __uint_as_float(o[8 * c8 + 5]) * inv);
-          w.w = pack_half2(__uint_as_float(o[8 * c8 + 6]) * inv, __uint_as_float(o[8 * c8 + 7]) * inv);
-          dst[c8] = w;
+          for (int c16 = 0; c16 < HD / 16; ++c16) {
+            uint32_t w[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e)
+              w[e] = pack_half2(__uint_as_float(o[16 * c16 + 2 * e]) * inv,
+                                __uint_as_float(o[16 * c16 + 2 * e + 1]) * inv);
+            st_global_v8(drow + 16 * c16, w);
+          }
+        } else {
+          uint4* dst = reinterpret_cast<uint4*>(drow);
+#pragma unroll
+          for (int c8 = 0; c8 < HD / 8; ++c8) {
+            uint4 w;
+            w.x = pack_half2(__uint_as_float(o[8 * c8 + 0]) * inv, __uint_as_float(o[8 * c8 + 1]) * inv);
+            w.y = pack_half2(__uint_as_float(o[8 * c8 + 2]) * inv, __uint_as_float(o[8 * c8 + 3]) * inv);
+            w.z = pack_half2(__uint_as_float(o[8 * c8 + 4]) * inv, __uint_as_float(o[8 * c8 + 5]) * inv);
+            w.w = pack_half2(__uint_as_float(o[8 * c8 + 6]) * inv, __uint_as_float(o[8 * c8 + 7]) * inv);
+            dst[c8] = w;
+          }
         }
       }
     }
@@ -388,6 +402,7 @@ sam3_status_t attention_tc(sam3_ctx_t* ctx, const uint16_t* qkv, int batch, int 
   a.dim = dim;
   a.scale_log2 = scale * 1.4426950408889634f;
   a.kv3d = kv3d ? 1 : 0;
+  a.o32 = (reinterpret_cast<uintptr_t>(o) & 31u) == 0;
   dim3 grid((seq + BQ - 1) / BQ, heads, batch * groups);
   const cudaError_t e = launch_pdl(attn_tc_kernel, grid, dim3(THREADS), SMEM_BYTES, ctx->stream,
                                    map, kv3d ? map_kv : map, a);

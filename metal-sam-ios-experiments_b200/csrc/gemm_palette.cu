@@ -68,15 +68,10 @@ struct GemmArgs {
   int rope_rows;
   int qk_cols;
   int m_tiles, total_tiles;
-  int y32;  // y is 32-byte aligned: 256-bit stores
+  int y32;    // y is 32-byte aligned: 256-bit stores
+  int res32;  // residual is 32-byte aligned: 256-bit loads
 };
 
-// 32 bytes to global memory in one store (sm_100 256-bit access).
-__device__ __forceinline__ void st_global_v8(void* p, const uint32_t (&r)[8]) {
-  asm volatile("st.global.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(p), "r"(r[0]),
-               "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
-               : "memory");
-}
 
 __device__ __forceinline__ void add_half8(float* f, uint4 v) {
   const uint32_t w[4] = {v.x, v.y, v.z, v.w};
@@ -159,9 +154,20 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs& a, int row, int c
   if (row >= a.m) return;
   const size_t off = (size_t)row * a.n + col0;
   if (a.epi == SAM3_EPI_BIAS_RESIDUAL) {
-    const uint4* rp = reinterpret_cast<const uint4*>(a.residual + off);
+    uint4 r[4];
+    if (res) {
 #pragma unroll
-    for (int q = 0; q < 4; ++q) add_half8(f + 8 * q, res ? res[q] : rp[q]);
+      for (int q = 0; q < 4; ++q) r[q] = res[q];
+    } else if (a.res32) {
+      ld_global_v8(a.residual + off, r[0], r[1]);
+      ld_global_v8(a.residual + off + 16, r[2], r[3]);
+    } else {
+      const uint4* rp = reinterpret_cast<const uint4*>(a.residual + off);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) r[q] = rp[q];
+    }
+#pragma unroll
+    for (int q = 0; q < 4; ++q) add_half8(f + 8 * q, r[q]);
   }
   // Each lane writes its own row: 32-byte stores fill whole sectors and halve
   // the store instructions (the epilogue's issue cost slows the whole GEMM).
@@ -752,9 +758,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(WS_THREADS, 1)
       uint4 res[8];
       const bool has_res = args.epi == SAM3_EPI_BIAS_RESIDUAL && row < args.m;
       if (has_res) {
-        const uint4* rp = reinterpret_cast<const uint4*>(args.residual + (size_t)row * args.n + col0);
+        const __half* rp = args.residual + (size_t)row * args.n + col0;
+        if (args.res32) {
 #pragma unroll
-        for (int q = 0; q < 8; ++q) res[q] = rp[q];
+          for (int q = 0; q < 4; ++q) ld_global_v8(rp + 16 * q, res[2 * q], res[2 * q + 1]);
+        } else {
+#pragma unroll
+          for (int q = 0; q < 8; ++q) res[q] = reinterpret_cast<const uint4*>(rp)[q];
+        }
       }
       ok = __all_sync(0xffffffffu, mbar_wait_cluster(bar_tfull + 8 * acc, use, abort_flag,
                                                      args.err, kDevErrTimeoutEpilogue));
@@ -1261,6 +1272,7 @@ sam3_status_t gemm_palette(sam3_ctx_t* ctx, const uint16_t* x, int m, int k, con
   a.palette = reinterpret_cast<const __half*>(palette);
   a.y = reinterpret_cast<__half*>(y);
   a.y32 = (reinterpret_cast<uintptr_t>(y) & 31u) == 0;
+  a.res32 = (reinterpret_cast<uintptr_t>(a.residual) & 31u) == 0;
   a.err = ctx->dev_err;
   a.m = m;
   a.n = n;
@@ -1338,6 +1350,7 @@ sam3_status_t gemm_dense(sam3_ctx_t* ctx, const uint16_t* x, int m, int k, const
   a.bias = reinterpret_cast<const __half*>(bias);
   a.y = reinterpret_cast<__half*>(y);
   a.y32 = (reinterpret_cast<uintptr_t>(y) & 31u) == 0;
+  a.res32 = (reinterpret_cast<uintptr_t>(a.residual) & 31u) == 0;
   a.err = ctx->dev_err;
   a.m = m;
   a.n = n;
