@@ -428,20 +428,22 @@ __device__ __forceinline__ float rcp_approx(float x) {
   asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
-// GELU(v) = v * Phi(v) = 0.5 v erfc(-v / sqrt 2), with erfc from Abramowitz &
-// Stegun, Handbook of Mathematical Functions, eq. 7.1.26: for z >= 0,
-// erfc(z) = t (a1 + t (a2 + t (a3 + t (a4 + t a5)))) exp(-z^2), t = 1/(1 + p z),
-// |error| <= 1.5e-7. One reciprocal and one exp2 on the MUFU pipe, the rest on
-// FMA; the negative side uses erfc directly (no 1 - erf cancellation).
+// GELU(v) = v * Phi(v), Phi(v) = 0.5 erfc(-v / sqrt 2), with erfc from
+// Abramowitz & Stegun, Handbook of Mathematical Functions, eq. 7.1.26: for
+// z >= 0, erfc(z) = t (a1 + t (a2 + t (a3 + t (a4 + t a5)))) exp(-z^2),
+// t = 1/(1 + p z), |error| <= 1.5e-7. Here z = |v| / sqrt 2 is folded into
+// the constants (p / sqrt 2; exp(-z^2) = 2^(-log2(e) / 2 * v^2)) and the a_i
+// are halved, so q = Phi(-|v|) directly. One reciprocal and one exp2 on the
+// MUFU pipe, the rest on FMA; the negative side uses q itself (no 1 - erf
+// cancellation), the positive side 1 - q.
 __device__ __forceinline__ float gelu_as(float v) {
-  const float z = fabsf(v) * 0.70710678118654752f;
-  const float t = rcp_approx(fmaf(0.3275911f, z, 1.0f));
-  float q = fmaf(1.061405429f, t, -1.453152027f);
-  q = fmaf(q, t, 1.421413741f);
-  q = fmaf(q, t, -0.284496736f);
-  q = fmaf(q, t, 0.254829592f);
-  q *= t * ex2_approx(-1.4426950408889634f * z * z);  // erfc(z)
-  return 0.5f * v * (v >= 0.f ? 2.0f - q : q);
+  const float t = rcp_approx(fmaf(0.3275911f * 0.70710678118654752f, fabsf(v), 1.0f));
+  float q = fmaf(0.5f * 1.061405429f, t, 0.5f * -1.453152027f);
+  q = fmaf(q, t, 0.5f * 1.421413741f);
+  q = fmaf(q, t, 0.5f * -0.284496736f);
+  q = fmaf(q, t, 0.5f * 0.254829592f);
+  q *= t * ex2_approx(v * v * (-0.5f * 1.4426950408889634f));  // Phi(-|v|)
+  return v * (v >= 0.f ? 1.0f - q : q);
 }
 
 }  // namespace sam3

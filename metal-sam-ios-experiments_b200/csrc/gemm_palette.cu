@@ -1091,11 +1091,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(WS_THREADS, 1)
         }
         fence_proxy_async_smem();
         mbar_arrive_cluster(mapa_shared(bar_slab_full + 8 * b, 0));
-        if (c == 0 && pend_it >= 0) {
+        // The previous group's epilogue, once chunks 0 and 1 are expanded:
+        // the MMAs on them cover it and the next chunk's expansion.
+        if (c == 1 && pend_it >= 0) {
           ok = epilogue(pend_it, pend_g);
           pend_it = -1;
         }
       }
+      if (ok && pend_it >= 0) ok = epilogue(pend_it, pend_g);  // a one-chunk group
       pend_it = it;
       pend_g = g;
     }
