@@ -423,6 +423,13 @@ __device__ __forceinline__ float2 unpack_half2(uint32_t v) {
   __half2 h = *reinterpret_cast<__half2*>(&v);
   return __half22float2(h);
 }
+// 0xFF in each byte of u whose bit 7 is set, 0x00 elsewhere (`prmt` with
+// the sign-replicate bit set in every selector nibble).
+__device__ __forceinline__ uint32_t byte_sign_mask(uint32_t u) {
+  uint32_t r;
+  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(u), "r"(0u), "r"(0xBA98u));
+  return r;
+}
 __device__ __forceinline__ float rcp_approx(float x) {
   float y;
   asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));

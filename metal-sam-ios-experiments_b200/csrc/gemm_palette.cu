@@ -485,10 +485,16 @@ static_assert(WS_BN * 128 * 4 <= WS_STAGES * WS_A_STAGE, "palette staging fits t
 // pal[e*64].
 // All N16 16-byte index loads of the range are issued before the first
 // lookup, so the thread waits for one L2 round trip instead of N16.
+// Per 4 indices: one `prmt` per lookup builds its byte offset
+// (index & 127) * 256 + r * 4, and one sign-replicating `prmt` plus one
+// `lop3` build the two half-word selectors (bit 7 of an index picks the
+// high half of its word).
 template <int N16>
 __device__ __forceinline__ void ws_expand_range(const uint8_t* irow, const uint32_t* pal,
                                                 uint8_t* buf, int exp_row, int k0, int kbase) {
   const int sw = exp_row & 7;
+  const uint8_t* palb = reinterpret_cast<const uint8_t*>(pal - exp_row);
+  const uint32_t rowoff = (uint32_t)exp_row * 4u;  // < 256: byte 0 only
   uint4 iv[N16];
 #pragma unroll
   for (int i = 0; i < N16; ++i) iv[i] = __ldg(reinterpret_cast<const uint4*>(irow + k0) + i);
@@ -501,13 +507,16 @@ __device__ __forceinline__ void ws_expand_range(const uint8_t* irow, const uint3
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
       const uint32_t uu = w4[q];
-      const uint32_t p0 = pal[(uu & 0x7Fu) << 6];
-      const uint32_t p1 = pal[((uu >> 8) & 0x7Fu) << 6];
-      const uint32_t p2 = pal[((uu >> 16) & 0x7Fu) << 6];
-      const uint32_t p3 = pal[((uu >> 24) & 0x7Fu) << 6];
-      const uint32_t t = (uu >> 6) & 0x02020202u;
-      o[2 * q] = __byte_perm(p0, p1, 0x5410u | ((t & 0x0202u) * 0x11u));
-      o[2 * q + 1] = __byte_perm(p2, p3, 0x5410u | (((t >> 16) & 0x0202u) * 0x11u));
+      const uint32_t m = uu & 0x7F7F7F7Fu;
+      // offset bytes [r * 4, index j & 127, 0, 0]
+      const uint32_t p0 = *reinterpret_cast<const uint32_t*>(palb + __byte_perm(m, rowoff, 0x5504u));
+      const uint32_t p1 = *reinterpret_cast<const uint32_t*>(palb + __byte_perm(m, rowoff, 0x5514u));
+      const uint32_t p2 = *reinterpret_cast<const uint32_t*>(palb + __byte_perm(m, rowoff, 0x5524u));
+      const uint32_t p3 = *reinterpret_cast<const uint32_t*>(palb + __byte_perm(m, rowoff, 0x5534u));
+      // selector nibbles 0,1 | 4,5 (low halves), + 2 where the index is >= 128
+      const uint32_t sel = (byte_sign_mask(uu) & 0x22222222u) | 0x54105410u;
+      o[2 * q] = __byte_perm(p0, p1, sel);
+      o[2 * q + 1] = __byte_perm(p2, p3, sel >> 16);
     }
     const int kb = (k - kbase) >> 6, c = (k & 63) >> 3;
     uint8_t* dst = buf + kb * WS_SLAB_KB + exp_row * 128;
