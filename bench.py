@@ -136,6 +136,8 @@ class ClockSampler:
 
     def stop(self):
         if self.proc is None:
+            self.file.close()
+            os.unlink(self.file.name)
             return None
         time.sleep(0.25)
         self.proc.terminate()
@@ -411,7 +413,8 @@ def run_ours(args):
                     "d2h_bytes_per_step": args.images * keep * (DIM * 2 + 4),
                     "matches_device_path": same},
             "roofline": {
-                "kernel": "gemm_palette_kernel (palette-dequant tcgen05 GEMM: QKV/proj/fc1/fc2)",
+                "kernel": "gemm_ws_kernel + gemm_wsc_kernel (palette-dequant tcgen05 pair GEMMs: "
+                          "QKV/proj/fc1/fc2, averaged over their launches)",
                 "bound": "tensor", "achieved": gemm_tflops,
                 "peak": peaks["bf16_tflops_sustained"], "unit": "TFLOP/s",
                 "frac": gemm_tflops / peaks["bf16_tflops_sustained"],
