@@ -384,13 +384,9 @@ sam3_status_t attention_tc(sam3_ctx_t* ctx, const uint16_t* qkv, int batch, int 
                      dims3, strides3, box3, es3, CU_TENSOR_MAP_INTERLEAVE_NONE,
                      CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
-  static bool attr_set = false;
-  if (!attr_set) {
-    cudaError_t e = cudaFuncSetAttribute(attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         SMEM_BYTES);
-    if (e != cudaSuccess) return check_cuda(ctx, e, "attention smem attribute");
-    attr_set = true;
-  }
+  const sam3_status_t st =
+      ensure_smem_attr(ctx, kSmemAttn, attn_tc_kernel, SMEM_BYTES, "attention smem attribute");
+  if (st != SAM3_OK) return st;
   AttnArgs a;
   a.out = reinterpret_cast<__half*>(o);
   a.err = ctx->dev_err;

@@ -1193,13 +1193,9 @@ bool make_map_a3d(CUtensorMap* map, const void* x, int k, int m) {
 }
 
 sam3_status_t launch_ws(sam3_ctx_t* ctx, const CUtensorMap& ma, const WsArgs& wa) {
-  static bool attr_set = false;
-  if (!attr_set) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_ws_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         WS_SMEM_BYTES);
-    if (e != cudaSuccess) return check_cuda(ctx, e, "gemm_ws smem attribute");
-    attr_set = true;
-  }
+  sam3_status_t st = ensure_smem_attr(ctx, kSmemWs, gemm_ws_kernel, WS_SMEM_BYTES,
+                                      "gemm_ws smem attribute");
+  if (st != SAM3_OK) return st;
   const int max_pairs = ctx->num_sms / 2;
   const int pairs = wa.sets > 0 ? wa.sets * wa.n_tiles
                                 : (wa.units < max_pairs ? wa.units : max_pairs);
@@ -1209,13 +1205,9 @@ sam3_status_t launch_ws(sam3_ctx_t* ctx, const CUtensorMap& ma, const WsArgs& wa
 }
 
 sam3_status_t launch_wsc(sam3_ctx_t* ctx, const CUtensorMap& ma, const WscArgs& wa) {
-  static bool attr_set = false;
-  if (!attr_set) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_wsc_kernel,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, WSC_SMEM_BYTES);
-    if (e != cudaSuccess) return check_cuda(ctx, e, "gemm_wsc smem attribute");
-    attr_set = true;
-  }
+  sam3_status_t st = ensure_smem_attr(ctx, kSmemWsc, gemm_wsc_kernel, WSC_SMEM_BYTES,
+                                      "gemm_wsc smem attribute");
+  if (st != SAM3_OK) return st;
   const int pairs = wa.sets * wa.n_tiles;
   return check_launch_ret(ctx, launch_pdl(gemm_wsc_kernel, dim3(2 * pairs), dim3(WS_THREADS),
                                          WSC_SMEM_BYTES, ctx->stream, ma, wa),
@@ -1225,13 +1217,9 @@ sam3_status_t launch_wsc(sam3_ctx_t* ctx, const CUtensorMap& ma, const WscArgs& 
 template <int MODE>
 sam3_status_t launch(sam3_ctx_t* ctx, const CUtensorMap& ma, const CUtensorMap& mb,
                      const GemmArgs& args) {
-  static bool attr_set = false;
-  if (!attr_set) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_palette_kernel<MODE>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
-    if (e != cudaSuccess) return check_cuda(ctx, e, "gemm smem attribute");
-    attr_set = true;
-  }
+  sam3_status_t st = ensure_smem_attr(ctx, kSmemGemm << MODE, gemm_palette_kernel<MODE>,
+                                      SMEM_BYTES, "gemm smem attribute");
+  if (st != SAM3_OK) return st;
   const int grid = args.total_tiles < ctx->num_sms ? args.total_tiles : ctx->num_sms;
   gemm_palette_kernel<MODE><<<grid, NUM_THREADS, SMEM_BYTES, ctx->stream>>>(ma, mb, args);
   return check_launch(ctx, "gemm_palette_kernel");

@@ -70,6 +70,10 @@ struct sam3_ctx {
   std::vector<ProfRecord> prof_pending;
   std::vector<cudaEvent_t> event_pool;
   sam3_profile_t prof{};
+
+  // Kernels whose dynamic shared-memory limit has been raised on this
+  // context's device (sam3::kSmem* bits; the attribute is per device).
+  uint32_t smem_attr_done = 0;
 };
 
 namespace sam3 {
@@ -79,6 +83,20 @@ sam3_status_t check_launch(sam3_ctx_t* ctx, const char* what);
 // For launches that return their error (cudaLaunchKernelEx).
 sam3_status_t check_launch_ret(sam3_ctx_t* ctx, cudaError_t e, const char* what);
 sam3_status_t check_cuda(sam3_ctx_t* ctx, cudaError_t e, const char* what);
+
+// Raise `kernel`'s dynamic shared-memory limit to `bytes` once per context:
+// the attribute belongs to the device, and each context is bound to one.
+enum : uint32_t { kSmemAttn = 1u, kSmemWs = 2u, kSmemWsc = 4u, kSmemGemm = 8u /* << MODE */ };
+template <typename Kernel>
+sam3_status_t ensure_smem_attr(sam3_ctx_t* ctx, uint32_t bit, Kernel kernel, int bytes,
+                               const char* what) {
+  if (ctx->smem_attr_done & bit) return SAM3_OK;
+  const cudaError_t e =
+      cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e != cudaSuccess) return check_cuda(ctx, e, what);
+  ctx->smem_attr_done |= bit;
+  return SAM3_OK;
+}
 sam3_status_t ensure_workspace(sam3_ctx_t* ctx);
 bool aligned16(const void* p);
 
