@@ -269,12 +269,16 @@ class Context:
         arr = np.ascontiguousarray(arr)
         if buf is None:
             buf = self.alloc(arr.nbytes)
+        elif isinstance(buf, DeviceBuffer) and arr.nbytes > buf.nbytes:
+            raise ValueError(f"upload of {arr.nbytes} bytes into a {buf.nbytes}-byte buffer")
         self._check(lib.sam3_upload(self.handle, ptr(buf), arr.ctypes.data_as(C.c_void_p),
                                     arr.nbytes))
         return buf
 
     def download(self, src, shape, dtype) -> np.ndarray:
         out = np.empty(shape, dtype)
+        if isinstance(src, DeviceBuffer) and out.nbytes > src.nbytes:
+            raise ValueError(f"download of {out.nbytes} bytes from a {src.nbytes}-byte buffer")
         self._check(lib.sam3_download(self.handle, out.ctypes.data_as(C.c_void_p), ptr(src),
                                       out.nbytes))
         return out
@@ -358,22 +362,54 @@ class Context:
         self._check(lib.sam3_windowed_encoder_forward_rgba(self.handle, ptr(rgba), batch,
                                                            C.byref(w), ptr(out)))
 
+    @staticmethod
+    def _host_ptr(a, nbytes, itemsize, what, write=False):
+        """Address of a host buffer, after checking that an array or tensor is
+        contiguous, has the element size and holds at least `nbytes`: the C ABI
+        takes raw host pointers and cannot check them. A plain integer address
+        is passed through (its caller vouches for its size)."""
+        if isinstance(a, np.ndarray):
+            if not a.flags.c_contiguous:
+                raise ValueError(f"{what}: host array must be C-contiguous")
+            if a.dtype.itemsize != itemsize:
+                raise ValueError(f"{what}: element size {a.dtype.itemsize}, expected {itemsize}")
+            if write and not a.flags.writeable:
+                raise ValueError(f"{what}: host array is read-only")
+            if a.nbytes < nbytes:
+                raise ValueError(f"{what}: {a.nbytes} bytes, needs {nbytes}")
+            return a.ctypes.data_as(C.c_void_p)
+        if hasattr(a, "data_ptr") and hasattr(a, "is_contiguous"):
+            if not a.is_contiguous():
+                raise ValueError(f"{what}: host tensor must be contiguous")
+            if a.element_size() != itemsize:
+                raise ValueError(f"{what}: element size {a.element_size()}, expected {itemsize}")
+            if a.numel() * a.element_size() < nbytes:
+                raise ValueError(f"{what}: {a.numel() * a.element_size()} bytes, needs {nbytes}")
+            return a.data_ptr()
+        return ptr(a)
+
+    def _host_io(self, n, image, feats, idx):
+        side = self.config.image_size
+        t = self.out_tokens
+        return (self._host_ptr(image, n * side * side * 3 * 2, 2, "image"),
+                self._host_ptr(feats, n * t * self.config.embed_dim * 2, 2, "feats", write=True),
+                self._host_ptr(idx, n * t * 4, 4, "idx", write=True))
+
     def encoder_forward_host(self, image_host: np.ndarray, batch, w: EncoderWeights,
                              feats_host: np.ndarray, idx_host: np.ndarray):
-        """Host buffers in and out (numpy arrays or anything with a ctypes data pointer)."""
-        def hp(a):
-            return a.ctypes.data_as(C.c_void_p) if isinstance(a, np.ndarray) else ptr(a)
-        self._check(lib.sam3_encoder_forward_host(self.handle, hp(image_host), batch, C.byref(w),
-                                                  hp(feats_host), hp(idx_host)))
+        """Host buffers in and out: fp16 images [batch, H, W, 3], fp16 features
+        [batch, out_tokens, D] and int32 indices [batch, out_tokens] (numpy
+        arrays, contiguous tensors, or raw addresses)."""
+        img, feats, idx = self._host_io(batch, image_host, feats_host, idx_host)
+        self._check(lib.sam3_encoder_forward_host(self.handle, img, batch, C.byref(w), feats, idx))
 
     def encoder_forward_host_pipelined(self, image_host, n_images, w: EncoderWeights, feats_host,
                                        idx_host):
-        """n_images from host buffers in chunks of max_batch, copies overlapped."""
-        def hp(a):
-            return a.ctypes.data_as(C.c_void_p) if isinstance(a, np.ndarray) else ptr(a)
-        self._check(lib.sam3_encoder_forward_host_pipelined(self.handle, hp(image_host), n_images,
-                                                            C.byref(w), hp(feats_host),
-                                                            hp(idx_host)))
+        """n_images from host buffers in chunks of max_batch, copies overlapped
+        (buffers as for encoder_forward_host, n_images long)."""
+        img, feats, idx = self._host_io(n_images, image_host, feats_host, idx_host)
+        self._check(lib.sam3_encoder_forward_host_pipelined(self.handle, img, n_images,
+                                                            C.byref(w), feats, idx))
 
     @property
     def out_tokens(self) -> int:
