@@ -47,7 +47,9 @@ def _worker(rank, world, port, out):
 
 def test_two_rank_gloo_sharding_and_max_reduction():
     port = _free_port()
-    with mp.Manager() as m:
+    # the manager's server process is spawned, not forked: this process may
+    # already run threads (torch), and a fork of a threaded process can hang
+    with mp.get_context("spawn").Manager() as m:
         out = m.dict()
         mp.spawn(_worker, args=(2, port, out), nprocs=2, join=True)
         res = dict(out)
