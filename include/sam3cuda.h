@@ -137,7 +137,8 @@ typedef struct {
 } sam3_windowed_encoder_weights_t;
 
 /* ---- context ------------------------------------------------------------ */
-/* Fill *cfg with the benchmark defaults listed above. */
+/* Fill *cfg with the benchmark defaults listed above. Reference: the
+ * encoder topology of SAM3EncoderConfig (SAM3EncoderConfig.swift:6-12). */
 sam3_status_t sam3_config_default(sam3_encoder_config_t* cfg);
 
 /* Create a context on `device`; cfg may be NULL (defaults). Replaces the
@@ -148,17 +149,29 @@ sam3_status_t sam3_config_default(sam3_encoder_config_t* cfg);
 sam3_status_t sam3_ctx_create(int device, const sam3_encoder_config_t* cfg,
                               sam3_ctx_t** out);
 sam3_status_t sam3_ctx_destroy(sam3_ctx_t* ctx);
-/* Use a caller-provided cudaStream_t (NULL = the context's own stream). */
+/* Use a caller-provided cudaStream_t (NULL = the context's own stream), or
+ * read the stream calls are queued on. Reference: the caller's
+ * `commandBuffer:` every forward encodes onto (ViTEncoder.swift:374). */
 sam3_status_t sam3_ctx_set_stream(sam3_ctx_t* ctx, void* cuda_stream);
 void* sam3_ctx_stream(sam3_ctx_t* ctx);
-/* Last error message of this context ("" when none). Never NULL. */
+/* Last error message of this context ("" when none). Never NULL.
+ * Reference: the message of `SAM3Error` (SAM3MetalPipeline.swift:176). */
 const char* sam3_last_error(const sam3_ctx_t* ctx);
-/* Wait for the context's stream; reports device errors and kernel timeouts. */
+/* Wait for the context's stream; reports device errors and kernel timeouts.
+ * Reference: commandBuffer.waitUntilCompleted() (SAM3MetalPipeline.swift:79). */
 sam3_status_t sam3_sync(sam3_ctx_t* ctx);
-/* Count of this library's kernel launches since context creation. */
+/* Count of this library's kernel launches since context creation.
+ * Reference: the allocator's usage metrics (OptimizationInfrastructure.swift:
+ * 230), here counting launches. */
 uint64_t sam3_launch_count(const sam3_ctx_t* ctx);
 
-/* ---- memory --------------------------------------------------------------- */
+/* ---- memory ---------------------------------------------------------------
+ * Device buffers: BufferAllocator.privateBuffer / recycle
+ * (OptimizationInfrastructure.swift:280, 307). Host-visible buffers: Apple's
+ * shared-storage MTLBuffers (SAM3Predictor.swift:416) become pinned host
+ * memory plus explicit copies on the context's stream that wait for
+ * completion (upload / download; cf. makePrivateCopy,
+ * OptimizationInfrastructure.swift:323). */
 sam3_status_t sam3_alloc(sam3_ctx_t* ctx, size_t bytes, void** dptr);
 sam3_status_t sam3_free(sam3_ctx_t* ctx, void* dptr);
 sam3_status_t sam3_host_alloc(sam3_ctx_t* ctx, size_t bytes, void** hptr);
@@ -443,7 +456,9 @@ sam3_status_t sam3_profile_enable(sam3_ctx_t* ctx, int32_t enable);
 /* Wait for the stream and return the counters accumulated since enabling. */
 sam3_status_t sam3_profile_read(sam3_ctx_t* ctx, sam3_profile_t* out);
 
-/* Rows kept per image by the encoder under the context's config. */
+/* Rows kept per image by the encoder under the context's config: keep_tokens
+ * when the config prunes, else the full grid. Reference: the kept count of
+ * TokenPruner.prune (TokenPruner.swift:32-126). */
 int32_t sam3_encoder_out_tokens(const sam3_ctx_t* ctx);
 
 #ifdef __cplusplus
