@@ -149,6 +149,11 @@ int so_num_threads(void) {
 #endif
 }
 
+// Seeded synthetic inputs (counter-based: element i depends only on seed,
+// stream and i, so any thread count gives the same tensor). The reference has
+// no generator for this path; these give the benchmark's distributions:
+// activations N(0,1), images U(-1,1), indices U{0..255}, per-row palettes
+// N(0, std) sorted ascending, biases and patch weights N(0, small).
 void so_gen_normal_f16(uint64_t seed, uint64_t stream, int64_t n, float mean,
                        float std, uint16_t* out) {
   Rng r(seed, stream);
@@ -236,6 +241,9 @@ void so_linear(const uint16_t* x, int64_t m, const uint8_t* idx,
   }
 }
 
+// Dense fp16 linear y = x w^T + bias, fp32 accumulation, one fp16 rounding:
+// the patch embedding's 14x14 stride-14 convolution as a GEMM over im2col
+// rows (PatchEmbedding.forward, ViTEncoder.swift:218-263).
 void so_linear_dense(const uint16_t* x, int64_t m, const uint16_t* w,
                      const uint16_t* bias, int64_t n, int64_t k, uint16_t* y) {
   std::vector<float> xf = to_float(x, m * k);
