@@ -54,3 +54,38 @@ def test_two_rank_gloo_sharding_and_max_reduction():
         mp.spawn(_worker, args=(2, port, out), nprocs=2, join=True)
         res = dict(out)
     assert res[0] == res[1] == (1, 1, 20.0)
+
+
+def _dying_rank_worker(rank, port, q):
+    import datetime
+    import time
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=2,
+                            timeout=datetime.timedelta(seconds=10))
+    if rank == 1:
+        os._exit(3)  # leaves between steps: nothing of it is in flight
+    t0 = time.monotonic()
+    try:
+        dist.barrier()
+        q.put(("completed", time.monotonic() - t0))
+    except Exception as e:  # the surviving rank learns of it at its next collective
+        q.put((type(e).__name__, time.monotonic() - t0))
+    os._exit(0)
+
+
+def test_rank_that_dies_ends_the_others_next_collective_with_an_error():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_dying_rank_worker, args=(r, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=90)
+    alive = [p for p in procs if p.is_alive()]
+    for p in alive:
+        p.kill()
+    assert not alive, "a rank hung instead of failing"
+    outcome, seconds = q.get(timeout=5)
+    assert outcome != "completed" and seconds < 60
+    assert procs[1].exitcode == 3 and procs[0].exitcode == 0
