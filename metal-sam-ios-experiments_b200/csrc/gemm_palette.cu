@@ -807,14 +807,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(WS_THREADS, 1)
 }
 
 // ============================================================================
-// Chunked weight-stationary pair kernel (K > 1024, K % 512 == 0; fc2 with
-// K = 4096): the pair's 128-row slab is expanded one 512-wide K chunk at a
-// time into two alternating 64 KB shared-memory buffers, so the expansion of
-// chunk c+1 overlaps the MMAs on chunk c. Each expanded chunk feeds a group of
-// two 256-row M tiles accumulating in their own TMEM buffers (4 x 128
-// columns: groups alternate between accumulator pairs, so the epilogue of one
-// group overlaps the MMAs of the next). Each pair keeps one N tile (palette
-// staged once, 32 KB) and the pairs of a "set" sweep the M groups in lockstep.
+// Chunked weight-stationary pair kernel (K > 1024, K % 128 == 0; fc2 with
+// K = 4096, or 4736 for the checkpoint): the pair's 128-row slab is expanded
+// one 512-wide K chunk at a time (the last one shorter when K % 512 != 0)
+// into two alternating 64 KB shared-memory buffers, so the expansion of chunk
+// c+1 overlaps the MMAs on chunk c. Each expanded chunk feeds a group of two
+// 256-row M tiles accumulating in their own TMEM buffers (4 x 128 columns:
+// groups alternate between accumulator pairs, so the epilogue of one group,
+// run by the expander warps after chunk 1 of the next, overlaps its MMAs).
+// Each pair keeps one N tile (palette staged once, 32 KB) and the pairs of a
+// "set" sweep the M groups in lockstep.
 // ============================================================================
 constexpr int WSC_KC = 512;
 constexpr int WSC_KB_PER_CHUNK = WSC_KC / WS_BK;                    // 8
