@@ -70,6 +70,8 @@ def _dying_rank_worker(rank, port, q):
         q.put(("completed", time.monotonic() - t0))
     except Exception as e:  # the surviving rank learns of it at its next collective
         q.put((type(e).__name__, time.monotonic() - t0))
+    q.close()
+    q.join_thread()  # the message reaches the pipe before the hard exit
     os._exit(0)
 
 
