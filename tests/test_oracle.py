@@ -316,3 +316,25 @@ def test_windowed_encoder_matches_window_partition_composition(oracle):
 
 def _lin(d):
     return {"idx": d["idx"], "palette": d["palette"], "bias": d["bias"]}
+
+
+@pytest.mark.parametrize("keep", [1, 5, 16])
+@pytest.mark.parametrize("order", [0, 1])
+def test_prune_keep_extremes_known_answer(oracle, keep, order):
+    # rows of constant value v (distinct |v| per row, exact in fp16): the L2
+    # score ranks rows by |v|; keep 1 is the arg-max, keep = seq keeps every
+    # row (index order: 0..seq-1; score order: by descending score)
+    seq, d = 16, 8
+    rng = np.random.default_rng(keep * 10 + order)
+    x = np.empty((2 * seq, d), F16)
+    for b in range(2):
+        v = rng.permutation(np.arange(1, seq + 1)) * rng.choice([-1, 1], seq)
+        x[b * seq:(b + 1) * seq] = v[:, None].astype(F16)
+    feats, _, idx = oracle.prune(x, 2, seq, keep, norm=0, order=order)
+    for b in range(2):
+        mag = np.abs(x[b * seq:(b + 1) * seq, 0].astype(np.float64))
+        top = np.argsort(-mag, kind="stable")[:keep]
+        want = top if order == 1 else np.sort(top)
+        assert np.array_equal(idx[b], want)
+        assert np.array_equal(feats[b * keep:(b + 1) * keep].view(np.uint16),
+                              x[b * seq + want].view(np.uint16))
