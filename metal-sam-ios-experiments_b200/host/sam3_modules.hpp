@@ -49,11 +49,14 @@ inline void* allocate(sam3_ctx_t* ctx, size_t bytes, BufferList& recycled, const
 
 // Frees every buffer a forward() handed out, after the stream has drained
 // (the reference recycles in the command buffer's completion handler,
-// ViTEncoder.swift:1459-1464).
+// ViTEncoder.swift:1459-1464). The buffers are freed even when the sync
+// reports an error (a kernel timeout leaves the context usable); the error
+// is thrown afterwards.
 inline void recycle(sam3_ctx_t* ctx, BufferList& recycled) {
-  check(ctx, sam3_sync(ctx), "recycle sync");
+  const sam3_status_t st = sam3_sync(ctx);
   for (void* p : recycled) sam3_free(ctx, p);
   recycled.clear();
+  check(ctx, st, "recycle sync");
 }
 
 // RoPE.swift:9-121: the 2D axial table for a square grid, built once.
