@@ -4,6 +4,7 @@
     python microbench.py gemm --m 41472 --n 4096 --k 1024 --epi gelu
     python microbench.py attention --batch 8 --seq 5184
     python microbench.py layernorm --m 41472
+    python microbench.py prune --batch 16        (L2 score + top-2592 + gather of rows and RoPE rows)
     python microbench.py patch --batch 8 [--rgba]
     python microbench.py preprocess --batch 8
     python microbench.py neck --batch 8          (restoreSpatial + neck, 72x72, 1024 -> 256)
@@ -42,7 +43,7 @@ def main():
     import sam3cuda as sam3
 
     ap = argparse.ArgumentParser()
-    ap.add_argument("op", choices=("gemm", "attention", "layernorm", "dequant", "patch",
+    ap.add_argument("op", choices=("gemm", "attention", "layernorm", "prune", "dequant", "patch",
                                    "preprocess", "neck", "windowed", "encoder"))
     ap.add_argument("--rgba", action="store_true",
                     help="patch: f32 RGBA frames, normalisation fused into the patch gather")
@@ -253,6 +254,25 @@ def main():
                           "gbs_gather_and_pad": prof["bytes"] / (prof["ms"] * 1e-3) / 1e9}))
         ctx.close()
         return
+    elif a.op == "prune":
+        # the encoder's prune after block 16: seq tokens per image -> seq / 2,
+        # L2 score, kept in token order, with their RoPE rows
+        ctx.close()
+        ctx = sam3.Context(0, max_batch=a.batch)
+        keep = a.seq // 2
+        x = torch.randn((a.batch * a.seq, 1024), generator=g, device=dev).half()
+        rope = torch.randn((a.seq, 64), generator=g, device=dev)
+        feats = torch.empty((a.batch * keep, 1024), dtype=torch.float16, device=dev)
+        rope_out = torch.empty((a.batch * keep, 64), dtype=torch.float32, device=dev)
+        idx = torch.empty((a.batch, keep), dtype=torch.int32, device=dev)
+        prof = run(lambda: ctx.prune(x, a.batch, a.seq, 1024, keep, sam3.SCORE_L2,
+                                     sam3.ORDER_INDEX, feats, idx, rope, a.seq, 64,
+                                     rope_out))["prune"]
+        calls = prof["launches"] / 3  # score, select, gather per call
+        us = prof["ms"] / calls * 1e3
+        gbs = prof["bytes"] / (prof["ms"] * 1e-3) / 1e9
+        print(json.dumps({"op": "prune", "batch": a.batch, "seq": a.seq, "keep": keep,
+                          "us_per_call": us, "gbs": gbs, "frac_hbm": gbs / bw_peak}))
     else:
         x = torch.randn((a.m, 1024), generator=g, device=dev).half()
         y = torch.empty_like(x)
