@@ -41,11 +41,19 @@ int main() {
   } catch (const sam3::SAM3Error& e) {
     caught += e.status == SAM3_ERR_INVALID_ARG;
   }
+  // recycle() empties its list even when the sync before the frees fails
+  // (the null context rejects both calls before touching the pointer)
+  sam3::BufferList handed_out{reinterpret_cast<void*>(0x1000)};
+  try {
+    sam3::recycle(nullptr, handed_out);
+  } catch (const sam3::SAM3Error& e) {
+    caught += e.status == SAM3_ERR_INVALID_ARG && handed_out.empty();
+  }
   // fault injection and the wait self-test need a context too
   const bool no_ctx = sam3_set_fault(nullptr, SAM3_FAULT_ALLOC) == SAM3_ERR_INVALID_ARG &&
                       sam3_selftest_wait_timeout(nullptr) == SAM3_ERR_INVALID_ARG &&
                       sam3_get_fault(nullptr) == 0;
-  std::printf("caught %d of 5, embed_dim %d, no-context checks %s\n", caught, cfg.embed_dim,
+  std::printf("caught %d of 6, embed_dim %d, no-context checks %s\n", caught, cfg.embed_dim,
               no_ctx ? "ok" : "failed");
-  return caught == 5 && recycled.empty() && no_ctx ? 0 : 1;
+  return caught == 6 && recycled.empty() && no_ctx ? 0 : 1;
 }
