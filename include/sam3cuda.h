@@ -245,10 +245,16 @@ sam3_status_t sam3_attention(sam3_ctx_t* ctx, const uint16_t* qkv, int32_t batch
  * library until the process exits). batch * seq beyond that limit returns
  * SAM3_ERR_SHAPE; other argument errors return SAM3_ERR_INVALID_ARG /
  * SAM3_ERR_SHAPE as sam3_prune does, and a failed launch SAM3_ERR_CUDA.
- * The first call on each device looks up the array's device address, so make
- * it before any stream capture. All calls share the one array: calls that
- * overlap on the GPU (different streams, or graph replays running at the same
- * time) race on it and must be serialised by the caller. */
+ * The work runs on the stream's device, which is made current for the call
+ * (the calling thread's current device is restored before returning). An
+ * error already pending on the calling thread is left in place, not cleared.
+ * The first call on each device looks up the array's device address (and
+ * raises the selection kernel's shared-memory limit there), so make it
+ * before any stream capture. That address is kept for the life of the
+ * process: after cudaDeviceReset of a device, do not call this entry point
+ * on that device again. All calls share the one array: calls that overlap on
+ * the GPU (different streams, or graph replays running at the same time)
+ * race on it and must be serialised by the caller. */
 sam3_status_t sam3_prune_noalloc(void* cuda_stream, const uint16_t* x, int32_t batch,
                                  int32_t seq, int32_t d, int32_t keep, int32_t norm,
                                  int32_t order, const float* rope_in, int32_t rope_rows,

@@ -86,7 +86,9 @@ sam3_status_t check_cuda(sam3_ctx_t* ctx, cudaError_t e, const char* what);
 
 // Raise `kernel`'s dynamic shared-memory limit to `bytes` once per context:
 // the attribute belongs to the device, and each context is bound to one.
-enum : uint32_t { kSmemAttn = 1u, kSmemWs = 2u, kSmemWsc = 4u, kSmemGemm = 8u /* << MODE */ };
+enum : uint32_t {
+  kSmemAttn = 1u, kSmemWs = 2u, kSmemWsc = 4u, kSmemGemm = 8u /* << MODE */, kSmemPrune = 64u
+};
 template <typename Kernel>
 sam3_status_t ensure_smem_attr(sam3_ctx_t* ctx, uint32_t bit, Kernel kernel, int bytes,
                                const char* what) {
@@ -156,6 +158,19 @@ cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t s
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
+// A plain launch (no attributes) that returns its own error instead of
+// leaving it only in the thread's last-error state.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_plain(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                         cudaStream_t stream, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
   return cudaLaunchKernelEx(&cfg, kernel, args...);
 }
 

@@ -469,6 +469,10 @@ sam3_status_t rope_pos_from_idx(sam3_ctx_t* ctx, const int32_t* idx, int n, int 
   return check_launch(ctx, "rope_pos_idx_kernel");
 }
 
+// prune_select_kernel's largest dynamic shared memory: seq <= 16384 score
+// keys plus, in score order, a bitonic buffer of up to 8192 (key, index) pairs.
+constexpr int kPruneSelectSmemMax = 16384 * 4 + 8192 * 8;
+
 sam3_status_t prune(sam3_ctx_t* ctx, const uint16_t* x, int batch, int seq, int d, int keep,
                     int norm, int order, const float* rope_in, int rope_rows, int rope_cols,
                     uint16_t* feats, float* rope_out, int32_t* idx, float* scores) {
@@ -502,11 +506,12 @@ sam3_status_t prune(sam3_ctx_t* ctx, const uint16_t* x, int batch, int seq, int 
     while (p2 < keep) p2 <<= 1;
     smem += (size_t)p2 * 8;
   }
-  if (smem > 48 * 1024) {
-    cudaError_t e = cudaFuncSetAttribute(prune_select_kernel,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return check_cuda(ctx, e, "prune smem attribute");
-  }
+  // The limit is raised once per device to the largest size the checks above
+  // allow and never lowered, so threads pruning different sizes at the same
+  // time cannot undo each other's setting.
+  st = ensure_smem_attr(ctx, kSmemPrune, prune_select_kernel, kPruneSelectSmemMax,
+                        "prune smem attribute");
+  if (st != SAM3_OK) return st;
   {
     ProfScope prof(ctx, SAM3_PROF_PRUNE, 0.0, 4.0 * rows + 4.0 * batch * keep);
     prune_select_kernel<<<batch, 1024, smem, ctx->stream>>>(scores, seq, keep, order, idx);
@@ -681,7 +686,28 @@ namespace {
 static __device__ __align__(256) float g_noalloc_scores[SAM3_PRUNE_NOALLOC_MAX_ROWS];
 constexpr int kMaxDevices = 64;
 std::mutex g_noalloc_mu;
-float* g_noalloc_addr[kMaxDevices] = {};  // device address of the array, per device
+// Per device: the array's device address and whether prune_select_kernel's
+// shared-memory limit has been raised there. Looked up once per device; a
+// cudaDeviceReset of that device invalidates them (see the header).
+float* g_noalloc_addr[kMaxDevices] = {};
+bool g_noalloc_smem[kMaxDevices] = {};
+
+// Switches to `dev` for the lifetime of the scope when it is not current.
+struct DeviceScope {
+  int prev = -1;
+  bool ok = true;
+  explicit DeviceScope(int dev) {
+    int cur = -1;
+    if (cudaGetDevice(&cur) != cudaSuccess) { ok = false; return; }
+    if (cur != dev) {
+      if (cudaSetDevice(dev) != cudaSuccess) { ok = false; return; }
+      prev = cur;
+    }
+  }
+  ~DeviceScope() {
+    if (prev >= 0) cudaSetDevice(prev);
+  }
+};
 }  // namespace
 
 extern "C" sam3_status_t sam3_prune_noalloc(void* cuda_stream, const uint16_t* x, int32_t batch,
@@ -701,52 +727,70 @@ extern "C" sam3_status_t sam3_prune_noalloc(void* cuda_stream, const uint16_t* x
     return SAM3_ERR_INVALID_ARG;
   if (!aligned16(x) || !aligned16(feats)) return SAM3_ERR_INVALID_ARG;
 
+  // An error already pending on this thread belongs to earlier work: it is
+  // left in place, and only errors of this call's own runtime calls are
+  // cleared (each of those returns its error directly).
+  const bool clean_before = cudaPeekAtLastError() == cudaSuccess;
+  auto fail = [clean_before]() {
+    if (clean_before) cudaGetLastError();
+    return SAM3_ERR_CUDA;
+  };
+
+  // The work runs on the stream's device (the current device for the legacy
+  // default stream), which is made current for the call.
+  cudaStream_t stream = static_cast<cudaStream_t>(cuda_stream);
+  int dev = -1;
+  if (stream == nullptr ? cudaGetDevice(&dev) != cudaSuccess
+                        : cudaStreamGetDevice(stream, &dev) != cudaSuccess)
+    return fail();
+  if (dev < 0 || dev >= kMaxDevices) return SAM3_ERR_UNSUPPORTED;
+  DeviceScope on_dev(dev);
+  if (!on_dev.ok) return fail();
+
   // Set-up, once per device with that device current: the host-side name of
   // a __device__ array is only a stand-in, so ask the runtime for its device
-  // address and hand that to the kernels.
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
-    cudaGetLastError();
-    return SAM3_ERR_CUDA;
-  }
+  // address and hand that to the kernels. prune_select_kernel's dynamic
+  // shared-memory limit is raised there once, to the largest size accepted
+  // above, and never lowered.
   float* scores = nullptr;
   {
     std::lock_guard<std::mutex> lock(g_noalloc_mu);
     if (!g_noalloc_addr[dev]) {
       void* p = nullptr;
-      if (cudaGetSymbolAddress(&p, g_noalloc_scores) != cudaSuccess || !p) {
-        cudaGetLastError();
-        return SAM3_ERR_CUDA;
-      }
+      if (cudaGetSymbolAddress(&p, g_noalloc_scores) != cudaSuccess || !p) return fail();
       g_noalloc_addr[dev] = static_cast<float*>(p);
+    }
+    if (!g_noalloc_smem[dev]) {
+      if (cudaFuncSetAttribute(prune_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               kPruneSelectSmemMax) != cudaSuccess)
+        return fail();
+      g_noalloc_smem[dev] = true;
     }
     scores = g_noalloc_addr[dev];
   }
 
-  cudaStream_t stream = static_cast<cudaStream_t>(cuda_stream);
   const long long rows = (long long)batch * seq;
   // Every score is rewritten before it is read, so nothing needs clearing.
-  token_score_kernel<<<blocks_for(rows, 8), 256, 0, stream>>>(
-      reinterpret_cast<const __half*>(x), (int)rows, d, norm, scores);
-  if (cudaGetLastError() != cudaSuccess) return SAM3_ERR_CUDA;
+  if (launch_plain(token_score_kernel, dim3(blocks_for(rows, 8)), dim3(256), 0, stream,
+                   reinterpret_cast<const __half*>(x), (int)rows, (int)d, (int)norm,
+                   scores) != cudaSuccess)
+    return fail();
   size_t smem = ((size_t)seq * 4 + 15) & ~(size_t)15;
   if (order == SAM3_ORDER_SCORE) {
     int p2 = 1;
     while (p2 < keep) p2 <<= 1;
     smem += (size_t)p2 * 8;
   }
-  if (smem > 48 * 1024 &&
-      cudaFuncSetAttribute(prune_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           (int)smem) != cudaSuccess) {
-    cudaGetLastError();
-    return SAM3_ERR_CUDA;
-  }
-  prune_select_kernel<<<batch, 1024, smem, stream>>>(scores, seq, keep, order, idx);
-  if (cudaGetLastError() != cudaSuccess) return SAM3_ERR_CUDA;
+  if (launch_plain(prune_select_kernel, dim3(batch), dim3(1024), smem, stream,
+                   static_cast<const float*>(scores), (int)seq, (int)keep, (int)order,
+                   idx) != cudaSuccess)
+    return fail();
   const int total = batch * keep;
-  prune_gather_kernel<<<blocks_for(total, 8), 256, 0, stream>>>(
-      reinterpret_cast<const __half*>(x), seq, d, keep, idx, rope_in, rope_rows > 0 ? rope_rows : 1,
-      rope_cols, reinterpret_cast<__half*>(feats), rope_out, total);
-  if (cudaGetLastError() != cudaSuccess) return SAM3_ERR_CUDA;
+  if (launch_plain(prune_gather_kernel, dim3(blocks_for(total, 8)), dim3(256), 0, stream,
+                   reinterpret_cast<const __half*>(x), (int)seq, (int)d, (int)keep,
+                   static_cast<const int32_t*>(idx), rope_in, rope_rows > 0 ? (int)rope_rows : 1,
+                   (int)rope_cols, reinterpret_cast<__half*>(feats), rope_out,
+                   total) != cudaSuccess)
+    return fail();
   return SAM3_OK;
 }

@@ -23,15 +23,15 @@ import json
 import os
 import sys
 
-HERE = os.path.dirname(os.path.abspath(__file__))
-sys.path.insert(0, HERE)
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "metal-sam-ios-experiments_b200"))
 
 EPIS = {"bias": 0, "gelu": 1, "residual": 2, "rope": 3}
 
 
 def peaks():
     try:
-        with open(os.path.join(os.path.dirname(HERE), "MEASURED_PEAKS.json")) as f:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
             p = json.load(f)
         return float(p["bf16_tflops"]), float(p["hbm_gbs"])
     except Exception:
@@ -144,7 +144,7 @@ def main():
         ctx.close()
         return
     elif a.op == "encoder":
-        sys.path.insert(0, os.path.dirname(HERE))
+        sys.path.insert(0, ROOT)
         import bench  # the benchmark's synthetic weights
         ctx.close()
         prune_after = a.blocks // 2 if a.blocks > 1 else 0

@@ -21,6 +21,9 @@ _LIB_PATH = os.path.join(_HERE, "libsam3oracle.so")
 
 EPI_BIAS, EPI_BIAS_GELU, EPI_BIAS_RESIDUAL, EPI_BIAS_ROPE_QKV = 0, 1, 2, 3
 SCORE_L2, SCORE_L1 = 0, 1
+# Rounding points: the CUDA path's fused operators (default), or the
+# reference's MPSGraph op boundaries (every graph op returns fp16).
+ROUND_FUSED, ROUND_GRAPH = 0, 1
 ORDER_INDEX, ORDER_SCORE = 0, 1
 
 _lib = None
@@ -86,6 +89,9 @@ def _declare(L):
         fn = getattr(L, name)
         fn.argtypes = args
         fn.restype = None
+    L.so_set_rounding.argtypes = [C.c_int]
+    L.so_set_rounding.restype = None
+    L.so_rounding.restype = C.c_int
     L.so_num_threads.restype = C.c_int
     L.so_set_num_threads.argtypes = [C.c_int]
     L.so_set_num_threads.restype = None
@@ -112,6 +118,23 @@ def set_num_threads(n: int) -> None:
     """OpenMP threads for the oracle's loops (process launchers such as
     torch.distributed.run set OMP_NUM_THREADS=1 per rank)."""
     lib().so_set_num_threads(int(n))
+
+
+class rounding:
+    """Context manager: run the oracle with the given rounding points
+    (ROUND_FUSED or ROUND_GRAPH) and restore the previous mode on exit."""
+
+    def __init__(self, mode):
+        self.mode = mode
+
+    def __enter__(self):
+        self.prev = lib().so_rounding()
+        lib().so_set_rounding(int(self.mode))
+        return self
+
+    def __exit__(self, *exc):
+        lib().so_set_rounding(self.prev)
+        return False
 
 
 # ---- generators ---------------------------------------------------------------

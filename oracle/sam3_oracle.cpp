@@ -122,6 +122,12 @@ void gemm_nt(const float* A, int64_t m, const float* B, int64_t n, int64_t k,
   }
 }
 
+// Rounding points (SO_ROUND_FUSED / SO_ROUND_GRAPH, see sam3_oracle.h).
+int g_rounding = SO_ROUND_FUSED;
+
+// One MPSGraph op's fp16 result.
+inline float hr(float v) { return h2f(f2h(v)); }
+
 inline float gelu_erf(float v) {
   // Exact GELU: 0.5 x (1 + erf(x / sqrt 2)).
   // Reference: ViTEncoder.swift:985-992 (MLP) and :582-589 (fused block).
@@ -131,6 +137,9 @@ inline float gelu_erf(float v) {
 }  // namespace
 
 extern "C" {
+
+void so_set_rounding(int mode) { g_rounding = mode == SO_ROUND_GRAPH ? SO_ROUND_GRAPH : SO_ROUND_FUSED; }
+int so_rounding(void) { return g_rounding; }
 
 float so_half_to_float(uint16_t h) { return h2f(h); }
 uint16_t so_float_to_half(float f) { return f2h(f); }
@@ -218,6 +227,35 @@ void so_linear(const uint16_t* x, int64_t m, const uint8_t* idx,
   gemm_nt(xf.data(), m, wf.data(), n, k, acc.data());
   const int64_t qk_cols = 2LL * heads * head_dim;
   const int pairs = head_dim / 2;
+  if (g_rounding == SO_ROUND_GRAPH) {
+    // The reference's graph: every op returns an fp16 tensor.
+    const float sqrt2_h = hr(1.41421356f);  // graph.constant(1.41421356, fp16)
+#pragma omp parallel for schedule(static)
+    for (int64_t i = 0; i < m; ++i) {
+      float* row = acc.data() + i * n;
+      for (int64_t j = 0; j < n; ++j) row[j] = hr(hr(row[j]) + (bias ? h2f(bias[j]) : 0.f));
+      if (epilogue == SO_EPI_BIAS_GELU) {
+        for (int64_t j = 0; j < n; ++j) {
+          const float v = row[j];
+          const float e = hr((float)std::erf((double)hr(v / sqrt2_h)));
+          row[j] = hr(hr(0.5f * v) * hr(1.0f + e));
+        }
+      } else if (epilogue == SO_EPI_BIAS_RESIDUAL) {
+        for (int64_t j = 0; j < n; ++j) row[j] = hr(h2f(residual[i * n + j]) + row[j]);
+      } else if (epilogue == SO_EPI_BIAS_ROPE_QKV) {
+        const float* t = rope + (i % rope_period) * (int64_t)head_dim;
+        for (int64_t j = 0; j < qk_cols; j += 2) {
+          const int p = (int)((j % head_dim) / 2);
+          const float c = hr(t[2 * p]), s = hr(t[2 * p + 1]);
+          const float a = row[j], b = row[j + 1];
+          row[j] = hr(hr(a * c) - hr(b * s));
+          row[j + 1] = hr(hr(a * s) + hr(b * c));
+        }
+      }
+      for (int64_t j = 0; j < n; ++j) y[i * n + j] = f2h(row[j]);
+    }
+    return;
+  }
 #pragma omp parallel for schedule(static)
   for (int64_t i = 0; i < m; ++i) {
     float* row = acc.data() + i * n;
@@ -262,6 +300,31 @@ void so_linear_dense(const uint16_t* x, int64_t m, const uint16_t* w,
 void so_layernorm(const uint16_t* x, int64_t m, int64_t d,
                   const uint16_t* gamma, const uint16_t* beta, float eps,
                   uint16_t* y) {
+  if (g_rounding == SO_ROUND_GRAPH) {
+    // mean, variance about the fp16 mean, centre, sqrt(var + eps), divide,
+    // scale, shift: each an fp16 tensor (eps is an fp16 graph constant).
+    const float eps_h = hr(eps);
+#pragma omp parallel for schedule(static)
+    for (int64_t i = 0; i < m; ++i) {
+      const uint16_t* xr = x + i * d;
+      double s = 0.0;
+      for (int64_t j = 0; j < d; ++j) s += h2f(xr[j]);
+      const float mean = hr((float)(s / (double)d));
+      double v = 0.0;
+      for (int64_t j = 0; j < d; ++j) {
+        const double t = (double)h2f(xr[j]) - (double)mean;
+        v += t * t;
+      }
+      const float var = hr((float)(v / (double)d));
+      const float denom = hr(std::sqrt(hr(var + eps_h)));
+      for (int64_t j = 0; j < d; ++j) {
+        const float g = gamma ? h2f(gamma[j]) : 1.f, b = beta ? h2f(beta[j]) : 0.f;
+        const float c = hr(h2f(xr[j]) - mean);
+        y[i * d + j] = f2h(hr(hr(c / denom) * g) + b);
+      }
+    }
+    return;
+  }
 #pragma omp parallel for schedule(static)
   for (int64_t i = 0; i < m; ++i) {
     const uint16_t* xr = x + i * d;

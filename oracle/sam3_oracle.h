@@ -39,6 +39,31 @@ enum {
 enum { SO_SCORE_L2 = 0, SO_SCORE_L1 = 1 };
 enum { SO_ORDER_INDEX = 0, SO_ORDER_SCORE = 1 };
 
+/* ---- rounding points ------------------------------------------------------ */
+/* SO_ROUND_FUSED (default): the CUDA path's rounding points listed above, one
+ * fp16 rounding per fused operator.
+ * SO_ROUND_GRAPH: the reference's MPSGraph op boundaries, where every graph
+ * op (matmul, bias add, each multiply / add of RoPE, each step of LN and
+ * GELU, the residual add) returns an fp16 tensor:
+ *   linear:  h(h(x w^T) + b)                 (MPSAttention.swift:113-117,
+ *                                             ViTEncoder.swift:479-483)
+ *   RoPE:    c = h(cos), s = h(sin); (a, b) -> (h(h(a c) - h(b s)),
+ *            h(h(a s) + h(b c)))             (MPSAttention.swift:137-160;
+ *                                             the cast at :151-153)
+ *   residual: h(x + h(h(y w^T) + b))         (ViTEncoder.swift:559, 605)
+ *   GELU:    h(h(0.5 v) * h(1 + h(erf(h(v / h(1.41421356))))))
+ *                                            (ViTEncoder.swift:581-589)
+ *   LN:      mean, variance (about that fp16 mean), x - mean, sqrt(var + eps),
+ *            the division, * gamma, + beta each rounded to fp16
+ *                                            (ViTEncoder.swift:466-474).
+ * Reductions inside one op (matmul, mean, variance) accumulate in fp32 or
+ * wider before their single rounding; SDPA is unchanged (fp32 inside, fp16
+ * out). The mode is process-global: set it before a computation, not while
+ * one runs. */
+enum { SO_ROUND_FUSED = 0, SO_ROUND_GRAPH = 1 };
+void so_set_rounding(int mode);
+int so_rounding(void);
+
 /* ---- seeded synthetic data (counter-based, order independent) ---------- */
 /* Every value i of a tensor is a pure function of (seed, stream, i):
  * u64 = splitmix64(seed ^ mix(stream) + i * 0x9E3779B97F4A7C15). */

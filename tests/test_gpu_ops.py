@@ -13,7 +13,7 @@ import numpy as np
 import pytest
 
 from conftest import PKG
-from util import f16_ulps, max_rel_err
+from util import elem_rel_err, f16_ulps, margin_check, max_rel_err
 
 pytestmark = pytest.mark.gpu
 F16 = np.float16
@@ -407,23 +407,6 @@ def test_prune_l1(ctx, sam3, golden):
     assert np.array_equal(ctx.download(idx, (2, 12), np.int32), golden["pr_idx_l1"])
 
 
-def _margin_check(got_idx, scores, keep):
-    """Indices must agree exactly unless the keep-th / (keep+1)-th score gap is
-    <= 1e-3; inside that band only tokens within 1e-3 of the cut may differ."""
-    order = np.lexsort((np.arange(len(scores)), -scores.astype(np.float64)))
-    ref = np.sort(order[:keep])
-    s_sorted = scores[order]
-    gap = float(s_sorted[keep - 1] - s_sorted[keep])
-    if gap > 1e-3:
-        assert np.array_equal(np.sort(got_idx), ref)
-    else:
-        cut = 0.5 * float(s_sorted[keep - 1] + s_sorted[keep])
-        sure_in = set(np.nonzero(scores > cut + 1e-3)[0])
-        sure_out = set(np.nonzero(scores < cut - 1e-3)[0])
-        g = set(got_idx.tolist())
-        assert sure_in <= g and not (sure_out & g)
-
-
 def test_prune_full_size_index_order_with_rope(ctx_full, sam3, oracle):
     ctx = ctx_full
     seq, keep, d = 5184, 2592, 1024
@@ -436,7 +419,7 @@ def test_prune_full_size_index_order_with_rope(ctx_full, sam3, oracle):
     ctx.sync()
     gi = ctx.download(idx, (keep,), np.int32)
     assert (np.diff(gi) > 0).all()
-    _margin_check(gi, oracle.token_scores(x), keep)
+    margin_check(gi, oracle.token_scores(x), keep)
     gf = ctx.download(feats, (keep, d), F16)
     assert np.array_equal(gf.view(np.uint16), x[gi].view(np.uint16))
     gr = ctx.download(rope_out, (keep, 32, 2), np.float32)
@@ -453,7 +436,7 @@ def test_prune_score_order_matches_oracle(ctx_full, sam3, oracle):
     gi = ctx.download(idx, (keep,), np.int32)
     s = oracle.token_scores(x)
     assert (np.diff(s[gi].astype(np.float64)) <= 1e-3).all()  # non-increasing score
-    _margin_check(gi, s, keep)
+    margin_check(gi, s, keep)
 
 
 # ------------------------------------------------------------------ patch embedding
@@ -770,34 +753,43 @@ def test_encoder_host_pipelined_equals_per_call(ctx, sam3, oracle):
 
 def test_encoder_full_size_two_blocks_matches_oracle(sam3, oracle):
     # 1008^2 image, full width (1024, 16 heads, 4096), two blocks with the
-    # prune (to 2592 tokens by L2 norm) between them. Upstream fp16 rounding
-    # differs between the two sides, so the kept sets may differ only for
-    # tokens whose oracle score lies within a relative 1e-3 of the cut; the
-    # output rows of tokens both sides kept must agree within the fp16 spec.
+    # prune (to 2592 tokens by L2 norm) between them.
+    # Indices: on the GPU's own 1-block state the prune must agree with the
+    # oracle's selection wherever the cut margin exceeds 1e-3 (absolute).
+    # Against the oracle's own run, whose 1-block state differs by fp16
+    # rounding, a token may differ only within 1e-3 + 2*eps of the cut (eps:
+    # the measured max score deviation; each score and the cut move by <= eps).
+    # Rows both sides kept must agree within the fp16 spec.
+    blocks = [oracle.SyntheticBlock(41, i) for i in range(2)]
+    pw = oracle.gen_normal(41, 900, (1024, 3, 14, 14), 0.0, 0.02)
+    pb = oracle.gen_normal(41, 901, (1024,), 0.0, 0.02)
+    img = oracle.gen_uniform(41, 77, (1, 1008, 1008, 3), -1.0, 1.0)
     with sam3.Context(0, num_blocks=2, prune_after_block=1, max_batch=1) as ctx:
-        blocks = [oracle.SyntheticBlock(41, i) for i in range(2)]
-        pw = oracle.gen_normal(41, 900, (1024, 3, 14, 14), 0.0, 0.02)
-        pb = oracle.gen_normal(41, 901, (1024,), 0.0, 0.02)
         w = _upload_encoder(ctx, sam3, blocks, pw, pb)
-        img = oracle.gen_uniform(41, 77, (1, 1008, 1008, 3), -1.0, 1.0)
         hf = np.empty((1, 2592, 1024), F16)
         hi = np.empty((1, 2592), np.int32)
         ctx.encoder_forward_host(img, 1, w, hf, hi)
+    with sam3.Context(0, num_blocks=1, prune_after_block=0, max_batch=1) as ctx:
+        w = _upload_encoder(ctx, sam3, blocks[:1], pw, pb)
+        pre = np.empty((1, 5184, 1024), F16)
+        pi = np.empty((1, 5184), np.int32)
+        ctx.encoder_forward_host(img, 1, w, pre, pi)
     ref_f, ref_i = oracle.encoder_forward(img, blocks, pw, pb, prune_after=1, keep=2592)
     x1 = oracle.vit_block(oracle.patch_embed(img, pw, pb, 14), 1, 5184, 16, blocks[0],
                           oracle.rope_table(72, 72), 5184)
-    scores = oracle.token_scores(x1).astype(np.float64)
-    srt = np.sort(scores)[::-1]
-    cut = 0.5 * (srt[2591] + srt[2592])
     assert (np.diff(hi[0]) > 0).all()
-    g, r = set(hi[0].tolist()), set(ref_i[0].tolist())
-    diff = np.array(sorted(g ^ r), dtype=np.int64)
-    if diff.size:
-        assert np.abs(scores[diff] - cut).max() <= 1e-3 * cut, (diff.size, np.abs(scores[diff] - cut).max())
-    common = np.array(sorted(g & r))
+    gpu_scores = oracle.token_scores(pre[0]).astype(np.float64)
+    margin_check(hi[0], gpu_scores, 2592, margin=1e-3)
+    scores = oracle.token_scores(x1).astype(np.float64)
+    eps = float(np.abs(gpu_scores - scores).max())
+    n_diff = margin_check(hi[0], scores, 2592, margin=1e-3 + 2 * eps)
+    common = np.intersect1d(hi[0], ref_i[0])
     gpos = np.searchsorted(hi[0], common)
     rpos = np.searchsorted(ref_i[0], common)
-    assert max_rel_err(hf[0][gpos], ref_f[0][rpos]) < SPEC_TOL
+    err = max_rel_err(hf[0][gpos], ref_f[0][rpos])
+    print(f"[parity] 2-block encoder: score eps {eps:.3e}, kept tokens differing {n_diff}, "
+          f"normwise {err:.3e}, elementwise {elem_rel_err(hf[0][gpos], ref_f[0][rpos]):.3e}")
+    assert err < SPEC_TOL
 
 
 def test_encoder_full_32_blocks_properties(ctx_full, sam3, oracle):

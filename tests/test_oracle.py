@@ -9,7 +9,7 @@ import math
 import numpy as np
 import pytest
 
-from util import f16_ulps, max_rel_err
+from util import f16_ulps, max_rel_err, staged_encoder
 
 F16 = np.float16
 
@@ -338,3 +338,93 @@ def test_prune_keep_extremes_known_answer(oracle, keep, order):
         assert np.array_equal(idx[b], want)
         assert np.array_equal(feats[b * keep:(b + 1) * keep].view(np.uint16),
                               x[b * seq + want].view(np.uint16))
+
+
+# ------------------------------------------------------------------ reference rounding points
+def _graph_ops_numpy(h0, bias, epi, residual=None, table=None, heads=2, head_dim=8):
+    """numpy restatement of the reference's fp16 graph ops after the matmul:
+    every op on fp16 operands is computed in float32 and rounded to fp16
+    (numpy's float16 arithmetic), as MPSGraph returns an fp16 tensor per op.
+    MPSAttention.swift:113-160 (bias, RoPE with cos/sin cast to fp16) and
+    ViTEncoder.swift:559-605 (residual) / :581-589 (GELU)."""
+    from scipy.special import erf
+    r = (h0 + bias.astype(F16)).astype(F16)
+    if epi == 1:
+        sqrt2 = F16(1.41421356)
+        div = (r / sqrt2).astype(F16)
+        e = erf(div.astype(np.float64)).astype(F16)
+        return ((F16(0.5) * r).astype(F16) * (F16(1.0) + e).astype(F16)).astype(F16)
+    if epi == 2:
+        return (residual.astype(F16) + r).astype(F16)
+    if epi == 3:
+        out = r.copy()
+        qk = 2 * heads * head_dim
+        for i in range(r.shape[0]):
+            t = table[i % table.shape[0]].astype(F16)  # [head_dim/2, 2], cast to fp16
+            for j in range(0, qk, 2):
+                p = (j % head_dim) // 2
+                c, s = t[p, 0], t[p, 1]
+                a, b = r[i, j], r[i, j + 1]
+                out[i, j] = F16(F16(a * c) - F16(b * s))
+                out[i, j + 1] = F16(F16(a * s) + F16(b * c))
+        return out
+    return r
+
+
+@pytest.mark.parametrize("epi", [0, 1, 2, 3])
+def test_graph_rounding_linear_matches_numpy(oracle, epi):
+    # The matmul result rounded to fp16 comes from the oracle itself (graph
+    # mode, no bias), so the comparison covers the ops after it bit for bit.
+    m, k, heads, hd = 24, 64, 2, 8
+    n = 3 * heads * hd
+    x = oracle.gen_normal(81, 1, (m, k))
+    idx = oracle.gen_u8(81, 2, (n, k))
+    pal = oracle.gen_palette(81, 3, n, 0.2)
+    bias = oracle.gen_normal(81, 4, (n,), 0.0, 0.5)
+    res = oracle.gen_normal(81, 5, (m, n))
+    table = oracle.rope_table(4, 6, hd)
+    with oracle.rounding(oracle.ROUND_GRAPH):
+        h0 = oracle.linear(x, idx, pal, None, epilogue=0)
+        got = oracle.linear(x, idx, pal, bias, epilogue=epi,
+                            residual=res if epi == 2 else None,
+                            rope=table if epi == 3 else None, rope_period=24,
+                            heads=heads, head_dim=hd)
+    ref = _graph_ops_numpy(h0, bias, epi, res, table, heads, hd)
+    assert np.array_equal(got.view(np.uint16), ref.view(np.uint16))
+    # the mode is restored on exit, and the two modes agree within the spec
+    assert oracle.lib().so_rounding() == oracle.ROUND_FUSED
+    fused = oracle.linear(x, idx, pal, bias, epilogue=epi, residual=res if epi == 2 else None,
+                          rope=table if epi == 3 else None, rope_period=24, heads=heads,
+                          head_dim=hd)
+    assert max_rel_err(got, fused) < 1e-2
+
+
+def test_graph_rounding_layernorm_matches_numpy(oracle):
+    # ViTEncoder.swift:466-474: mean, variance about the fp16 mean, centre,
+    # sqrt(var + eps), divide, scale, shift, each an fp16 tensor
+    x = oracle.gen_normal(82, 1, (16, 256), 0.3, 2.0)
+    g = oracle.gen_normal(82, 2, (256,), 1.0, 0.1)
+    b = oracle.gen_normal(82, 3, (256,), 0.0, 0.1)
+    with oracle.rounding(oracle.ROUND_GRAPH):
+        got = oracle.layernorm(x, g, b, 1e-6)
+    xd = x.astype(np.float64)
+    mean = xd.mean(axis=1, keepdims=True).astype(np.float32).astype(F16)
+    var = ((xd - mean.astype(np.float64)) ** 2).mean(axis=1, keepdims=True).astype(
+        np.float32).astype(F16)
+    denom = np.sqrt((var + F16(1e-6)).astype(F16)).astype(F16)
+    cen = (x - mean).astype(F16)
+    ref = ((cen / denom).astype(F16) * g).astype(F16) + b
+    assert np.array_equal(got.view(np.uint16), ref.astype(F16).view(np.uint16))
+    fused = oracle.layernorm(x, g, b, 1e-6)
+    assert max_rel_err(got, fused) < 1e-2
+
+
+def test_staged_oracle_equals_encoder_forward(oracle):
+    # small shape: the staged composition used above is the oracle's encoder
+    blocks = [oracle.SyntheticBlock(55, i, 256, 512) for i in range(3)]
+    pw = oracle.gen_normal(55, 900, (256, 3, 14, 14), 0.0, 0.02)
+    pb = oracle.gen_normal(55, 901, (256,), 0.0, 0.02)
+    img = oracle.gen_uniform(55, 77, (1, 112, 112, 3), -1.0, 1.0)
+    _, f, i = staged_encoder(oracle, img, blocks, pw, pb, prune_after=2, keep=32)
+    ef, ei = oracle.encoder_forward(img, blocks, pw, pb, heads=4, prune_after=2, keep=32)
+    assert np.array_equal(i, ei[0]) and np.array_equal(f.view(np.uint16), ef[0].view(np.uint16))

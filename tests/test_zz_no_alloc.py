@@ -6,14 +6,19 @@ cudaMalloc/cudaFree, callers without a sam3 context) pass their own buffers and
 the stream; the entry point keeps its per-token scores in a fixed device array
 inside the library. This test calls it through the C ABI twice in a row, with
 different inputs, and checks each result against sam3_prune (the context
-entry point) on the same input. The two share their kernels, so indices,
-features and RoPE rows must be identical. The test allocates its buffers
-through a context; the entry point under test allocates nothing.
+entry point) on the same input, where the two share their kernels, so
+indices, features and RoPE rows must be identical, and against the oracle's
+prune, where the indices must agree wherever the score margin at the cut
+exceeds 1e-3 and the gathered rows must equal the input rows they name. The
+test allocates its buffers through a context; the entry point under test
+allocates nothing.
 """
 import ctypes as C
 
 import numpy as np
 import pytest
+
+from util import margin_check
 
 pytestmark = pytest.mark.gpu
 F16 = np.float16
@@ -55,6 +60,18 @@ def test_prune_noalloc_matches_context_entry_point(sam3, oracle):
             assert np.array_equal(gi, ri)
             assert np.array_equal(gf, rf)
             assert np.array_equal(gr, rr)
+            # the oracle's prune on the same input
+            of, orr, oi = oracle.prune(x, batch, seq, keep, norm=norm, order=order, rope=table)
+            scores = oracle.token_scores(x, norm).astype(np.float64).reshape(batch, seq)
+            for b in range(batch):
+                if order == sam3.ORDER_INDEX:
+                    assert (np.diff(gi[b]) > 0).all()
+                margin_check(gi[b], scores[b], keep)
+            rows = (gi + seq * np.arange(batch)[:, None]).reshape(-1)
+            assert np.array_equal(gf, x[rows].view(np.uint16))
+            assert np.array_equal(gr, table[gi.reshape(-1)])
+            if np.array_equal(gi, oi):
+                assert np.array_equal(gf, of.view(np.uint16)) and np.array_equal(gr, orr)
 
 
 def test_prune_noalloc_rejects_sizes_beyond_its_scratch(sam3):
