@@ -3,7 +3,8 @@
 // o[b*S + i, h*64 + :] = softmax_j(q_i . k_j * scale) v_j, per image b and
 // head h, reading q | k | v straight from the QKV GEMM output
 // [B*S, 3*H*64] (no transpose pass) and writing the [B*S, H*64] layout the
-// out-projection GEMM consumes. The kernel is in attention_tc.cu.
+// out-projection GEMM consumes. The kernels are in attention_pp.cu (global
+// attention) and attention_tc.cu (windowed attention).
 //
 // Reference: scaledDotProductAttention in MPSAttentionLayer
 // (MPSAttention.swift:165-176, scale 1/sqrt(64), no mask) and the explicit
@@ -14,6 +15,8 @@
 namespace sam3 {
 
 sam3_status_t attention_tc(sam3_ctx_t* ctx, const uint16_t* qkv, int batch, int seq, int heads,
+                           float scale, uint16_t* o, int groups, int img_rows, int first_row);
+sam3_status_t attention_pp(sam3_ctx_t* ctx, const uint16_t* qkv, int batch, int seq, int heads,
                            float scale, uint16_t* o, int groups, int img_rows, int first_row);
 
 sam3_status_t attention_grouped(sam3_ctx_t* ctx, const uint16_t* qkv, int images, int groups,
@@ -32,6 +35,11 @@ sam3_status_t attention_grouped(sam3_ctx_t* ctx, const uint16_t* qkv, int images
   ProfScope prof(ctx, SAM3_PROF_ATTENTION,
                  4.0 * images * groups * heads * (double)seq * seq * kHeadDim,
                  8.0 * images * groups * seq * heads * kHeadDim);
+  // Global attention over whole images takes the 128-key, two-query-tile
+  // kernel; windows (groups of a few hundred rows) keep the 64-key kernel,
+  // whose 128-row CTAs waste less on a short ragged group.
+  if (groups == 1)
+    return attention_pp(ctx, qkv, images, seq, heads, scale, o, groups, img_rows, first_row);
   return attention_tc(ctx, qkv, images, seq, heads, scale, o, groups, img_rows, first_row);
 }
 

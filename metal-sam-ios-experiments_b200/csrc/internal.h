@@ -87,7 +87,8 @@ sam3_status_t check_cuda(sam3_ctx_t* ctx, cudaError_t e, const char* what);
 // Raise `kernel`'s dynamic shared-memory limit to `bytes` once per context:
 // the attribute belongs to the device, and each context is bound to one.
 enum : uint32_t {
-  kSmemAttn = 1u, kSmemWs = 2u, kSmemWsc = 4u, kSmemGemm = 8u /* << MODE */, kSmemPrune = 64u
+  kSmemAttn = 1u, kSmemWs = 2u, kSmemWsc = 4u, kSmemGemm = 8u /* << MODE */, kSmemPrune = 64u,
+  kSmemAttnPP = 128u
 };
 template <typename Kernel>
 sam3_status_t ensure_smem_attr(sam3_ctx_t* ctx, uint32_t bit, Kernel kernel, int bytes,

@@ -16,6 +16,8 @@
 #include <numeric>
 #include <vector>
 
+#include <immintrin.h>
+
 #ifdef _OPENMP
 #include <omp.h>
 #endif
@@ -65,60 +67,72 @@ std::vector<float> to_float(const uint16_t* x, int64_t n) {
   return f;
 }
 
-inline float dot8(const float* a, const float* b, int64_t k) {
-  v8f acc = {0, 0, 0, 0, 0, 0, 0, 0};
-  int64_t i = 0;
-  for (; i + 8 <= k; i += 8) {
-    v8f va, vb;
-    std::memcpy(&va, a + i, 32);
-    std::memcpy(&vb, b + i, 32);
-    acc += va * vb;
+// ---- float32 GEMM C[m][n] = sum_k A[m][k] * B[n][k] (both operands K-major).
+// Panels of A (6 rows) and B (16 rows) are packed k-interleaved and an AVX2
+// 6x16 register tile accumulates each C element in one fp32 sum over k in
+// order. gemm_nt_tile computes one block of C on the calling thread;
+// gemm_nt spreads the blocks over the OpenMP threads.
+constexpr int64_t kMR = 6, kNR = 16, kKC = 256, kMB = 96, kNB = 192;
+
+// C[0:mr][0:nr] (+)= Ap (packed [kc][6]) . Bp (packed [kc][16])^T
+inline void micro_6x16(const float* Ap, const float* Bp, int64_t kc, float* C, int64_t ldc,
+                       int mr, int nr, bool accumulate) {
+  __m256 c[6][2];
+  for (int r = 0; r < 6; ++r) c[r][0] = c[r][1] = _mm256_setzero_ps();
+  for (int64_t p = 0; p < kc; ++p) {
+    const __m256 b0 = _mm256_loadu_ps(Bp + p * 16), b1 = _mm256_loadu_ps(Bp + p * 16 + 8);
+    for (int r = 0; r < 6; ++r) {
+      const __m256 a = _mm256_broadcast_ss(Ap + p * 6 + r);
+      c[r][0] = _mm256_fmadd_ps(a, b0, c[r][0]);
+      c[r][1] = _mm256_fmadd_ps(a, b1, c[r][1]);
+    }
   }
-  float s = 0.f;
-  for (int l = 0; l < 8; ++l) s += acc[l];
-  for (; i < k; ++i) s += a[i] * b[i];
-  return s;
+  alignas(32) float t[6][16];
+  for (int r = 0; r < 6; ++r) {
+    _mm256_store_ps(t[r], c[r][0]);
+    _mm256_store_ps(t[r] + 8, c[r][1]);
+  }
+  for (int r = 0; r < mr; ++r)
+    for (int q = 0; q < nr; ++q) C[r * ldc + q] = accumulate ? C[r * ldc + q] + t[r][q] : t[r][q];
 }
 
-// C[i][j] = sum_k A[i][k] * B[j][k], float32 accumulation, blocked for cache.
-void gemm_nt(const float* A, int64_t m, const float* B, int64_t n, int64_t k,
-             float* C) {
-  const int64_t MB = 64, NB = 64;
-  const int64_t mblocks = (m + MB - 1) / MB, nblocks = (n + NB - 1) / NB;
-#pragma omp parallel for collapse(2) schedule(dynamic, 1)
-  for (int64_t bi = 0; bi < mblocks; ++bi) {
-    for (int64_t bj = 0; bj < nblocks; ++bj) {
-      const int64_t i0 = bi * MB, i1 = std::min(m, i0 + MB);
-      const int64_t j0 = bj * NB, j1 = std::min(n, j0 + NB);
-      int64_t i = i0;
-      for (; i + 4 <= i1; i += 4) {
-        int64_t j = j0;
-        for (; j + 4 <= j1; j += 4) {
-          v8f acc[4][4];
-          for (int a = 0; a < 4; ++a)
-            for (int b = 0; b < 4; ++b) acc[a][b] = (v8f){0, 0, 0, 0, 0, 0, 0, 0};
-          int64_t kk = 0;
-          for (; kk + 8 <= k; kk += 8) {
-            v8f va[4], vb[4];
-            for (int a = 0; a < 4; ++a) std::memcpy(&va[a], A + (i + a) * k + kk, 32);
-            for (int b = 0; b < 4; ++b) std::memcpy(&vb[b], B + (j + b) * k + kk, 32);
-            for (int a = 0; a < 4; ++a)
-              for (int b = 0; b < 4; ++b) acc[a][b] += va[a] * vb[b];
-          }
-          for (int a = 0; a < 4; ++a)
-            for (int b = 0; b < 4; ++b) {
-              float s = 0.f;
-              for (int l = 0; l < 8; ++l) s += acc[a][b][l];
-              for (int64_t t = kk; t < k; ++t) s += A[(i + a) * k + t] * B[(j + b) * k + t];
-              C[(i + a) * n + j + b] = s;
-            }
-        }
-        for (; j < j1; ++j)
-          for (int a = 0; a < 4; ++a) C[(i + a) * n + j] = dot8(A + (i + a) * k, B + j * k, k);
-      }
-      for (; i < i1; ++i)
-        for (int64_t j = j0; j < j1; ++j) C[i * n + j] = dot8(A + i * k, B + j * k, k);
+// One block of C: rows [i0, i1), columns [j0, j1), single thread. `pa`/`pb`
+// are scratch of kMB*kKC and kNB*kKC floats.
+void gemm_nt_tile(const float* A, const float* B, int64_t n, int64_t k, float* C,
+                  int64_t i0, int64_t i1, int64_t j0, int64_t j1, float* pa, float* pb) {
+  for (int64_t k0 = 0; k0 < k; k0 += kKC) {
+    const int64_t kc = std::min(kKC, k - k0);
+    // pack B rows j0..j1 in panels of 16: pb[panel][p][16]
+    for (int64_t j = j0; j < j1; j += kNR) {
+      float* dst = pb + ((j - j0) / kNR) * kKC * kNR;
+      const int64_t nr = std::min(kNR, j1 - j);
+      for (int64_t p = 0; p < kc; ++p)
+        for (int64_t q = 0; q < kNR; ++q)
+          dst[p * kNR + q] = q < nr ? B[(j + q) * k + k0 + p] : 0.f;
     }
+    for (int64_t i = i0; i < i1; i += kMR) {
+      const int64_t mr = std::min(kMR, i1 - i);
+      for (int64_t p = 0; p < kc; ++p)
+        for (int64_t r = 0; r < kMR; ++r) pa[p * kMR + r] = r < mr ? A[(i + r) * k + k0 + p] : 0.f;
+      for (int64_t j = j0; j < j1; j += kNR) {
+        const int64_t nr = std::min(kNR, j1 - j);
+        micro_6x16(pa, pb + ((j - j0) / kNR) * kKC * kNR, kc, C + i * n + j, n, (int)mr,
+                   (int)nr, k0 > 0);
+      }
+    }
+  }
+}
+
+void gemm_nt(const float* A, int64_t m, const float* B, int64_t n, int64_t k, float* C) {
+  const int64_t mblocks = (m + kMB - 1) / kMB, nblocks = (n + kNB - 1) / kNB;
+#pragma omp parallel
+  {
+    std::vector<float> pa((size_t)(kKC * kMR)), pb((size_t)(kNB * kKC));
+#pragma omp for collapse(2) schedule(dynamic, 1)
+    for (int64_t bi = 0; bi < mblocks; ++bi)
+      for (int64_t bj = 0; bj < nblocks; ++bj)
+        gemm_nt_tile(A, B, n, k, C, bi * kMB, std::min(m, (bi + 1) * kMB), bj * kNB,
+                     std::min(n, (bj + 1) * kNB), pa.data(), pb.data());
   }
 }
 
@@ -392,45 +406,56 @@ void so_rope_apply(uint16_t* qkv, int64_t m, int heads, int head_dim,
 // scale 1/sqrt(d)); AttentionKernels.swift:48-68 (explicit softmax form).
 void so_attention(const uint16_t* qkv, int batch, int64_t seq, int heads,
                   int head_dim, float scale, uint16_t* o) {
-  const int64_t dim = (int64_t)heads * head_dim;
+  // Blocks of 64 query rows: S = Q K^T and O = P V as float32 GEMMs, the
+  // softmax in between in float32 (row max, exp, row sum), one fp16 rounding
+  // of O / rowsum at the end.
+  const int64_t dim = (int64_t)heads * head_dim, hd = head_dim, QB = 64;
+  const int64_t nqb = (seq + QB - 1) / QB;
+  std::vector<float> q((size_t)(heads * seq * hd)), kk((size_t)(heads * seq * hd)),
+      vt((size_t)(heads * hd * seq));
   for (int b = 0; b < batch; ++b) {
-    for (int h = 0; h < heads; ++h) {
-      std::vector<float> q((size_t)(seq * head_dim)), kk((size_t)(seq * head_dim)),
-          v((size_t)(seq * head_dim));
 #pragma omp parallel for schedule(static)
-      for (int64_t s = 0; s < seq; ++s) {
-        const uint16_t* row = qkv + (b * seq + s) * 3 * dim + (int64_t)h * head_dim;
-        for (int d = 0; d < head_dim; ++d) {
-          q[(size_t)(s * head_dim + d)] = h2f(row[d]);
-          kk[(size_t)(s * head_dim + d)] = h2f(row[dim + d]);
-          v[(size_t)(s * head_dim + d)] = h2f(row[2 * dim + d]);
+    for (int64_t s = 0; s < seq; ++s) {
+      const uint16_t* row = qkv + (b * seq + s) * 3 * dim;
+      for (int h = 0; h < heads; ++h)
+        for (int64_t d = 0; d < hd; ++d) {
+          q[(size_t)((h * seq + s) * hd + d)] = h2f(row[h * hd + d]);
+          kk[(size_t)((h * seq + s) * hd + d)] = h2f(row[dim + h * hd + d]);
+          vt[(size_t)((h * hd + d) * seq + s)] = h2f(row[2 * dim + h * hd + d]);
         }
-      }
+    }
 #pragma omp parallel
-      {
-        std::vector<float> p((size_t)seq), acc((size_t)head_dim);
-#pragma omp for schedule(static)
-        for (int64_t i = 0; i < seq; ++i) {
-          const float* qi = q.data() + i * head_dim;
-          float mx = -INFINITY;
-          for (int64_t j = 0; j < seq; ++j) {
-            p[(size_t)j] = dot8(qi, kk.data() + j * head_dim, head_dim) * scale;
-            mx = std::max(mx, p[(size_t)j]);
+    {
+      std::vector<float> S((size_t)(QB * seq)), acc((size_t)(QB * hd)),
+          pa((size_t)(kKC * kMR)), pb((size_t)(kNB * kKC));
+#pragma omp for collapse(2) schedule(dynamic, 1)
+      for (int h = 0; h < heads; ++h) {
+        for (int64_t qb = 0; qb < nqb; ++qb) {
+          const int64_t i0 = qb * QB, rows = std::min(QB, seq - i0);
+          const float* qh = q.data() + (h * seq + i0) * hd;
+          const float* kh = kk.data() + h * seq * hd;
+          for (int64_t j0 = 0; j0 < seq; j0 += kNB)
+            gemm_nt_tile(qh, kh, seq, hd, S.data(), 0, rows, j0, std::min(seq, j0 + kNB),
+                         pa.data(), pb.data());
+          std::vector<float> l((size_t)rows);
+          for (int64_t r = 0; r < rows; ++r) {
+            float* sr = S.data() + r * seq;
+            float mx = -INFINITY;
+            for (int64_t j = 0; j < seq; ++j) mx = std::max(mx, sr[j] * scale);
+            float sum = 0.f;
+            for (int64_t j = 0; j < seq; ++j) {
+              sr[j] = std::exp(sr[j] * scale - mx);
+              sum += sr[j];
+            }
+            l[(size_t)r] = sum;
           }
-          float l = 0.f;
-          for (int64_t j = 0; j < seq; ++j) {
-            p[(size_t)j] = std::exp(p[(size_t)j] - mx);
-            l += p[(size_t)j];
+          gemm_nt_tile(S.data(), vt.data() + h * hd * seq, hd, seq, acc.data(), 0, rows, 0, hd,
+                       pa.data(), pb.data());
+          for (int64_t r = 0; r < rows; ++r) {
+            const float inv = 1.f / l[(size_t)r];
+            uint16_t* orow = o + (b * seq + i0 + r) * dim + (int64_t)h * hd;
+            for (int64_t d = 0; d < hd; ++d) orow[d] = f2h(acc[(size_t)(r * hd + d)] * inv);
           }
-          std::fill(acc.begin(), acc.end(), 0.f);
-          for (int64_t j = 0; j < seq; ++j) {
-            const float pj = p[(size_t)j];
-            const float* vj = v.data() + j * head_dim;
-            for (int d = 0; d < head_dim; ++d) acc[(size_t)d] += pj * vj[d];
-          }
-          const float inv = 1.f / l;
-          uint16_t* orow = o + (b * seq + i) * dim + (int64_t)h * head_dim;
-          for (int d = 0; d < head_dim; ++d) orow[d] = f2h(acc[(size_t)d] * inv);
         }
       }
     }

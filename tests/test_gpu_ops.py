@@ -312,7 +312,8 @@ def test_attention_zero_query_is_mean_of_v(ctx, sam3, oracle):
     assert np.abs(got - v.mean(0)).max() < 2e-3
 
 
-@pytest.mark.parametrize("batch,seq,heads", [(3, 300, 2), (2, 2592, 4), (1, 129, 1)])
+@pytest.mark.parametrize("batch,seq,heads", [(3, 300, 2), (2, 2592, 4), (1, 129, 1), (2, 256, 2),
+                                            (2, 257, 1), (1, 384, 2), (2, 128, 2)])
 def test_attention_batched_ragged_tiles(ctx, sam3, oracle, batch, seq, heads):
     # key tiles of 128 that straddle image boundaries or end past the buffer
     qkv = oracle.gen_normal(15, seq, (batch * seq, 3 * heads * 64))
