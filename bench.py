@@ -10,6 +10,19 @@ calls of --batch images. Synthetic data with the spec's distributions, random
 weights of the spec's architecture.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--config c4|c3|c2|c1|c0]
+
+--config picks the workload (default c4, the line above):
+  c4  the batched encoder above (images/s);
+  c3  the same encoder on one image per call, 1 GPU (images/s);
+  c2  attention block at the 72x72 grid: LN, palettized QKV + 2D RoPE,
+      attention, palettized out-proj + residual (TFLOP/s);
+  c1  MLP block at 5184 tokens: LN, palettized fc1 + GELU, fc2 + residual
+      (TFLOP/s);
+  c0  palettized QKV projection 5184 x 3072 x 1024 + bias (TFLOP/s).
+c0-c2 fit in L2, so every timed step is preceded (outside its events) by a
+write of 256 MB and a fresh copy of the inputs; value sums the per-step
+event times.
 
 N > 1 is launched by torch.distributed.run (one rank per GPU). Rank 0 prints
 one JSON line:
@@ -29,7 +42,10 @@ one JSON line:
   cpu_baseline  the CPU oracle (a C++ restatement of the path) on a bounded
           sample, rank 0 at N=1 only.
 --impl reference times the reference path's CPU restatement (the reference
-itself is Swift/Metal and cannot run here) on the same workload and metric.
+itself is Swift/Metal and cannot run here) on the same workload and metric,
+on all host cores: each timed step is one whole unit of the workload (one
+1008^2 image through all 32 blocks for c3/c4, one full operator call for
+c0-c2), nothing extrapolated.
 """
 from __future__ import annotations
 
@@ -56,8 +72,55 @@ SEQ = GRID * GRID
 KEEP = SEQ // 2
 DIM, HEADS, HIDDEN, BLOCKS = 1024, 16, 4096, 32
 
+# Per-call algorithmic FLOPs of the single-operator configs (2*M*N*K for the
+# linears, 4*S^2*64 per head for attention).
+_LIN = lambda m, n, k: 2.0 * m * n * k
+CONFIGS = {
+    "c0": {"what": "palettized QKV projection 5184 x 3072 x 1024 + bias",
+           "flops": _LIN(SEQ, 3 * DIM, DIM)},
+    "c1": {"what": "MLP block at 5184 tokens: LN, palettized fc1 1024->4096 + GELU, "
+                   "fc2 4096->1024 + residual",
+           "flops": _LIN(SEQ, HIDDEN, DIM) + _LIN(SEQ, DIM, HIDDEN)},
+    "c2": {"what": "attention block at the 72x72 grid: LN, palettized QKV + 2D RoPE, "
+                   "16-head attention, palettized out-proj + residual",
+           "flops": _LIN(SEQ, 3 * DIM, DIM) + _LIN(SEQ, DIM, DIM) + 4.0 * HEADS * SEQ * SEQ * 64},
+}
+
+
+METRIC_C3 = ("encoder images/s at 1008^2, one image per call (32-block uint8-palettized ViT, "
+             "prune to 2592 after block 16)")
+
+
+def metric_of(config):
+    """(metric, unit) of a --config."""
+    if config == "c4":
+        return METRIC, UNIT
+    if config == "c3":
+        return METRIC_C3, UNIT
+    return f"{config} {CONFIGS[config]['what']}: TFLOP/s", "TFLOP/s"
+
+
+def op_config(config):
+    return {"workload": f"{config} {CONFIGS[config]['what']}; fp16 activations, uint8 indices, "
+                        "per-output-channel 256-entry fp16 palettes",
+            "tokens": SEQ, "algorithmic_gflop_per_call": CONFIGS[config]["flops"] / 1e9,
+            "parallelism": "single GPU",
+            "l2": "inputs fit in L2: a 256 MB write and a fresh copy of the inputs precede "
+                  "every timed call, outside its CUDA events"}
+
 
 def workload_config(args, world):
+    if args.config in CONFIGS:
+        return op_config(args.config)
+    if args.config == "c3":
+        return {
+            "workload": "c3 encoder, one image per call: seeded 1008x1008 images, 32-block "
+                        "uint8-palettized ViT (D 1024, 16 heads, MLP 4096), 5184 tokens pruned "
+                        "to 2592 by L2 norm after block 16",
+            "images": args.images, "images_per_gpu": args.images // world, "batch_per_call": 1,
+            "parallelism": f"dp{world} (one image per GPU per step)",
+            "l2": "inputs larger than L2: 554 MB of palettized weights are streamed every step",
+        }
     return {
         "workload": "c4 batched encoder: 64 seeded 1008x1008 images, 32-block uint8-palettized "
                     "ViT (D 1024, 16 heads, MLP 4096, per-output-channel 256-entry fp16 "
@@ -164,39 +227,66 @@ class ClockSampler:
                 "samples": len(mine)}
 
 
-# ---------------------------------------------------------------- CPU oracle sample
-def cpu_oracle_sample(repeats=1):
-    """Per-image time of the CPU oracle on one 1008^2 image, extrapolated from a
-    bounded sample: patch embedding + block 1 (5184 tokens) + prune + block 17
-    (2592 tokens), with the two blocks weighted x16 each."""
-    import numpy as np
+# ---------------------------------------------------------------- CPU oracle
+def _oracle():
     from oracle import oracle as O
     O.build()
     # every host core this process may run on (torch.distributed.run sets
     # OMP_NUM_THREADS=1 for each rank, which would time a single core)
     O.set_num_threads(len(os.sched_getaffinity(0)))
-    blk_a = O.SyntheticBlock(7, 0)
-    blk_b = O.SyntheticBlock(7, 16)
-    img = O.gen_uniform(7, 1, (1, IMAGE, IMAGE, 3), -1.0, 1.0)
-    pw = O.gen_normal(7, 2, (DIM, 3, 14, 14), 0.0, 0.02)
-    pb = O.gen_normal(7, 3, (DIM,), 0.0, 0.02)
-    table = O.rope_table(GRID, GRID)
-    best = None
-    for _ in range(repeats):
+    return O
+
+
+class OracleEncoder:
+    """The CPU oracle's encoder (c3/c4 unit: one 1008^2 image through all 32
+    blocks, prune to 2592 after block 16) on seeded weights."""
+
+    def __init__(self, blocks=BLOCKS):
+        self.O = _oracle()
+        self.blocks = [self.O.SyntheticBlock(7, i) for i in range(blocks)]
+        self.pw = self.O.gen_normal(7, 2, (DIM, 3, 14, 14), 0.0, 0.02)
+        self.pb = self.O.gen_normal(7, 3, (DIM,), 0.0, 0.02)
+        self.img = self.O.gen_uniform(7, 1, (1, IMAGE, IMAGE, 3), -1.0, 1.0)
+
+    def run(self, blocks=None):
+        blks = self.blocks if blocks is None else self.blocks[:blocks]
         t0 = time.perf_counter()
-        x = O.patch_embed(img, pw, pb, 14)
-        t1 = time.perf_counter()
-        x = O.vit_block(x, 1, SEQ, HEADS, blk_a, table, SEQ)
-        t2 = time.perf_counter()
-        xp, rope_p, _ = O.prune(x, 1, SEQ, KEEP, rope=table, rope_period=SEQ)
-        t3 = time.perf_counter()
-        O.vit_block(xp, 1, KEEP, HEADS, blk_b, rope_p, KEEP)
-        t4 = time.perf_counter()
-        per_image = (t1 - t0) + 16 * (t2 - t1) + (t3 - t2) + 16 * (t4 - t3)
-        best = per_image if best is None else min(best, per_image)
-    return {"seconds_per_image": best, "cores": O.num_threads(),
-            "sample": "1 image 1008^2: patch embed + block 1 (5184 tokens) + prune + block 17 "
-                      "(2592 tokens) timed, blocks extrapolated x16 each to 32 blocks"}
+        self.O.encoder_forward(self.img, blks, self.pw, self.pb, heads=HEADS,
+                               prune_after=min(16, len(blks)), keep=KEEP)
+        return time.perf_counter() - t0
+
+    def sample(self):
+        return "1 image 1008^2 through the oracle's 32-block encoder (prune after block 16), timed whole"
+
+
+class OracleOp:
+    """The CPU oracle on one full c0 / c1 / c2 operator call."""
+
+    def __init__(self, config):
+        O = self.O = _oracle()
+        self.config = config
+        self.x = O.gen_normal(8, 1, (SEQ, DIM))
+        self.blk = O.SyntheticBlock(8, 0)
+        self.table = O.rope_table(GRID, GRID)
+
+    def run(self):
+        O, blk, x = self.O, self.blk, self.x
+        lin = lambda d: {"idx": d["idx"], "palette": d["palette"], "bias": d["bias"]}
+        t0 = time.perf_counter()
+        if self.config == "c0":
+            O.linear(x, **lin(blk.qkv))
+        elif self.config == "c1":
+            h = O.linear(O.layernorm(x), **lin(blk.fc1), epilogue=O.EPI_BIAS_GELU)
+            O.linear(h, **lin(blk.fc2), epilogue=O.EPI_BIAS_RESIDUAL, residual=x)
+        else:
+            qkv = O.linear(O.layernorm(x), **lin(blk.qkv), epilogue=O.EPI_BIAS_ROPE_QKV,
+                           rope=self.table, rope_period=SEQ)
+            att = O.attention(qkv, 1, SEQ, HEADS, 64)
+            O.linear(att, **lin(blk.proj), epilogue=O.EPI_BIAS_RESIDUAL, residual=x)
+        return time.perf_counter() - t0
+
+    def sample(self):
+        return f"one full {self.config} call ({CONFIGS[self.config]['what']}), timed whole"
 
 
 # ---------------------------------------------------------------- synthetic weights
@@ -237,26 +327,39 @@ def dist_env():
 
 def run_reference(args):
     """CPU restatement of the reference path (the reference's Swift/Metal code
-    cannot run here), timed on the host cores on the same workload and metric."""
+    cannot run here), timed on all host cores on the same workload and metric.
+    Each timed step is one whole unit: one image through all 32 blocks (c3,
+    c4) or one full operator call (c0-c2). Warm-up steps (threads, caches) run
+    a 2-block image for c3/c4."""
     world, rank, _ = dist_env()
     if rank != 0:
         return 0
-    samples = []
-    for i in range(args.warmup + args.steps):
-        r = cpu_oracle_sample(1)
-        if i >= args.warmup:
-            samples.append(r["seconds_per_image"])
-    spi = statistics.median(samples)
-    value = 1.0 / spi
+    metric, unit = metric_of(args.config)
+    if args.config in ("c3", "c4"):
+        unit_of_work = OracleEncoder()
+        for _ in range(args.warmup):
+            unit_of_work.run(blocks=2)
+        times = [unit_of_work.run() for _ in range(args.steps)]
+        per_step = statistics.median(times)
+        value = 1.0 / per_step
+    else:
+        unit_of_work = OracleOp(args.config)
+        for _ in range(args.warmup):
+            unit_of_work.run()
+        times = [unit_of_work.run() for _ in range(args.steps)]
+        per_step = statistics.median(times)
+        value = CONFIGS[args.config]["flops"] / per_step / 1e12
     line = {
-        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT,
+        "impl": "reference", "metric": metric, "value": value, "unit": unit,
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": spi * args.images * 1e3, "higher_is_better": True,
+        "ms_per_step": per_step * 1e3, "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "fp16 storage, fp32 accumulate",
         "data": "synthetic", "config": workload_config(args, world),
-        "cpu_baseline": {"value": value, "unit": UNIT, "cores": r["cores"], "kind": "port",
-                         "sample": r["sample"] + "; each step = one such sample"},
-        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "cpu_baseline": {"value": value, "unit": unit, "cores": unit_of_work.O.num_threads(),
+                         "kind": "port",
+                         "sample": unit_of_work.sample() + "; each timed step = one such unit "
+                                   "(median of the steps)"},
+        "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
     return 0
@@ -399,11 +502,12 @@ def run_ours(args):
     result = None
     if rank == 0:
         value = args.images * args.steps / (ms_max * 1e-3)
+        metric, _ = metric_of(args.config)
         flops = encoder_flops_per_image()
         total_flops = sum(flops.values()) * args.images
         step_ms = ms_max / args.steps
         result = {
-            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+            "metric": metric, "value": value, "unit": UNIT, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_ms,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": "fp16 (uint8-palette weights expanded to fp16 on chip, fp32 accumulate)",
@@ -440,10 +544,148 @@ def run_ours(args):
         dist.destroy_process_group()
     if rank == 0:
         if world == 1 and not args.no_cpu_baseline:
-            r = cpu_oracle_sample(1)
-            result["cpu_baseline"] = {"value": 1.0 / r["seconds_per_image"], "unit": UNIT,
-                                      "cores": r["cores"], "kind": "port", "sample": r["sample"]}
+            enc = OracleEncoder()
+            enc.run(blocks=2)
+            spi = enc.run()
+            result["cpu_baseline"] = {"value": 1.0 / spi, "unit": UNIT,
+                                      "cores": enc.O.num_threads(), "kind": "port",
+                                      "sample": enc.sample()}
         print(json.dumps(result), flush=True)
+    ctx.close()
+    return 0
+
+
+def run_op(args):
+    """c0-c2: one operator at the 72x72 grid through the C ABI on one GPU."""
+    import torch
+    import sam3cuda as sam3
+
+    world, rank, local = dist_env()
+    if world != 1:
+        raise SystemExit("--config c0, c1 and c2 run on one GPU")
+    cfg = args.config
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    ctx = sam3.Context(local, max_batch=1)
+    g = torch.Generator(device=dev)
+    g.manual_seed(4321)
+    keep = []
+
+    def lin(n, k):
+        idx = torch.randint(0, 256, (n, k), generator=g, device=dev, dtype=torch.uint8)
+        pal = (torch.randn((n, 256), generator=g, device=dev) * 0.02).half().float()
+        pal = pal.sort(dim=1).values.half().contiguous()
+        bias = (torch.randn((n,), generator=g, device=dev) * 0.01).half()
+        keep.extend((idx, pal, bias))
+        return sam3.palette_linear(idx, pal, bias, n, k)
+
+    ones = torch.ones(DIM, dtype=torch.float16, device=dev)
+    zeros = torch.zeros(DIM, dtype=torch.float16, device=dev)
+    qkv_w, proj_w = lin(3 * DIM, DIM), lin(DIM, DIM)
+    bw = sam3.block_weights(ones, zeros, qkv_w, proj_w, ones, zeros, lin(HIDDEN, DIM),
+                            lin(DIM, HIDDEN))
+    rope = torch.empty((SEQ, 32, 2), dtype=torch.float32, device=dev)
+    ctx.rope_table(GRID, GRID, 64, 10000.0, rope)
+    x0 = torch.randn((SEQ, DIM), generator=g, device=dev).half()
+    x = x0.clone()
+    out = torch.empty((SEQ, 3 * DIM), dtype=torch.float16, device=dev) if cfg == "c0" else x
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.ExternalStream(ctx.stream, device=dev)
+
+    def call():
+        if cfg == "c0":
+            ctx.linear_palette(x, SEQ, qkv_w, sam3.EPI_BIAS, out)
+        elif cfg == "c1":
+            ctx.mlp_block(x, SEQ, bw)
+        else:
+            ctx.attention_block(x, 1, SEQ, bw, rope, SEQ)
+
+    def prep():  # L2 flush and fresh inputs, outside the timed events
+        flush.zero_()
+        x.copy_(x0)
+        torch.cuda.synchronize()
+
+    def timed(fn, steps):
+        evs = []
+        for _ in range(steps):
+            prep()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            fn()
+            e1.record(stream)
+            evs.append((e0, e1))
+        ctx.sync()
+        torch.cuda.synchronize()
+        return sum(a.elapsed_time(b) for a, b in evs)
+
+    for _ in range(args.warmup):
+        prep()
+        call()
+    ctx.sync()
+    uuid = None
+    try:
+        uuid = "GPU-" + str(torch.cuda.get_device_properties(local).uuid)
+    except Exception:
+        pass
+    clocks = ClockSampler(uuid)
+    clocks.start()
+    launches0 = ctx.launches
+    ms = timed(call, args.steps)
+    launches = ctx.launches - launches0
+    clk = clocks.stop()
+    # per-kernel device time with events around every launch
+    ctx.profile_enable(True)
+    timed(call, args.steps)
+    prof = ctx.profile_read()
+    ctx.profile_enable(False)
+    # end to end: pinned host input in, result out, through sam3_upload /
+    # sam3_download around the operator
+    h_x = torch.empty(x.shape, dtype=torch.float16, pin_memory=True)
+    h_x.copy_(x0)
+    h_out = torch.empty(out.shape, dtype=torch.float16, pin_memory=True)
+
+    def call_e2e():
+        sam3.lib.sam3_upload(ctx.handle, x.data_ptr(), h_x.data_ptr(), h_x.numel() * 2)
+        call()
+        sam3.lib.sam3_download(ctx.handle, h_out.data_ptr(), out.data_ptr(), h_out.numel() * 2)
+
+    e2e_ms = timed(call_e2e, args.steps)
+    peaks = load_peaks()
+    flops = CONFIGS[cfg]["flops"]
+    metric, unit = metric_of(cfg)
+    dom = "attention" if cfg == "c2" else "gemm"
+    d = prof[dom]
+    dom_tf = d["flops"] / (d["ms"] * 1e-3) / 1e12 if d["ms"] > 0 else 0.0
+    result = {
+        "metric": metric, "value": flops * args.steps / (ms * 1e-3) / 1e12, "unit": unit,
+        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "fp16 (uint8-palette weights expanded to fp16 on chip, fp32 accumulate)",
+        "data": "synthetic", "config": workload_config(args, 1),
+        "e2e": {"value": flops * args.steps / (e2e_ms * 1e-3) / 1e12, "unit": unit,
+                "h2d_bytes_per_step": h_x.numel() * 2, "d2h_bytes_per_step": h_out.numel() * 2},
+        "roofline": {
+            "kernel": ("attn_pp_kernel (tcgen05 global attention)" if dom == "attention" else
+                       "palette-dequant tcgen05 GEMMs"),
+            "bound": "tensor", "achieved": dom_tf, "peak": peaks["bf16_tflops"],
+            "unit": "TFLOP/s", "frac": dom_tf / peaks["bf16_tflops"],
+            "peak_kind": f"bf16_tflops burst ({peaks['source']}; kernel timed alone)",
+            "traffic": None, "launches": d["launches"], "kernel_ms": d["ms"]},
+        "kernels": {k: {"launches": v["launches"], "ms": round(v["ms"], 4),
+                        "tflops": (v["flops"] / (v["ms"] * 1e-3) / 1e12) if v["ms"] and v["flops"] else None,
+                        "gbs": (v["bytes"] / (v["ms"] * 1e-3) / 1e9) if v["ms"] and v["bytes"] else None}
+                    for k, v in prof.items() if v["launches"]},
+        "gpu_launches": int(launches),
+        "clocks": clk,
+    }
+    if not args.no_cpu_baseline:
+        op = OracleOp(cfg)
+        op.run()
+        t = min(op.run() for _ in range(2))
+        result["cpu_baseline"] = {"value": flops / t / 1e12, "unit": unit,
+                                  "cores": op.O.num_threads(), "kind": "port",
+                                  "sample": op.sample()}
+    print(json.dumps(result), flush=True)
     ctx.close()
     return 0
 
@@ -459,12 +701,19 @@ def main():
                     help="images per encoder call (16: the post-prune GEMMs and attention "
                          "fill the GPU better than at 8; a rank with fewer images uses them all)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--config", choices=("c4", "c3", "c2", "c1", "c0"), default="c4",
+                    help="workload (see the module docstring); c4 is the benchmark line")
     args = ap.parse_args()
+    if args.config == "c3":  # one image per call, one image per GPU per step
+        args.images = int(os.environ.get("WORLD_SIZE", "1"))
+        args.batch = 1
     if args.warmup < 3 and args.impl == "ours":
         print("note: warm-up raised to the minimum of 3 steps", file=sys.stderr)
         args.warmup = 3
     if args.impl == "reference":
         return run_reference(args)
+    if args.config in CONFIGS:
+        return run_op(args)
     return run_ours(args)
 
 

@@ -1,6 +1,8 @@
 """The benchmark's reference arm on CPU: `bench.py --impl reference` times the
 CPU restatement of the path on the host cores and prints the same JSON line as
-the GPU arm, with `impl: reference`; ranks other than 0 print nothing."""
+the GPU arm, with `impl: reference`; ranks other than 0 print nothing. Each
+timed step is one whole unit of the workload (one image through all 32 blocks,
+or one full operator call), so ms_per_step is a time that was measured."""
 import json
 import os
 import subprocess
@@ -33,8 +35,21 @@ def test_reference_arm_prints_one_json_line_with_the_contract_keys():
     assert "1008^2" in cb["sample"]
     assert d["e2e"] == {"value": d["value"], "unit": "images/s", "h2d_bytes_per_step": 0,
                         "d2h_bytes_per_step": 0}
-    # 64 images at the measured per-image rate
-    assert abs(d["ms_per_step"] - 64e3 / d["value"]) < 1e-6 * d["ms_per_step"]
+    # one measured image per step
+    assert abs(d["ms_per_step"] - 1e3 / d["value"]) < 1e-6 * d["ms_per_step"]
+    assert "timed whole" in cb["sample"]
+
+
+def test_reference_arm_single_operator_config():
+    r = _run({"WORLD_SIZE": "1", "RANK": "0", "LOCAL_RANK": "0"}, "--config", "c0",
+             "--steps", "2", "--warmup", "1")
+    assert r.returncode == 0, r.stderr
+    d = json.loads([ln for ln in r.stdout.splitlines() if ln.strip()][0])
+    assert d["unit"] == "TFLOP/s" and d["metric"].startswith("c0 palettized QKV projection")
+    gflop = 2 * 5184 * 3072 * 1024 / 1e9
+    assert abs(d["config"]["algorithmic_gflop_per_call"] - gflop) < 1e-6
+    # value is the measured call's FLOP rate
+    assert abs(d["value"] - gflop / d["ms_per_step"]) < 1e-6 * d["value"]
 
 
 def test_reference_arm_other_ranks_exit_quietly():
