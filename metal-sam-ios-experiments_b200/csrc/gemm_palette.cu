@@ -809,23 +809,26 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(WS_THREADS, 1)
 // ============================================================================
 // Chunked weight-stationary pair kernel (K > 1024, K % 128 == 0; fc2 with
 // K = 4096, or 4736 for the checkpoint): the pair's 128-row slab is expanded
-// one 512-wide K chunk at a time (the last one shorter when K % 512 != 0)
-// into two alternating 64 KB shared-memory buffers, so the expansion of chunk
-// c+1 overlaps the MMAs on chunk c. Each expanded chunk feeds a group of two
+// one 384-wide K chunk at a time (the last one shorter when K % 384 != 0)
+// into two alternating 48 KB shared-memory buffers, so the expansion of chunk
+// c+1 overlaps the MMAs on chunk c. 384 rather than 512: the 32 KB this frees
+// holds a third 32 KB stage of X, and with two stages the MMAs waited for X
+// (fc2 782 -> 825 TFLOP/s at M = 82944; 256-wide chunks with four stages ran
+// 752, paying more per-chunk barrier round trips). Each expanded chunk feeds a group of two
 // 256-row M tiles accumulating in their own TMEM buffers (4 x 128 columns:
 // groups alternate between accumulator pairs, so the epilogue of one group,
 // run by the expander warps after chunk 1 of the next, overlaps its MMAs).
 // Each pair keeps one N tile (palette staged once, 32 KB) and the pairs of a
 // "set" sweep the M groups in lockstep.
 // ============================================================================
-constexpr int WSC_KC = 512;
-constexpr int WSC_KB_PER_CHUNK = WSC_KC / WS_BK;                    // 8
-constexpr int WSC_BUF = WSC_KB_PER_CHUNK * WS_SLAB_KB;              // 64 KB
-constexpr int WSC_STAGES = 2;                                      // A stages of WS_KSPLIT k-blocks
+constexpr int WSC_KC = 384;
+constexpr int WSC_KB_PER_CHUNK = WSC_KC / WS_BK;                    // 6
+constexpr int WSC_BUF = WSC_KB_PER_CHUNK * WS_SLAB_KB;              // 48 KB
+constexpr int WSC_STAGES = 3;                                      // A stages of WS_KSPLIT k-blocks
 constexpr int WSC_GROUP = 2;                                        // M tiles per group
 constexpr int WSC_OFF_SLAB = 0;                                     // 2 buffers
-constexpr int WSC_OFF_PAL = 2 * WSC_BUF;                            // 128 KB
-constexpr int WSC_OFF_A = WSC_OFF_PAL + WS_BN * 128 * 4;            // 160 KB
+constexpr int WSC_OFF_PAL = 2 * WSC_BUF;                            // 96 KB
+constexpr int WSC_OFF_A = WSC_OFF_PAL + WS_BN * 128 * 4;            // 128 KB
 constexpr int WSC_OFF_BAR = WSC_OFF_A + WSC_STAGES * WS_A_STAGE;    // 224 KB
 constexpr int WSC_NUM_BARS = 2 * WSC_STAGES + 2 + 2 + 2 + 2 + 2;
 constexpr int WSC_OFF_MISC = WSC_OFF_BAR + WSC_NUM_BARS * 8;
@@ -1313,8 +1316,8 @@ sam3_status_t gemm_palette(sam3_ctx_t* ctx, const uint16_t* x, int m, int k, con
     return launch_ws(ctx, wa.a3d ? ma3 : ma, wa);
   }
   if (k % (WS_KSPLIT * WS_BK) == 0 && n / (2 * WS_BN) <= ctx->num_sms / 2) {
-    // chunked weight-stationary pair kernel (K > 1024; 512-wide chunks, the
-    // last one shorter when K % 512 != 0)
+    // chunked weight-stationary pair kernel (K > 1024; 384-wide chunks, the
+    // last one shorter when K % 384 != 0)
     WscArgs wa;
     wa.g = a;
     wa.idx = idx;
