@@ -453,4 +453,24 @@ __device__ __forceinline__ float gelu_as(float v) {
   return v * (v >= 0.f ? 1.0f - q : q);
 }
 
+// gelu_as on two values at once: the same formula and constants, the
+// polynomial and products in packed fp32x2 FMAs (one instruction per pair).
+__device__ __forceinline__ float2 gelu_as2(float2 v) {
+  const float2 a = make_float2(fabsf(v.x), fabsf(v.y));
+  const float2 den = __ffma2_rn(make_float2(0.3275911f * 0.70710678118654752f,
+                                            0.3275911f * 0.70710678118654752f),
+                                a, make_float2(1.0f, 1.0f));
+  const float2 t = make_float2(rcp_approx(den.x), rcp_approx(den.y));
+  float2 q = __ffma2_rn(make_float2(0.5f * 1.061405429f, 0.5f * 1.061405429f), t,
+                        make_float2(0.5f * -1.453152027f, 0.5f * -1.453152027f));
+  q = __ffma2_rn(q, t, make_float2(0.5f * 1.421413741f, 0.5f * 1.421413741f));
+  q = __ffma2_rn(q, t, make_float2(0.5f * -0.284496736f, 0.5f * -0.284496736f));
+  q = __ffma2_rn(q, t, make_float2(0.5f * 0.254829592f, 0.5f * 0.254829592f));
+  const float2 vv = __fmul2_rn(__fmul2_rn(v, v),
+                               make_float2(-0.5f * 1.4426950408889634f,
+                                           -0.5f * 1.4426950408889634f));
+  q = __fmul2_rn(__fmul2_rn(q, t), make_float2(ex2_approx(vv.x), ex2_approx(vv.y)));
+  return __fmul2_rn(v, make_float2(v.x >= 0.f ? 1.0f - q.x : q.x, v.y >= 0.f ? 1.0f - q.y : q.y));
+}
+
 }  // namespace sam3

@@ -73,13 +73,14 @@ struct GemmArgs {
 };
 
 
+// f[0..7] += the 8 fp16 values of v (packed fp32x2 adds).
 __device__ __forceinline__ void add_half8(float* f, uint4 v) {
   const uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
   for (int q = 0; q < 4; ++q) {
-    const float2 p = unpack_half2(w[q]);
-    f[2 * q] += p.x;
-    f[2 * q + 1] += p.y;
+    const float2 s = __fadd2_rn(make_float2(f[2 * q], f[2 * q + 1]), unpack_half2(w[q]));
+    f[2 * q] = s.x;
+    f[2 * q + 1] = s.y;
   }
 }
 
@@ -124,7 +125,11 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs& a, int row, int c
   }
   if (a.epi == SAM3_EPI_BIAS_GELU) {
 #pragma unroll
-    for (int j = 0; j < 32; ++j) f[j] = gelu_as(f[j]);
+    for (int j = 0; j < 32; j += 2) {
+      const float2 g = gelu_as2(make_float2(f[j], f[j + 1]));
+      f[j] = g.x;
+      f[j + 1] = g.y;
+    }
   } else if (a.epi == SAM3_EPI_BIAS_ROPE_QKV && col0 < a.qk_cols) {
     // 32 columns = 16 interleaved (even, odd) pairs of one 64-wide head;
     // a full table row holds 32 (cos, sin) pairs, pair j at float offset 2j;
