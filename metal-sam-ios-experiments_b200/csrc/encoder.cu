@@ -33,7 +33,8 @@ sam3_status_t check_block_weights(sam3_ctx_t* ctx, const sam3_block_weights_t* w
 }
 
 // rope_pos null: rope is a table of rope_rows full rows (row r % rope_rows);
-// otherwise the axial table with per-row coordinates (gemm_palette).
+// otherwise the pair-major axial table of rope_rows coordinates with per-row
+// coordinates (gemm_palette).
 sam3_status_t attention_block(sam3_ctx_t* ctx, uint16_t* x, int batch, int seq,
                               const sam3_block_weights_t* w, const float* rope, int rope_rows,
                               const int32_t* rope_pos = nullptr) {
@@ -111,7 +112,7 @@ sam3_status_t encoder_run(sam3_ctx_t* ctx, const void* image, bool rgba, int bat
       rope_pos = ctx->rope_pos_pruned;
     }
     if (blk == c.num_blocks) break;
-    if ((st = attention_block(ctx, cur, batch, rows, &w->blocks[blk], ctx->rope_axial, 0,
+    if ((st = attention_block(ctx, cur, batch, rows, &w->blocks[blk], ctx->rope_axial, grid,
                               rope_pos)) != SAM3_OK)
       return st;
     if ((st = mlp_block(ctx, cur, batch * rows, &w->blocks[blk])) != SAM3_OK) return st;

@@ -54,8 +54,9 @@ struct GemmArgs {
   const __half* bias;
   const __half* residual;
   const float* rope;
-  // Axial RoPE: when set, rope points at A[c][16] (cos, sin) pairs with
-  // A[c][i] = rotation of pair i at coordinate c, and row r of the output
+  // Axial RoPE: when set, rope points at the axial table of rope_rows
+  // coordinates, pair-major: float4 element q * rope_rows + c holds the
+  // (cos, sin) of pairs 2q and 2q+1 at coordinate c; row r of the output
   // takes its coordinates from rope_pos[r] = x | y << 16 (pairs 0-15 of a head
   // rotate by x, pairs 16-31 by y; -1: no rotation). Otherwise rope is a
   // table of rope_rows full rows (32 pairs) indexed by r % rope_rows.
@@ -134,19 +135,24 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs& a, int row, int c
     // 32 columns = 16 interleaved (even, odd) pairs of one 64-wide head;
     // a full table row holds 32 (cos, sin) pairs, pair j at float offset 2j;
     // the axial table holds the 16 pairs of one coordinate (x for the first
-    // 32 columns of the head, y for the last 32).
+    // 32 columns of the head, y for the last 32), pair-major: the float4 of
+    // pairs (2q, 2q+1) at coordinate c is element q * rope_rows + c, so the
+    // 32 lanes of a warp (32 consecutive tokens, consecutive x) read
+    // consecutive 16-byte entries instead of 32 different cache lines.
     const float4* t;
+    int tstride = 1;
     bool rotate = true;
     if (a.rope_pos) {
       rotate = rpos >= 0;
       const int c = (col0 & 32) ? (rpos >> 16) : (rpos & 0xFFFF);
-      t = reinterpret_cast<const float4*>(a.rope + (size_t)(rotate ? c : 0) * 32);
+      t = reinterpret_cast<const float4*>(a.rope) + (rotate ? c : 0);
+      tstride = a.rope_rows;
     } else {
       t = reinterpret_cast<const float4*>(a.rope + (size_t)(row % a.rope_rows) * 64 + (col0 & 63));
     }
 #pragma unroll
     for (int q = 0; q < 8 && rotate; ++q) {
-      const float4 cs = __ldg(t + q);
+      const float4 cs = __ldg(t + q * tstride);
       float x0 = f[4 * q], x1 = f[4 * q + 1];
       f[4 * q] = x0 * cs.x - x1 * cs.y;
       f[4 * q + 1] = x0 * cs.y + x1 * cs.x;

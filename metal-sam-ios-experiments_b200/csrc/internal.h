@@ -38,9 +38,10 @@ struct sam3_ctx {
   float* scores = nullptr;      // [B*S]
   float* rope = nullptr;        // [S, 32, 2]
   float* rope_pruned = nullptr; // [B*keep, 32, 2]
-  // Axial form of the grid table for the QKV GEMM epilogue: rope_axial[c][i]
-  // = pair i (0..15) at coordinate c, and per row the coordinates x | y << 16.
-  float* rope_axial = nullptr;        // [grid, 16, 2]
+  // Axial form of the grid table for the QKV GEMM epilogue, pair-major:
+  // float4 [q][c] = pairs 2q, 2q+1 at coordinate c (q < 8, c < grid); per row
+  // the coordinates x | y << 16.
+  float* rope_axial = nullptr;        // [8, grid, 4]
   int32_t* rope_pos_grid = nullptr;   // [B*S] grid order
   int32_t* rope_pos_win = nullptr;    // [B*(S+1)] window-major, -1 for the class token
   int32_t* rope_pos_pruned = nullptr; // [B*keep] the kept tokens

@@ -113,13 +113,18 @@ __global__ void rope_table_kernel(float* __restrict__ t, int gh, int gw, int hd,
   row[quarter + i] = make_float2(cosf(ay), sinf(ay));
 }
 
-// Axial form of the table: a[c][i] = pair i (i < 16) at coordinate c. The
-// row-index half of the table uses the same frequencies and formula as the
-// column-index half, so row c (h = 0, w = c) gives coordinate c for both
-// halves bit for bit; rows h*gw (w = 0) cover c >= gw on taller grids.
-__global__ void rope_axial_kernel(const float2* __restrict__ t, int gw, float2* __restrict__ a) {
+// Axial form of the table, pair-major: pair i (i < 16) at coordinate c is
+// float2 element ((i / 2) * coords + c) * 2 + i % 2, i.e. the float4 of pairs
+// (2q, 2q+1) of all coordinates are contiguous (consecutive tokens of a warp
+// read consecutive entries in the QKV epilogue). The row-index half of the
+// table uses the same frequencies and formula as the column-index half, so
+// row c (h = 0, w = c) gives coordinate c for both halves bit for bit; rows
+// h*gw (w = 0) cover c >= gw on taller grids.
+__global__ void rope_axial_kernel(const float2* __restrict__ t, int gw, int coords,
+                                  float2* __restrict__ a) {
   const int c = blockIdx.x, i = threadIdx.x;
-  a[c * 16 + i] = c < gw ? t[(size_t)c * 32 + i] : t[(size_t)c * gw * 32 + 16 + i];
+  a[((i >> 1) * coords + c) * 2 + (i & 1)] =
+      c < gw ? t[(size_t)c * 32 + i] : t[(size_t)c * gw * 32 + 16 + i];
 }
 
 // pos[r] = coordinates of grid token r % per, x | y << 16.
@@ -451,7 +456,8 @@ sam3_status_t rope_setup(sam3_ctx_t* ctx) {
   if (hd == 64) {  // the axial form serves the QKV epilogue (head_dim 64)
     ProfScope prof(ctx, SAM3_PROF_OTHER, 0.0, 2.0 * grid * 16 * 8);
     rope_axial_kernel<<<grid, 16, 0, ctx->stream>>>(reinterpret_cast<const float2*>(ctx->rope),
-                                                     grid, reinterpret_cast<float2*>(ctx->rope_axial));
+                                                     grid, grid,
+                                                     reinterpret_cast<float2*>(ctx->rope_axial));
     if ((st = check_launch(ctx, "rope_axial_kernel")) != SAM3_OK) return st;
     const int rows = std::max(1, c.max_batch) * S;
     rope_pos_grid_kernel<<<blocks_for(rows, 256), 256, 0, ctx->stream>>>(ctx->rope_pos_grid, rows,

@@ -174,7 +174,7 @@ sam3_status_t windowed_encoder_run(sam3_ctx_t* ctx, const void* image, bool rgba
     if ((st = layernorm(ctx, x, rows, D, bw->ln1_gamma, bw->ln1_beta, c.ln_eps, ctx->ln)) != SAM3_OK)
       return st;
     if ((st = gemm_palette(ctx, ctx->ln, rows, D, bw->qkv.idx, bw->qkv.palette, bw->qkv.bias,
-                           3 * D, SAM3_EPI_BIAS_ROPE_QKV, nullptr, ctx->rope_axial, 0,
+                           3 * D, SAM3_EPI_BIAS_ROPE_QKV, nullptr, ctx->rope_axial, grid,
                            ctx->qkv, ctx->rope_pos_win)) != SAM3_OK)
       return st;
     if (global) {
