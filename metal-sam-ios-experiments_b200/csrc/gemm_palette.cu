@@ -828,7 +828,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(WS_THREADS, 1)
 // 752, paying more per-chunk barrier round trips). Each expanded chunk feeds a group of two
 // 256-row M tiles accumulating in their own TMEM buffers (4 x 128 columns:
 // groups alternate between accumulator pairs, so the epilogue of one group,
-// run by the expander warps after chunk 1 of the next, overlaps its MMAs).
+// run by four epilogue warps of its own, overlaps the next group's MMAs).
 // Each pair keeps one N tile (palette staged once, 32 KB) and the pairs of a
 // "set" sweep the M groups in lockstep.
 // ============================================================================
@@ -845,6 +845,12 @@ constexpr int WSC_NUM_BARS = 2 * WSC_STAGES + 2 + 2 + 2 + 2 + 2;
 constexpr int WSC_OFF_MISC = WSC_OFF_BAR + WSC_NUM_BARS * 8;
 constexpr int WSC_SMEM_BYTES = WSC_OFF_MISC + 16 + 1024;
 static_assert(WSC_SMEM_BYTES <= 232448, "shared memory budget");
+// Warps 0 (producer), 1 (MMA issuer), 2-9 (slab expanders) and 10-13, four
+// epilogue warps of their own (one per TMEM lane quadrant, all 128 columns of
+// a row each): with the epilogue on the expander warps, the MMA issuer waited
+// for expanded chunks 24 % of its time (clock64 accounting at M = 82944).
+constexpr int WSC_THREADS = 448;
+constexpr int WSC_NUM_EPI_WARPS = 4;
 
 struct WscArgs {
   GemmArgs g;
@@ -858,7 +864,7 @@ struct WscArgs {
   int a3d;      // as WsArgs::a3d
 };
 
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(WS_THREADS, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(WSC_THREADS, 1)
     gemm_wsc_kernel(const __grid_constant__ CUtensorMap tmap_a, const WscArgs wa) {
   const GemmArgs& args = wa.g;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -888,7 +894,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(WS_THREADS, 1)
       mbar_init(bar_slab_full + 8 * b, 2 * WS_NUM_EXP);
       mbar_init(bar_slab_empty + 8 * b, 1);
       mbar_init(bar_tfull + 8 * b, 1);
-      mbar_init(bar_tempty + 8 * b, 2 * WS_NUM_EXP / 32);  // one arrive per epilogue warp
+      mbar_init(bar_tempty + 8 * b, 2 * WSC_NUM_EPI_WARPS);  // one arrive per epilogue warp
     }
     mbar_init(bar_pal, WS_NUM_EXP);
     mbar_init(bar_drain, 1);
@@ -1011,61 +1017,62 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(WS_THREADS, 1)
         mbar_wait_cluster_drain(bar_drain, 0);
       }
     }
-  } else {
-    // ------------------------------------------------------------- expanders + epilogue
-    const int ew = warp - 2;
-    const int exp_row = lane + 32 * (ew & 1);
-    const int exp_q = ew >> 1;
+  } else if (warp >= 2 + WS_NUM_EXP / 32) {
+    // ------------------------------------------------------------- epilogue warps
+    // Warp w handles TMEM lane quadrant w % 4 (rows quad*32 + lane of the CTA's
+    // 128) and all 128 columns, group after group, in the issuer's order.
     const int quad = warp & 3;
-    const int colhalf = ew >> 2;
-    uint32_t* pal = reinterpret_cast<uint32_t*>(smem + WSC_OFF_PAL) + exp_row;
-    uint32_t pal_ph = 0;
-    int cur_n = -1, it = 0, q = 0;
-    int pend_it = -1, pend_g = -1;  // group whose epilogue is still to do
-    bool ok = true, dep_waited = false;
-    // Epilogue of a group: per M tile, its 64 columns of this row go from
-    // tensor memory to registers (the accumulator pair is handed back to the
-    // MMA issuer as soon as the last tile's values are out), then the math
-    // and the stores.
-    auto epilogue = [&](int e_it, int g) -> bool {
-      const int gp = e_it & 1;
-      const int col0 = my_n * 2 * WS_BN + colhalf * 64;
+    int it = 0;
+    bool ok = true;
+    griddep_wait();  // the residual is the previous kernel's output
+    for (int g = my_set; g < wa.groups && ok; g += wa.sets, ++it) {
+      const int gp = it & 1;
       const int row0 = g * WSC_GROUP * 2 * WS_BM + (int)rank * WS_BM + quad * 32 + lane;
-      if (!dep_waited) {  // the slab chunks are weights only; the residual is not
-        griddep_wait();
-        dep_waited = true;
-      }
-      static_assert(WSC_GROUP == 2, "two M tiles per group");
 #pragma unroll
-      for (int t = 0; t < WSC_GROUP; ++t) epilogue_prefetch(args, row0 + t * 2 * WS_BM, col0);
+      for (int t = 0; t < WSC_GROUP; ++t)
+#pragma unroll
+        for (int ch = 0; ch < 2; ++ch)
+          epilogue_prefetch(args, row0 + t * 2 * WS_BM, my_n * 2 * WS_BN + ch * 64);
       const int rpos0 = rope_pos_of(args, row0), rpos1 = rope_pos_of(args, row0 + 2 * WS_BM);
-      const bool w = __all_sync(0xffffffffu,
-                                mbar_wait_cluster(bar_tfull + 8 * gp, (uint32_t)(e_it >> 1) & 1u,
-                                                  abort_flag, args.err, kDevErrTimeoutEpilogue));
-      if (!w) return false;
+      ok = __all_sync(0xffffffffu,
+                      mbar_wait_cluster(bar_tfull + 8 * gp, (uint32_t)(it >> 1) & 1u, abort_flag,
+                                        args.err, kDevErrTimeoutEpilogue));
+      if (!ok) break;
       tc_fence_after();
 #pragma unroll 1
       for (int t = 0; t < WSC_GROUP; ++t) {
         const int row = row0 + t * 2 * WS_BM;
-        const uint32_t taddr = tmem + ((uint32_t)(quad * 32) << 16) +
-                               (uint32_t)((2 * gp + t) * WS_ACC_COLS + colhalf * 64);
-        uint32_t v[64];
-        tmem_ld_32x32b_x32(taddr, *reinterpret_cast<uint32_t(*)[32]>(v));
-        tmem_ld_32x32b_x32(taddr + 32u, *reinterpret_cast<uint32_t(*)[32]>(v + 32));
-        tmem_wait_ld();
-        if (t == WSC_GROUP - 1) {
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive_cluster(mapa_shared(bar_tempty + 8 * gp, 0));
-        }
         const int rpos = t == 0 ? rpos0 : rpos1;
-        epilogue_chunk(args, row, col0, *reinterpret_cast<const uint32_t(*)[32]>(v), rpos);
-        epilogue_chunk(args, row, col0 + 32, *reinterpret_cast<const uint32_t(*)[32]>(v + 32),
-                       rpos);
+#pragma unroll 1
+        for (int ch = 0; ch < 2; ++ch) {
+          const int col0 = my_n * 2 * WS_BN + ch * 64;
+          const uint32_t taddr = tmem + ((uint32_t)(quad * 32) << 16) +
+                                 (uint32_t)((2 * gp + t) * WS_ACC_COLS + ch * 64);
+          uint32_t v[64];
+          tmem_ld_32x32b_x32(taddr, *reinterpret_cast<uint32_t(*)[32]>(v));
+          tmem_ld_32x32b_x32(taddr + 32u, *reinterpret_cast<uint32_t(*)[32]>(v + 32));
+          tmem_wait_ld();
+          if (t == WSC_GROUP - 1 && ch == 1) {  // the accumulator pair is free again
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(mapa_shared(bar_tempty + 8 * gp, 0));
+          }
+          epilogue_chunk(args, row, col0, *reinterpret_cast<const uint32_t(*)[32]>(v), rpos);
+          epilogue_chunk(args, row, col0 + 32, *reinterpret_cast<const uint32_t(*)[32]>(v + 32),
+                         rpos);
+        }
       }
-      return true;
-    };
-    for (int g = my_set; g < wa.groups && ok; g += wa.sets, ++it) {
+    }
+  } else {
+    // ------------------------------------------------------------- slab expanders
+    const int ew = warp - 2;
+    const int exp_row = lane + 32 * (ew & 1);
+    const int exp_q = ew >> 1;
+    uint32_t* pal = reinterpret_cast<uint32_t*>(smem + WSC_OFF_PAL) + exp_row;
+    uint32_t pal_ph = 0;
+    int cur_n = -1, q = 0;
+    bool ok = true;
+    for (int g = my_set; g < wa.groups && ok; g += wa.sets) {
       const int n_tile = my_n;
       const int wrow = n_tile * 2 * WS_BN + (int)rank * WS_BN + exp_row;
       if (n_tile != cur_n) {
@@ -1116,18 +1123,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(WS_THREADS, 1)
         }
         fence_proxy_async_smem();
         mbar_arrive_cluster(mapa_shared(bar_slab_full + 8 * b, 0));
-        // The previous group's epilogue, once chunks 0 and 1 are expanded:
-        // the MMAs on them cover it and the next chunk's expansion.
-        if (c == 1 && pend_it >= 0) {
-          ok = epilogue(pend_it, pend_g);
-          pend_it = -1;
-        }
       }
-      if (ok && pend_it >= 0) ok = epilogue(pend_it, pend_g);  // a one-chunk group
-      pend_it = it;
-      pend_g = g;
     }
-    if (ok && pend_it >= 0) epilogue(pend_it, pend_g);
   }
 
   tc_fence_before();
@@ -1225,7 +1222,7 @@ sam3_status_t launch_wsc(sam3_ctx_t* ctx, const CUtensorMap& ma, const WscArgs& 
                                       "gemm_wsc smem attribute");
   if (st != SAM3_OK) return st;
   const int pairs = wa.sets * wa.n_tiles;
-  return check_launch_ret(ctx, launch_pdl(gemm_wsc_kernel, dim3(2 * pairs), dim3(WS_THREADS),
+  return check_launch_ret(ctx, launch_pdl(gemm_wsc_kernel, dim3(2 * pairs), dim3(WSC_THREADS),
                                          WSC_SMEM_BYTES, ctx->stream, ma, wa),
                           "gemm_wsc_kernel");
 }
