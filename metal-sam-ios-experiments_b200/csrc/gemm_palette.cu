@@ -501,14 +501,11 @@ static_assert(WS_BN * 128 * 4 <= WS_STAGES * WS_A_STAGE, "palette staging fits t
 // `lop3` build the two half-word selectors (bit 7 of an index picks the
 // high half of its word).
 template <int N16>
-__device__ __forceinline__ void ws_expand_range(const uint8_t* irow, const uint32_t* pal,
-                                                uint8_t* buf, int exp_row, int k0, int kbase) {
+__device__ __forceinline__ void ws_expand_loaded(const uint4 (&iv)[N16], const uint32_t* pal,
+                                                 uint8_t* buf, int exp_row, int k0, int kbase) {
   const int sw = exp_row & 7;
   const uint8_t* palb = reinterpret_cast<const uint8_t*>(pal - exp_row);
   const uint32_t rowoff = (uint32_t)exp_row * 4u;  // < 256: byte 0 only
-  uint4 iv[N16];
-#pragma unroll
-  for (int i = 0; i < N16; ++i) iv[i] = __ldg(reinterpret_cast<const uint4*>(irow + k0) + i);
 #pragma unroll
   for (int i = 0; i < N16; ++i) {
     const int k = k0 + 16 * i;
@@ -534,6 +531,18 @@ __device__ __forceinline__ void ws_expand_range(const uint8_t* irow, const uint3
     *reinterpret_cast<uint4*>(dst + ((c ^ sw) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
     *reinterpret_cast<uint4*>(dst + (((c + 1) ^ sw) << 4)) = make_uint4(o[4], o[5], o[6], o[7]);
   }
+}
+template <int N16>
+__device__ __forceinline__ void ws_load_idx(const uint8_t* irow, int k0, uint4 (&iv)[N16]) {
+#pragma unroll
+  for (int i = 0; i < N16; ++i) iv[i] = __ldg(reinterpret_cast<const uint4*>(irow + k0) + i);
+}
+template <int N16>
+__device__ __forceinline__ void ws_expand_range(const uint8_t* irow, const uint32_t* pal,
+                                                uint8_t* buf, int exp_row, int k0, int kbase) {
+  uint4 iv[N16];
+  ws_load_idx<N16>(irow, k0, iv);
+  ws_expand_loaded<N16>(iv, pal, buf, exp_row, k0, kbase);
 }
 
 struct WsArgs {
@@ -1103,8 +1112,23 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(WSC_THREADS, 1)
         cur_n = n_tile;
       }
       const uint8_t* irow = wa.idx + (size_t)wrow * args.k;
+      constexpr int N16 = WSC_KC / 4 / 16;
+      auto full = [&](int c) { return (c + 1) * WSC_KB_PER_CHUNK <= wa.kblocks; };
+      // Software pipeline: the indices of the next full chunk are loaded into
+      // registers before the wait for this chunk's buffer, so their L2 round
+      // trip overlaps that wait and this chunk's expansion.
+      uint4 iv_next[N16];
+      if (full(0)) ws_load_idx<N16>(irow, exp_q * (WSC_KC / 4), iv_next);
       for (int c = 0; c < chunks && ok; ++c, ++q) {
         const int b = q & 1;
+        uint4 iv[N16];
+#pragma unroll
+        for (int i = 0; i < N16; ++i) iv[i] = iv_next[i];
+        // the next chunk: c + 1 of this group, or chunk 0 of the pair's next
+        // group (same weight rows)
+        const int cn = c + 1 < chunks ? c + 1 : (g + wa.sets < wa.groups ? 0 : -1);
+        if (cn >= 0 && full(cn))
+          ws_load_idx<N16>(irow, cn * WSC_KC + exp_q * (WSC_KC / 4), iv_next);
         if (q >= 2) {
           ok = __all_sync(0xffffffffu,
                           mbar_wait_cluster(bar_slab_empty + 8 * b, (uint32_t)((q >> 1) - 1) & 1u,
@@ -1113,8 +1137,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(WSC_THREADS, 1)
         }
         const int kb_c = min(WSC_KB_PER_CHUNK, wa.kblocks - c * WSC_KB_PER_CHUNK);
         if (kb_c == WSC_KB_PER_CHUNK) {
-          ws_expand_range<WSC_KC / 4 / 16>(irow, pal, smem + WSC_OFF_SLAB + b * WSC_BUF, exp_row,
-                                           c * WSC_KC + exp_q * (WSC_KC / 4), c * WSC_KC);
+          ws_expand_loaded<N16>(iv, pal, smem + WSC_OFF_SLAB + b * WSC_BUF, exp_row,
+                                c * WSC_KC + exp_q * (WSC_KC / 4), c * WSC_KC);
         } else {  // short last chunk: kb_c * 16 indices per quarter, 32 at a time
           const int k0 = c * WSC_KC + exp_q * kb_c * 16;
           for (int k = k0; k < k0 + kb_c * 16; k += 32)
