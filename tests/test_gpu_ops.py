@@ -348,13 +348,14 @@ def test_attention_batch8_repeated_is_batch_invariant(ctx_full, sam3, oracle):
         assert np.array_equal(single, outs[0][b * seq:(b + 1) * seq])
 
 
-@pytest.mark.parametrize("seq", [700, 5184])
-def test_attention_growing_scores_rescale_path(ctx, sam3, oracle, seq):
+@pytest.mark.parametrize("seq,batch,heads", [(700, 2, 2), (5184, 2, 2), (2592, 1, 16)])
+def test_attention_growing_scores_rescale_path(ctx_full, sam3, oracle, seq, batch, heads):
     # Keys whose scores climb along the sequence (up to ~90 in log2 units), so
     # the running row max grows past the lazy-rescale threshold many times;
     # query rows scaled from -1 to 1 mix rows that rescale often, rarely and
-    # never. Three repeats must be bit-identical and match the oracle.
-    heads, batch = 2, 2
+    # never. Three repeats must be bit-identical and match the oracle: two
+    # images of 2 heads, and one image of 16 heads after the prune's size.
+    ctx = ctx_full
     rng = np.random.default_rng(21)
     d = heads * 64
     qkv = np.empty((batch * seq, 3 * d), np.float32)
