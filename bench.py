@@ -28,11 +28,13 @@ N > 1 is launched by torch.distributed.run (one rank per GPU). Rank 0 prints
 one JSON line:
   value   images/s of the whole job, device-timed (CUDA events on the library's
           stream, inputs resident in HBM), max over ranks;
-  e2e     the same through the host-buffer C-ABI entry point
-          (sam3_encoder_forward_host_pipelined over all of the rank's images:
-          pinned host images in, pruned features and indices out, every copy
-          inside the timed region, overlapped with the encoder of the
-          neighbouring call);
+  e2e     the same through the host-buffer C-ABI entry points
+          (sam3_encoder_submit_host / sam3_encoder_wait_host, every step all
+          of the rank's images: pinned host images in, pruned features and
+          indices out, every copy inside the timed region, on upload and
+          download streams that overlap the encoder of the neighbouring
+          call or step); e2e.blocking_call_value times one blocking
+          sam3_encoder_forward_host_pipelined call per step instead;
   roofline  the palette-dequant GEMM (dominant kernel): algorithmic FLOPs
           (2*M*N*K) / its summed CUDA-event launch time, measured in a second
           pass over the same steps with events around every launch (kept out
@@ -466,32 +468,55 @@ def run_ours(args):
     prof_ms = p0.elapsed_time(p1)
     barrier()
 
-    # ---- end to end through the host-buffer entry point
+    # ---- end to end through the host-buffer entry points
     h_imgs = torch.empty(imgs.shape, dtype=torch.float16, pin_memory=True)
     h_imgs.copy_(imgs)
-    h_feats = torch.empty(feats.shape, dtype=torch.float16, pin_memory=True)
-    h_idx = torch.empty(idx.shape, dtype=torch.int32, pin_memory=True)
+    h_out = [(torch.empty(feats.shape, dtype=torch.float16, pin_memory=True),
+              torch.empty(idx.shape, dtype=torch.int32, pin_memory=True)) for _ in range(2)]
 
-    def step_e2e():
-        # every image of this rank through the pipelined host entry point:
-        # uploads of the next call and downloads of the previous one overlap
-        # the encoder
-        ctx.encoder_forward_host_pipelined(h_imgs.data_ptr(), per_rank, w, h_feats.data_ptr(),
-                                           h_idx.data_ptr())
+    def run_e2e(steps):
+        # A frame loop: every step submits all of this rank's images (pinned
+        # host images in, features and indices out) and the host waits for
+        # the step two back before reusing its output buffers. Uploads of
+        # step s+1 and downloads of step s run on their own streams under
+        # the encoder of step s / s+1.
+        tickets = []
+        for s in range(steps):
+            if s >= 2:
+                ctx.encoder_wait_host(tickets[s - 2])
+            hf, hi = h_out[s & 1]
+            tickets.append(ctx.encoder_submit_host(h_imgs.data_ptr(), per_rank, w,
+                                                   hf.data_ptr(), hi.data_ptr()))
+        ctx.encoder_wait_host(tickets[-1])
 
-    step_e2e()
-    barrier()
-    e0 = torch.cuda.Event(enable_timing=True)
-    e1 = torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(args.steps):
-        step_e2e()
-    e1.record(stream)
-    e1.synchronize()
-    e2e_ms = max_over_ranks(e0.elapsed_time(e1))
-    barrier()
-    # the host-path result must equal the device-path result
-    same = bool(torch.equal(h_idx.to(dev), idx)) and bool(torch.equal(h_feats.to(dev), feats))
+    def run_blocking(steps):
+        # each step one blocking call: the first upload and the last download
+        # of every step are exposed
+        hf, hi = h_out[0]
+        for _ in range(steps):
+            ctx.encoder_forward_host_pipelined(h_imgs.data_ptr(), per_rank, w, hf.data_ptr(),
+                                               hi.data_ptr())
+
+    def timed(fn):
+        fn(2)
+        barrier()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        fn(args.steps)
+        e1.record(stream)
+        e1.synchronize()
+        ms_ = max_over_ranks(e0.elapsed_time(e1))
+        barrier()
+        return ms_
+
+    e2e_ms = timed(run_e2e)
+    # the host-path results must equal the device-path result
+    same = all(bool(torch.equal(hi.to(dev), idx)) and bool(torch.equal(hf.to(dev), feats))
+               for hf, hi in h_out)
+    blocking_ms = timed(run_blocking)
+    same = same and bool(torch.equal(h_out[0][1].to(dev), idx)) and \
+        bool(torch.equal(h_out[0][0].to(dev), feats))
 
     peaks = load_peaks()
     g = prof["gemm"]
@@ -515,6 +540,11 @@ def run_ours(args):
             "e2e": {"value": args.images * args.steps / (e2e_ms * 1e-3), "unit": UNIT,
                     "h2d_bytes_per_step": args.images * IMAGE * IMAGE * 3 * 2,
                     "d2h_bytes_per_step": args.images * keep * (DIM * 2 + 4),
+                    "api": "sam3_encoder_submit_host / sam3_encoder_wait_host, each step "
+                           "submitted while the one before runs",
+                    "blocking_call_value": args.images * args.steps / (blocking_ms * 1e-3),
+                    "blocking_call_api": "sam3_encoder_forward_host_pipelined, one blocking "
+                                         "call per step",
                     "matches_device_path": same},
             "roofline": {
                 "kernel": "gemm_ws_kernel + gemm_wsc_kernel (palette-dequant tcgen05 pair GEMMs: "

@@ -366,6 +366,29 @@ sam3_status_t sam3_encoder_forward_host_pipelined(sam3_ctx_t* ctx, const uint16_
                                                   const sam3_encoder_weights_t* w,
                                                   uint16_t* host_feats, int32_t* host_idx);
 
+/* The same work without the wait: enqueues the uploads, the encoder and the
+ * downloads of n_images and returns at once with a ticket (1, 2, ... per
+ * context). Uploads and downloads run on their own streams, so a later
+ * submission's uploads overlap this one's encoder and this one's downloads
+ * overlap the next encoder: a stream of frames keeps the GPU busy across
+ * calls. The host buffers must stay valid, and host_feats/host_idx unread,
+ * until sam3_encoder_wait_host(ticket) returns SAM3_OK. Keep the context's
+ * stream unchanged while submissions are in flight. Reference: the encoder
+ * recorded into a command buffer and committed, SAM3MetalPipeline.swift:72-77
+ * (ViTEncoder.forward(image:commandBuffer:) + commandBuffer.commit()). */
+sam3_status_t sam3_encoder_submit_host(sam3_ctx_t* ctx, const uint16_t* host_image,
+                                       int32_t n_images, const sam3_encoder_weights_t* w,
+                                       uint16_t* host_feats, int32_t* host_idx,
+                                       uint64_t* ticket);
+
+/* Blocks until the downloads of submission `ticket` (and of every earlier
+ * one) are on the host. SAM3_ERR_INVALID_ARG for a ticket not issued;
+ * SAM3_ERR_TIMEOUT / SAM3_ERR_INVALID_ARG when the device error word was set
+ * by the time that submission's encoder ended (the word stays set until
+ * sam3_sync reads and clears it). Reference: commandBuffer.waitUntilCompleted(),
+ * SAM3MetalPipeline.swift:79. */
+sam3_status_t sam3_encoder_wait_host(sam3_ctx_t* ctx, uint64_t ticket);
+
 /* Pruned rows back to their grid positions: out [batch, seq, dim] fp16 is
  * zero except out[b, idx[b, k], :] = pruned[b, k, :] (idx int32 [batch, keep],
  * unique per image, as sam3_prune writes them). An index outside [0, seq) is

@@ -217,6 +217,14 @@ sam3_status_t ensure_workspace(sam3_ctx_t* ctx) {
   return SAM3_OK;
 }
 
+sam3_status_t device_error_status(sam3_ctx_t* ctx, int err) {
+  if (!err) return SAM3_OK;
+  if ((err & 0xF00) == 0x200)  // a kernel met an invalid index in its input and skipped it
+    return set_error(ctx, SAM3_ERR_INVALID_ARG, "index out of range in a kernel input (code 0x%x)",
+                     err);
+  return set_error(ctx, SAM3_ERR_TIMEOUT, "kernel bounded wait expired (code 0x%x)", err);
+}
+
 }  // namespace sam3
 
 using namespace sam3;
@@ -326,10 +334,15 @@ sam3_status_t sam3_ctx_destroy(sam3_ctx_t* ctx) {
   resolve_profile(ctx);
   for (cudaEvent_t e : ctx->event_pool) cudaEventDestroy(e);
   if (ctx->copy_stream) cudaStreamSynchronize(ctx->copy_stream);
+  if (ctx->down_stream) cudaStreamSynchronize(ctx->down_stream);
   for (cudaEvent_t e : ctx->pipe_ev)
     if (e) cudaEventDestroy(e);
+  for (cudaEvent_t e : ctx->pipe_done)
+    if (e) cudaEventDestroy(e);
+  if (ctx->pipe_err) cudaFreeHost(ctx->pipe_err);
   if (ctx->pipe_mem) cudaFree(ctx->pipe_mem);
   if (ctx->copy_stream) cudaStreamDestroy(ctx->copy_stream);
+  if (ctx->down_stream) cudaStreamDestroy(ctx->down_stream);
   if (ctx->ws) cudaFree(ctx->ws);
   if (ctx->dev_err) cudaFree(ctx->dev_err);
   if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);
@@ -360,14 +373,8 @@ sam3_status_t sam3_sync(sam3_ctx_t* ctx) {
   st = check_cuda(ctx, cudaMemcpy(&err, ctx->dev_err, sizeof(int), cudaMemcpyDeviceToHost),
                   "read device error word");
   if (st != SAM3_OK) return st;
-  if (err) {
-    cudaMemset(ctx->dev_err, 0, sizeof(int));
-    if ((err & 0xF00) == 0x200)  // a kernel met an invalid index in its input and skipped it
-      return set_error(ctx, SAM3_ERR_INVALID_ARG, "index out of range in a kernel input (code 0x%x)",
-                       err);
-    return set_error(ctx, SAM3_ERR_TIMEOUT, "kernel bounded wait expired (code 0x%x)", err);
-  }
-  return SAM3_OK;
+  if (err) cudaMemset(ctx->dev_err, 0, sizeof(int));
+  return sam3::device_error_status(ctx, err);
 }
 
 sam3_status_t sam3_profile_enable(sam3_ctx_t* ctx, int32_t enable) {

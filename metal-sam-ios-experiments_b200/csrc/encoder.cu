@@ -239,15 +239,15 @@ sam3_status_t sam3_encoder_forward_host(sam3_ctx_t* ctx, const uint16_t* host_im
   return sam3_sync(ctx);
 }
 
-sam3_status_t sam3_encoder_forward_host_pipelined(sam3_ctx_t* ctx, const uint16_t* host_image,
-                                                  int32_t n_images,
-                                                  const sam3_encoder_weights_t* w,
-                                                  uint16_t* host_feats, int32_t* host_idx) {
+sam3_status_t sam3_encoder_submit_host(sam3_ctx_t* ctx, const uint16_t* host_image,
+                                       int32_t n_images, const sam3_encoder_weights_t* w,
+                                       uint16_t* host_feats, int32_t* host_idx,
+                                       uint64_t* ticket) {
   SAM3_CHECK_CTX(ctx);
-  if (!host_image || !host_feats || !host_idx)
-    return set_error(ctx, SAM3_ERR_INVALID_ARG, "encoder_host_pipelined: null pointer");
+  if (!host_image || !host_feats || !host_idx || !ticket)
+    return set_error(ctx, SAM3_ERR_INVALID_ARG, "encoder_submit_host: null pointer");
   if (n_images <= 0)
-    return set_error(ctx, SAM3_ERR_SHAPE, "encoder_host_pipelined: n_images %d", n_images);
+    return set_error(ctx, SAM3_ERR_SHAPE, "encoder_submit_host: n_images %d", n_images);
   cudaSetDevice(ctx->device);
   const sam3_encoder_config_t& c = ctx->cfg;
   const int B = c.max_batch;
@@ -260,26 +260,43 @@ sam3_status_t sam3_encoder_forward_host_pipelined(sam3_ctx_t* ctx, const uint16_
   sam3_status_t st;
   if (!ctx->copy_stream) {
     if ((st = check_cuda(ctx, cudaStreamCreateWithFlags(&ctx->copy_stream, cudaStreamNonBlocking),
-                         "copy stream")) != SAM3_OK)
+                         "upload stream")) != SAM3_OK ||
+        (st = check_cuda(ctx, cudaStreamCreateWithFlags(&ctx->down_stream, cudaStreamNonBlocking),
+                         "download stream")) != SAM3_OK ||
+        (st = check_cuda(ctx, cudaHostAlloc(&ctx->pipe_err, sizeof(int) * ctx->kPipeTickets,
+                                            cudaHostAllocDefault),
+                         "pinned error words")) != SAM3_OK)
       return st;
     for (cudaEvent_t& e : ctx->pipe_ev)
       if ((st = check_cuda(ctx, cudaEventCreateWithFlags(&e, cudaEventDisableTiming),
                            "pipeline event")) != SAM3_OK)
         return st;
+    for (cudaEvent_t& e : ctx->pipe_done)
+      if ((st = check_cuda(ctx, cudaEventCreateWithFlags(&e, cudaEventDisableTiming),
+                           "pipeline event")) != SAM3_OK)
+        return st;
   }
+  const cudaStream_t up = ctx->copy_stream, down = ctx->down_stream;
+  // on an error after the first copy, nothing may still be in flight against
+  // the caller's host buffers when this returns
+  auto drain = [&](sam3_status_t s) {
+    cudaStreamSynchronize(up);
+    cudaStreamSynchronize(ctx->stream);
+    cudaStreamSynchronize(down);
+    return s;
+  };
   if (ctx->pipe_bytes < 2 * set_bytes && (ctx->fault & SAM3_FAULT_ALLOC))
-    return set_error(ctx, SAM3_ERR_OOM, "encoder_host_pipelined: injected allocation failure");
+    return set_error(ctx, SAM3_ERR_OOM, "encoder_submit_host: injected allocation failure");
   if (ctx->pipe_bytes < 2 * set_bytes) {
     if (ctx->pipe_mem) {
-      cudaStreamSynchronize(ctx->copy_stream);
-      cudaStreamSynchronize(ctx->stream);
+      drain(SAM3_OK);
       cudaFree(ctx->pipe_mem);
       ctx->pipe_mem = nullptr;
       ctx->pipe_bytes = 0;
     }
     if (cudaMalloc(&ctx->pipe_mem, 2 * set_bytes) != cudaSuccess) {
       cudaGetLastError();
-      return set_error(ctx, SAM3_ERR_OOM, "encoder_host_pipelined: %zu bytes of staging",
+      return set_error(ctx, SAM3_ERR_OOM, "encoder_submit_host: %zu bytes of staging",
                        2 * set_bytes);
     }
     ctx->pipe_bytes = 2 * set_bytes;
@@ -297,35 +314,33 @@ sam3_status_t sam3_encoder_forward_host_pipelined(sam3_ctx_t* ctx, const uint16_
   cudaEvent_t* img_free = ctx->pipe_ev + 2;  // the encoder has finished with them
   cudaEvent_t* out_ready = ctx->pipe_ev + 4; // chunk's features are staged
   cudaEvent_t* out_done = ctx->pipe_ev + 6;  // and copied to the host
-  const cudaStream_t cs = ctx->copy_stream;
   const int chunks = (n_images + B - 1) / B;
+  const uint64_t g0 = ctx->pipe_chunks;  // global number of this call's first chunk
   auto count = [&](int ch) { return std::min(B, n_images - ch * B); };
-  // Issue order upload(c+1), encoder(c), download(c): on the copy stream the
-  // next chunk's images go ahead of this chunk's features, so both copies run
-  // under the encoder of chunk c+1 / c.
+  // Three streams: uploads, the encoder (ctx->stream) and downloads. Staging
+  // set g & 1 is reused by chunk g + 2, so chunk g's upload waits until the
+  // encoder of chunk g - 2 has read its images, and its encoder until the
+  // download of chunk g - 2 has drained its features. Nothing else orders the
+  // streams, so a later call's upload runs under this call's encoder and this
+  // call's download under the later call's encoder.
   auto upload = [&](int ch) -> sam3_status_t {
-    const int b = ch & 1;
-    if (ch >= 2) cudaStreamWaitEvent(cs, img_free[b], 0);
+    const uint64_t g = g0 + ch;
+    const int b = (int)(g & 1);
+    if (g >= 2) cudaStreamWaitEvent(up, img_free[b], 0);
     sam3_status_t s = check_cuda(
         ctx, cudaMemcpyAsync(img[b], host_image + (size_t)ch * B * img_elems,
-                             (size_t)count(ch) * img_elems * 2, cudaMemcpyHostToDevice, cs),
-        "pipelined image upload");
-    if (s == SAM3_OK) s = check_cuda(ctx, cudaEventRecord(in_done[b], cs), "event");
-    return s;
-  };
-  // on an error after the first copy, nothing may still be in flight against
-  // the caller's host buffers when this returns
-  auto drain = [&](sam3_status_t s) {
-    cudaStreamSynchronize(cs);
-    cudaStreamSynchronize(ctx->stream);
+                             (size_t)count(ch) * img_elems * 2, cudaMemcpyHostToDevice, up),
+        "image upload");
+    if (s == SAM3_OK) s = check_cuda(ctx, cudaEventRecord(in_done[b], up), "event");
     return s;
   };
   if ((st = upload(0)) != SAM3_OK) return drain(st);
   for (int ch = 0; ch < chunks; ++ch) {
-    const int b = ch & 1, nb = count(ch);
+    const uint64_t g = g0 + ch;
+    const int b = (int)(g & 1), nb = count(ch);
     if (ch + 1 < chunks && (st = upload(ch + 1)) != SAM3_OK) return drain(st);
     cudaStreamWaitEvent(ctx->stream, in_done[b], 0);
-    if (ch >= 2) cudaStreamWaitEvent(ctx->stream, out_done[b], 0);
+    if (g >= 2) cudaStreamWaitEvent(ctx->stream, out_done[b], 0);
     const uint16_t* out = nullptr;
     int r = 0;
     if ((st = encoder_run(ctx, img[b], false, nb, w, idx[b], &out, &r)) != SAM3_OK) return drain(st);
@@ -333,22 +348,61 @@ sam3_status_t sam3_encoder_forward_host_pipelined(sam3_ctx_t* ctx, const uint16_
     if ((st = check_cuda(ctx, cudaEventRecord(img_free[b], ctx->stream), "event")) != SAM3_OK ||
         (st = check_cuda(ctx, cudaMemcpyAsync(feats[b], out, fb, cudaMemcpyDeviceToDevice,
                                               ctx->stream),
-                         "pipelined feats staging")) != SAM3_OK ||
+                         "feats staging")) != SAM3_OK ||
         (st = check_cuda(ctx, cudaEventRecord(out_ready[b], ctx->stream), "event")) != SAM3_OK)
       return drain(st);
-    cudaStreamWaitEvent(cs, out_ready[b], 0);
+    cudaStreamWaitEvent(down, out_ready[b], 0);
     if ((st = check_cuda(ctx, cudaMemcpyAsync(host_feats + (size_t)ch * B * r * c.embed_dim,
-                                              feats[b], fb, cudaMemcpyDeviceToHost, cs),
-                         "pipelined feats download")) != SAM3_OK ||
+                                              feats[b], fb, cudaMemcpyDeviceToHost, down),
+                         "feats download")) != SAM3_OK ||
         (st = check_cuda(ctx, cudaMemcpyAsync(host_idx + (size_t)ch * B * r, idx[b],
-                                              (size_t)nb * r * 4, cudaMemcpyDeviceToHost, cs),
-                         "pipelined idx download")) != SAM3_OK ||
-        (st = check_cuda(ctx, cudaEventRecord(out_done[b], cs), "event")) != SAM3_OK)
+                                              (size_t)nb * r * 4, cudaMemcpyDeviceToHost, down),
+                         "idx download")) != SAM3_OK ||
+        (st = check_cuda(ctx, cudaEventRecord(out_done[b], down), "event")) != SAM3_OK)
       return drain(st);
   }
-  if ((st = check_cuda(ctx, cudaStreamSynchronize(cs), "pipelined downloads")) != SAM3_OK)
-    return st;
-  return sam3_sync(ctx);
+  ctx->pipe_chunks = g0 + chunks;
+  // the device error word as the last chunk's encoder left it, then the
+  // ticket's event: both behind the last download
+  const uint64_t t = ++ctx->pipe_tickets;
+  const int slot = (int)(t % ctx->kPipeTickets);
+  if ((st = check_cuda(ctx, cudaMemcpyAsync(ctx->pipe_err + slot, ctx->dev_err, sizeof(int),
+                                            cudaMemcpyDeviceToHost, down),
+                       "error word download")) != SAM3_OK ||
+      (st = check_cuda(ctx, cudaEventRecord(ctx->pipe_done[slot], down), "event")) != SAM3_OK)
+    return drain(st);
+  *ticket = t;
+  return SAM3_OK;
+}
+
+sam3_status_t sam3_encoder_wait_host(sam3_ctx_t* ctx, uint64_t ticket) {
+  SAM3_CHECK_CTX(ctx);
+  if (ticket == 0 || ticket > ctx->pipe_tickets)
+    return set_error(ctx, SAM3_ERR_INVALID_ARG, "encoder_wait_host: ticket %llu not issued",
+                     (unsigned long long)ticket);
+  cudaSetDevice(ctx->device);
+  // The download stream runs submissions in order: a ticket older than the
+  // ones still held is complete once the oldest held one is.
+  const uint64_t oldest =
+      ctx->pipe_tickets > (uint64_t)ctx->kPipeTickets ? ctx->pipe_tickets - ctx->kPipeTickets + 1
+                                                      : 1;
+  const int slot = (int)(std::max(ticket, oldest) % ctx->kPipeTickets);
+  sam3_status_t st =
+      check_cuda(ctx, cudaEventSynchronize(ctx->pipe_done[slot]), "encoder_wait_host");
+  if (st != SAM3_OK) return st;
+  return device_error_status(ctx, ctx->pipe_err[slot]);
+}
+
+sam3_status_t sam3_encoder_forward_host_pipelined(sam3_ctx_t* ctx, const uint16_t* host_image,
+                                                  int32_t n_images,
+                                                  const sam3_encoder_weights_t* w,
+                                                  uint16_t* host_feats, int32_t* host_idx) {
+  uint64_t t = 0;
+  sam3_status_t st = sam3_encoder_submit_host(ctx, host_image, n_images, w, host_feats, host_idx, &t);
+  if (st != SAM3_OK) return st;
+  st = sam3_encoder_wait_host(ctx, t);
+  const sam3_status_t s2 = sam3_sync(ctx);  // reads and clears the device error word
+  return st != SAM3_OK ? st : s2;
 }
 
 }  // extern "C"

@@ -54,12 +54,22 @@ struct sam3_ctx {
   size_t block_rows = 0;        // rows the block scratch can hold (plain encoder)
   size_t token_rows = 0;        // rows with a class token per image (windowed encoder)
 
-  // Double-buffered staging of sam3_encoder_forward_host_pipelined, made on
-  // first use: two sets of (images, features, indices) and a copy stream.
-  cudaStream_t copy_stream = nullptr;
+  // Double-buffered staging of the host-buffer encoder submissions
+  // (sam3_encoder_submit_host and the calls built on it), made on first use:
+  // two sets of (images, features, indices), an upload and a download stream.
+  cudaStream_t copy_stream = nullptr;  // uploads
+  cudaStream_t down_stream = nullptr;  // downloads
   char* pipe_mem = nullptr;
   size_t pipe_bytes = 0;
   cudaEvent_t pipe_ev[8] = {};  // in_done[2], img_free[2], out_ready[2], out_done[2]
+  uint64_t pipe_chunks = 0;     // chunks issued so far; chunk g uses staging set g & 1
+  // Submission tickets (1, 2, ...): the last kPipeTickets keep an event on
+  // the download stream and a pinned copy of the device error word, both
+  // taken after the submission's last download.
+  static constexpr int kPipeTickets = 8;
+  uint64_t pipe_tickets = 0;
+  cudaEvent_t pipe_done[kPipeTickets] = {};
+  int* pipe_err = nullptr;      // pinned host [kPipeTickets]
 
   // Device-side stage timing (sam3_profile_enable / sam3_profile_read).
   struct ProfRecord {
@@ -84,6 +94,8 @@ sam3_status_t check_launch(sam3_ctx_t* ctx, const char* what);
 // For launches that return their error (cudaLaunchKernelEx).
 sam3_status_t check_launch_ret(sam3_ctx_t* ctx, cudaError_t e, const char* what);
 sam3_status_t check_cuda(sam3_ctx_t* ctx, cudaError_t e, const char* what);
+// Status for a value of the device error word (0: SAM3_OK), with the message.
+sam3_status_t device_error_status(sam3_ctx_t* ctx, int err);
 
 // Raise `kernel`'s dynamic shared-memory limit to `bytes` once per context:
 // the attribute belongs to the device, and each context is bound to one.

@@ -257,6 +257,22 @@ class ViTEncoder {
           "ViTEncoder.encodeHost");
   }
 
+  // The same, committed without waiting (SAM3MetalPipeline.swift:72-77, the
+  // encoder recorded into a command buffer and committed): returns a ticket;
+  // waitHost(ticket) is waitUntilCompleted (:79). Buffers stay owned by the
+  // caller and untouched until then.
+  uint64_t submitHost(const uint16_t* hostImages, int nImages, uint16_t* hostFeats,
+                      int32_t* hostIndices) {
+    uint64_t ticket = 0;
+    check(ctx_, sam3_encoder_submit_host(ctx_, hostImages, nImages, &w_, hostFeats, hostIndices,
+                                         &ticket),
+          "ViTEncoder.submitHost");
+    return ticket;
+  }
+  void waitHost(uint64_t ticket) {
+    check(ctx_, sam3_encoder_wait_host(ctx_, ticket), "ViTEncoder.waitHost");
+  }
+
  private:
   sam3_ctx_t* ctx_;
   sam3_encoder_weights_t w_;

@@ -120,6 +120,9 @@ SIGNATURES = {
     "sam3_windowed_encoder_forward_rgba": (_S, [_P, _P, _I, C.POINTER(WindowedEncoderWeights), _P]),
     "sam3_encoder_forward_host_pipelined": (_S, [_P, _P, _I, C.POINTER(EncoderWeights), _P, _P]),
     "sam3_encoder_forward_host": (_S, [_P, _P, _I, C.POINTER(EncoderWeights), _P, _P]),
+    "sam3_encoder_submit_host": (_S, [_P, _P, _I, C.POINTER(EncoderWeights), _P, _P,
+                                      C.POINTER(C.c_uint64)]),
+    "sam3_encoder_wait_host": (_S, [_P, C.c_uint64]),
     "sam3_encoder_out_tokens": (C.c_int32, [_P]),
     "sam3_selftest_wait_timeout": (_S, [_P]),
     "sam3_set_fault": (_S, [_P, _I]),
@@ -202,6 +205,7 @@ class Context:
         self.handle = h.value
         self.config = cfg
         self._buffers: set[DeviceBuffer] = set()
+        self._in_flight: dict[int, tuple] = {}  # ticket -> host buffers of a submission
 
     # ---- plumbing ---------------------------------------------------------
     def _check(self, st: int):
@@ -410,6 +414,25 @@ class Context:
         img, feats, idx = self._host_io(n_images, image_host, feats_host, idx_host)
         self._check(lib.sam3_encoder_forward_host_pipelined(self.handle, img, n_images,
                                                             C.byref(w), feats, idx))
+
+    def encoder_submit_host(self, image_host, n_images, w: EncoderWeights, feats_host,
+                            idx_host) -> int:
+        """Enqueue n_images from host buffers (as for encoder_forward_host_pipelined)
+        and return the submission's ticket at once; the buffers must stay alive
+        and the outputs unread until encoder_wait_host(ticket)."""
+        img, feats, idx = self._host_io(n_images, image_host, feats_host, idx_host)
+        t = C.c_uint64(0)
+        self._check(lib.sam3_encoder_submit_host(self.handle, img, n_images, C.byref(w), feats,
+                                                 idx, C.byref(t)))
+        # the buffers stay referenced until their ticket has been waited for
+        self._in_flight[int(t.value)] = (image_host, feats_host, idx_host)
+        return int(t.value)
+
+    def encoder_wait_host(self, ticket: int):
+        """Block until submission `ticket` (and every earlier one) is on the host."""
+        self._check(lib.sam3_encoder_wait_host(self.handle, ticket))
+        for t in [t for t in self._in_flight if t <= ticket]:
+            del self._in_flight[t]
 
     @property
     def out_tokens(self) -> int:

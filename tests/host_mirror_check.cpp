@@ -28,6 +28,16 @@ int main() {
   } catch (const sam3::SAM3Error& e) {
     caught += e.status == SAM3_ERR_INVALID_ARG;
   }
+  try {
+    enc.submitHost(nullptr, 1, nullptr, nullptr);
+  } catch (const sam3::SAM3Error& e) {
+    caught += e.status == SAM3_ERR_INVALID_ARG;
+  }
+  try {
+    enc.waitHost(1);
+  } catch (const sam3::SAM3Error& e) {
+    caught += e.status == SAM3_ERR_INVALID_ARG;
+  }
   sam3_windowed_encoder_weights_t ww{};
   sam3::SAM3Encoder wenc(nullptr, ww);
   try {
@@ -53,7 +63,7 @@ int main() {
   const bool no_ctx = sam3_set_fault(nullptr, SAM3_FAULT_ALLOC) == SAM3_ERR_INVALID_ARG &&
                       sam3_selftest_wait_timeout(nullptr) == SAM3_ERR_INVALID_ARG &&
                       sam3_get_fault(nullptr) == 0;
-  std::printf("caught %d of 6, embed_dim %d, no-context checks %s\n", caught, cfg.embed_dim,
+  std::printf("caught %d of 8, embed_dim %d, no-context checks %s\n", caught, cfg.embed_dim,
               no_ctx ? "ok" : "failed");
-  return caught == 6 && recycled.empty() && no_ctx ? 0 : 1;
+  return caught == 8 && recycled.empty() && no_ctx ? 0 : 1;
 }

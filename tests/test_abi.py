@@ -96,4 +96,4 @@ def test_cpp_operator_mirror_compiles_and_throws(tmp_path):
     assert r.returncode == 0, r.stderr
     r = subprocess.run([exe], capture_output=True, text=True, timeout=60)
     assert r.returncode == 0, r.stdout + r.stderr
-    assert "caught 6 of 6" in r.stdout
+    assert "caught 8 of 8" in r.stdout

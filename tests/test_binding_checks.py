@@ -18,6 +18,7 @@ def fake_ctx(sam3, monkeypatch):
     ctx.config = sam3.default_config(embed_dim=256, num_heads=4, mlp_hidden=512, num_blocks=2,
                                      image_size=112, prune_after_block=1, keep_tokens=32)
     ctx._buffers = set()
+    ctx._in_flight = {}
     monkeypatch.setattr(sam3.Context, "out_tokens", property(lambda self: 32))
     return ctx
 
@@ -43,7 +44,8 @@ def _io(n=2):
             np.empty((n, 32), np.int32))
 
 
-@pytest.mark.parametrize("entry", ["encoder_forward_host", "encoder_forward_host_pipelined"])
+@pytest.mark.parametrize("entry", ["encoder_forward_host", "encoder_forward_host_pipelined",
+                                   "encoder_submit_host"])
 def test_host_entry_points_check_their_buffers(sam3, fake_ctx, entry):
     call = getattr(fake_ctx, entry)
     w = sam3.EncoderWeights()
@@ -62,6 +64,11 @@ def test_host_entry_points_check_their_buffers(sam3, fake_ctx, entry):
     ro.setflags(write=False)
     with pytest.raises(ValueError, match="feats: host array is read-only"):
         call(img, 2, w, ro, idx)
+
+
+def test_wait_host_without_a_context_is_an_error(sam3, fake_ctx):
+    with pytest.raises(sam3.SAM3Error):
+        fake_ctx.encoder_wait_host(1)
 
 
 def test_host_tensors_are_checked_too(sam3, fake_ctx):

@@ -753,6 +753,36 @@ def test_encoder_host_pipelined_equals_per_call(ctx, sam3, oracle):
     assert np.array_equal(pi2, pi) and np.array_equal(pf2.view(np.uint16), pf.view(np.uint16))
 
 
+def test_encoder_submissions_overlap_and_equal_per_call(ctx, sam3, oracle):
+    # three submissions in flight at once (3, 1 and 2 images through max_batch
+    # 2, into separate host buffers), waited for out of order: each equals one
+    # sam3_encoder_forward_host call per chunk, bit for bit
+    blocks, pw, pb = _small_encoder(oracle)
+    w = _upload_encoder(ctx, sam3, blocks, pw, pb)
+    sizes = [3, 1, 2]
+    imgs = [oracle.gen_uniform(33, 80 + i, (n, 112, 112, 3), -1.0, 1.0) for i, n in enumerate(sizes)]
+    outs = [(np.full((n, 32, 256), np.nan, F16), np.full((n, 32), -1, np.int32)) for n in sizes]
+    tickets = [ctx.encoder_submit_host(im, n, w, f, i)
+               for im, n, (f, i) in zip(imgs, sizes, outs)]
+    assert tickets == sorted(tickets) and len(set(tickets)) == 3
+    ctx.encoder_wait_host(tickets[1])   # covers tickets[0] too
+    ctx.encoder_wait_host(tickets[2])
+    ctx.encoder_wait_host(tickets[0])   # already complete: returns at once
+    with pytest.raises(sam3.SAM3Error):
+        ctx.encoder_wait_host(tickets[2] + 1)  # not issued
+    with pytest.raises(sam3.SAM3Error):
+        ctx.encoder_wait_host(0)
+    ctx.sync()
+    for im, n, (pf, pi) in zip(imgs, sizes, outs):
+        for c0 in range(0, n, 2):
+            m = min(2, n - c0)
+            hf = np.empty((m, 32, 256), F16)
+            hi = np.empty((m, 32), np.int32)
+            ctx.encoder_forward_host(np.ascontiguousarray(im[c0:c0 + m]), m, w, hf, hi)
+            assert np.array_equal(pi[c0:c0 + m], hi)
+            assert np.array_equal(pf[c0:c0 + m].view(np.uint16), hf.view(np.uint16))
+
+
 def test_encoder_full_size_two_blocks_matches_oracle(sam3, oracle):
     # 1008^2 image, full width (1024, 16 heads, 4096), two blocks with the
     # prune (to 2592 tokens by L2 norm) between them.
