@@ -838,8 +838,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(WS_THREADS, 1)
 // 256-row M tiles accumulating in their own TMEM buffers (4 x 128 columns:
 // groups alternate between accumulator pairs, so the epilogue of one group,
 // run by four epilogue warps of its own, overlaps the next group's MMAs).
-// Each pair keeps one N tile (palette staged once, 32 KB) and the pairs of a
-// "set" sweep the M groups in lockstep.
+// Each pair keeps one N tile (palette staged once, 32 KB); the pairs of a
+// "set" share one contiguous range of M tiles, the ranges of the sets
+// differing by at most one tile, taken two at a time (the last group of a
+// range may hold one). Interleaving whole groups over the sets instead left
+// up to a quarter of the pairs idle in the last round (81 groups over 18
+// sets at M = 41472).
 // ============================================================================
 constexpr int WSC_KC = 384;
 constexpr int WSC_KB_PER_CHUNK = WSC_KC / WS_BK;                    // 6
@@ -867,9 +871,8 @@ struct WscArgs {
   int chunks;   // ceil(K / 512); the last chunk may hold fewer k-blocks
   int kblocks;  // K / 64 (even)
   int m_tiles;  // 256-row pair tiles
-  int groups;   // ceil(m_tiles / 2)
   int n_tiles;  // n / 128
-  int sets;     // pairs / n_tiles
+  int sets;     // pairs / n_tiles, at most m_tiles
   int a3d;      // as WsArgs::a3d
 };
 
@@ -923,11 +926,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(WSC_THREADS, 1)
   const uint32_t tmem = *tmem_slot;
   griddep_launch_dependents();
 
-  // Pair p owns N tile p % n_tiles and M groups p / n_tiles + k * sets: the
-  // n_tiles pairs of a set sweep the same A groups together (one DRAM read,
-  // the other N tiles hit L2) and each pair stages its palette once.
+  // Pair p owns N tile p % n_tiles and set p / n_tiles's M tiles
+  // [m_lo, m_hi): the n_tiles pairs of a set sweep the same A rows together
+  // (one DRAM read, the other N tiles hit L2) and each pair stages its
+  // palette once. Groups are WSC_GROUP tiles from m_lo; the last may be short.
   const int pair = blockIdx.x >> 1;
   const int my_n = pair % wa.n_tiles, my_set = pair / wa.n_tiles;
+  const int m_lo = (int)((long long)my_set * wa.m_tiles / wa.sets);
+  const int m_hi = (int)((long long)(my_set + 1) * wa.m_tiles / wa.sets);
   const int chunks = wa.chunks;
 
   if (warp == 0) {
@@ -938,10 +944,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(WSC_THREADS, 1)
       int s = 0;
       uint32_t ph = 0;
       bool ok = true;
-      for (int g = my_set; g < wa.groups && ok; g += wa.sets) {
+      for (int mt = m_lo; mt < m_hi && ok; mt += WSC_GROUP) {
+        const int gs = min(WSC_GROUP, m_hi - mt);
         for (int c = 0; c < chunks && ok; ++c)
-          for (int t = 0; t < WSC_GROUP && ok; ++t) {
-            const int row = (g * WSC_GROUP + t) * 2 * WS_BM + (int)rank * WS_BM;
+          for (int t = 0; t < gs && ok; ++t) {
+            const int row = (mt + t) * 2 * WS_BM + (int)rank * WS_BM;
             const int steps = min(WSC_KB_PER_CHUNK, wa.kblocks - c * WSC_KB_PER_CHUNK) / WS_KSPLIT;
             for (int ks = 0; ks < steps; ++ks) {
               if (!mbar_wait_cluster(bar_a_empty + 8 * s, ph ^ 1, abort_flag, args.err,
@@ -973,8 +980,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(WSC_THREADS, 1)
       int s = 0, it = 0, q = 0;
       uint32_t ph = 0;
       bool issued_any = false, ok = true;
-      for (int g = my_set; g < wa.groups && ok; g += wa.sets, ++it) {
-        const int gp = it & 1;
+      for (int mt = m_lo; mt < m_hi && ok; mt += WSC_GROUP, ++it) {
+        const int gp = it & 1, gs = min(WSC_GROUP, m_hi - mt);
         if (!mbar_wait_cluster(bar_tempty + 8 * gp, ((uint32_t)(it >> 1) & 1u) ^ 1u, abort_flag,
                                args.err, kDevErrTimeoutMma))
           break;
@@ -988,7 +995,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(WSC_THREADS, 1)
           }
           tc_fence_after();
           const int steps = min(WSC_KB_PER_CHUNK, wa.kblocks - c * WSC_KB_PER_CHUNK) / WS_KSPLIT;
-          for (int t = 0; t < WSC_GROUP && ok; ++t) {
+          for (int t = 0; t < gs && ok; ++t) {
             const uint32_t d_tmem = tmem + (uint32_t)((2 * gp + t) * WS_ACC_COLS);
             for (int ks = 0; ks < steps; ++ks) {
               if (!mbar_wait_cluster(bar_a_full + 8 * s, ph, abort_flag, args.err,
@@ -1034,14 +1041,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(WSC_THREADS, 1)
     int it = 0;
     bool ok = true;
     griddep_wait();  // the residual is the previous kernel's output
-    for (int g = my_set; g < wa.groups && ok; g += wa.sets, ++it) {
-      const int gp = it & 1;
-      const int row0 = g * WSC_GROUP * 2 * WS_BM + (int)rank * WS_BM + quad * 32 + lane;
+    for (int mt = m_lo; mt < m_hi && ok; mt += WSC_GROUP, ++it) {
+      const int gp = it & 1, gs = min(WSC_GROUP, m_hi - mt);
+      const int row0 = mt * 2 * WS_BM + (int)rank * WS_BM + quad * 32 + lane;
 #pragma unroll
       for (int t = 0; t < WSC_GROUP; ++t)
 #pragma unroll
         for (int ch = 0; ch < 2; ++ch)
-          epilogue_prefetch(args, row0 + t * 2 * WS_BM, my_n * 2 * WS_BN + ch * 64);
+          if (t < gs) epilogue_prefetch(args, row0 + t * 2 * WS_BM, my_n * 2 * WS_BN + ch * 64);
       const int rpos0 = rope_pos_of(args, row0), rpos1 = rope_pos_of(args, row0 + 2 * WS_BM);
       ok = __all_sync(0xffffffffu,
                       mbar_wait_cluster(bar_tfull + 8 * gp, (uint32_t)(it >> 1) & 1u, abort_flag,
@@ -1049,7 +1056,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(WSC_THREADS, 1)
       if (!ok) break;
       tc_fence_after();
 #pragma unroll 1
-      for (int t = 0; t < WSC_GROUP; ++t) {
+      for (int t = 0; t < gs; ++t) {
         const int row = row0 + t * 2 * WS_BM;
         const int rpos = t == 0 ? rpos0 : rpos1;
 #pragma unroll 1
@@ -1061,7 +1068,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(WSC_THREADS, 1)
           tmem_ld_32x32b_x32(taddr, *reinterpret_cast<uint32_t(*)[32]>(v));
           tmem_ld_32x32b_x32(taddr + 32u, *reinterpret_cast<uint32_t(*)[32]>(v + 32));
           tmem_wait_ld();
-          if (t == WSC_GROUP - 1 && ch == 1) {  // the accumulator pair is free again
+          if (t == gs - 1 && ch == 1) {  // the accumulator pair is free again
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive_cluster(mapa_shared(bar_tempty + 8 * gp, 0));
@@ -1081,7 +1088,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(WSC_THREADS, 1)
     uint32_t pal_ph = 0;
     int cur_n = -1, q = 0;
     bool ok = true;
-    for (int g = my_set; g < wa.groups && ok; g += wa.sets) {
+    for (int mt = m_lo; mt < m_hi && ok; mt += WSC_GROUP) {
       const int n_tile = my_n;
       const int wrow = n_tile * 2 * WS_BN + (int)rank * WS_BN + exp_row;
       if (n_tile != cur_n) {
@@ -1126,7 +1133,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(WSC_THREADS, 1)
         for (int i = 0; i < N16; ++i) iv[i] = iv_next[i];
         // the next chunk: c + 1 of this group, or chunk 0 of the pair's next
         // group (same weight rows)
-        const int cn = c + 1 < chunks ? c + 1 : (g + wa.sets < wa.groups ? 0 : -1);
+        const int cn = c + 1 < chunks ? c + 1 : (mt + WSC_GROUP < m_hi ? 0 : -1);
         if (cn >= 0 && full(cn))
           ws_load_idx<N16>(irow, cn * WSC_KC + exp_q * (WSC_KC / 4), iv_next);
         if (q >= 2) {
@@ -1356,10 +1363,9 @@ sam3_status_t gemm_palette(sam3_ctx_t* ctx, const uint16_t* x, int m, int k, con
     wa.kblocks = k / WS_BK;
     wa.chunks = (k + WSC_KC - 1) / WSC_KC;
     wa.m_tiles = (m + 2 * WS_BM - 1) / (2 * WS_BM);
-    wa.groups = (wa.m_tiles + WSC_GROUP - 1) / WSC_GROUP;
     wa.n_tiles = n / (2 * WS_BN);
     wa.sets = (ctx->num_sms / 2) / wa.n_tiles;
-    if (wa.sets > wa.groups) wa.sets = wa.groups;
+    if (wa.sets > wa.m_tiles) wa.sets = wa.m_tiles;
     CUtensorMap ma3;
     wa.a3d = make_map_a3d(&ma3, x, k, m) ? 1 : 0;
     return launch_wsc(ctx, wa.a3d ? ma3 : ma, wa);

@@ -166,10 +166,11 @@ def test_linear_many_tiles_gelu_and_rope(ctx, sam3, oracle):
     assert max_rel_err(y2, ref2) < 2e-3
 
 
-@pytest.mark.parametrize("m,n,k", [(300, 256, 2048), (700, 512, 1536)])
+@pytest.mark.parametrize("m,n,k", [(300, 256, 2048), (700, 512, 1536), (20736, 1024, 4096)])
 def test_linear_chunked_k(ctx, sam3, oracle, m, n, k):
-    # K > 1024 takes the chunked weight-stationary kernel; 300 rows leave the
-    # second M tile of the only group entirely out of range
+    # K > 1024 takes the chunked weight-stationary kernel; 300 rows give two
+    # sets of one M tile each; 20736 (8 images after pruning, fc2) gives 81 M
+    # tiles over 18 sets, ranges of 4 and 5 tiles ending in one-tile groups
     x = oracle.gen_normal(16, m, (m, k))
     idx = oracle.gen_u8(16, 2, (n, k))
     pal = oracle.gen_palette(16, 3, n)
