@@ -552,8 +552,11 @@ struct WsArgs {
   int m_tiles;  // 256-row pair tiles
   int n_tiles;  // n / 128
   int units;    // n_tiles * m_tiles
-  int sets;     // > 0: pair p owns N tile p % n_tiles and M tiles p / n_tiles + k * sets;
+  int sets;     // > 0: pair p < sets * n_tiles owns N tile p % n_tiles and M tiles
+                // p / n_tiles + k * sets below m_a; the pairs after them share the
+                // N-major units of M tiles [m_a, m_tiles) in contiguous ranges;
                 // 0: pair p owns a contiguous range of N-major units
+  int m_a;      // sets > 0: M tiles swept by the sets (the rest go to the extra pairs)
   int a3d;      // 1: the A map is 3-D (one request per A stage), 0: 2-D boxes
 };
 
@@ -561,9 +564,19 @@ struct WsArgs {
 __device__ __forceinline__ bool ws_unit(const WsArgs& wa, int pair, int npairs, int k, int& n_tile,
                                         int& m_tile) {
   if (wa.sets > 0) {
-    n_tile = pair % wa.n_tiles;
-    m_tile = pair / wa.n_tiles + k * wa.sets;
-    return m_tile < wa.m_tiles;
+    const int set_pairs = wa.sets * wa.n_tiles;
+    if (pair < set_pairs) {
+      n_tile = pair % wa.n_tiles;
+      m_tile = pair / wa.n_tiles + k * wa.sets;
+      return m_tile < wa.m_a;
+    }
+    const int mb = wa.m_tiles - wa.m_a, e = pair - set_pairs, extra = npairs - set_pairs;
+    const long long units_b = (long long)mb * wa.n_tiles;
+    const int u = (int)(e * units_b / extra) + k;
+    if (u >= (int)((e + 1) * units_b / extra)) return false;
+    n_tile = u / mb;
+    m_tile = wa.m_a + u % mb;
+    return true;
   }
   const int u = (int)((long long)pair * wa.units / npairs) + k;
   if (u >= (int)((long long)(pair + 1) * wa.units / npairs)) return false;
@@ -1236,12 +1249,37 @@ bool make_map_a3d(CUtensorMap* map, const void* x, int k, int m) {
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// The pairs left over by the sets (max_pairs - sets * n_tiles of them) take
+// the last M tiles for every N tile, in contiguous N-major ranges. Returns
+// m_a, the M tiles left to the sets: a multiple of `sets` (or all of them)
+// that minimises the busier side, counting units (one 256-row M tile by one
+// weight slab) for the sets and units plus slab changes for the extra pairs
+// (a change drains the MMAs and re-expands a 128 KB slab: about 1.5 units).
+int ws_split_m(int m_tiles, int n_tiles, int sets, int max_pairs) {
+  const int extra = max_pairs - sets * n_tiles;
+  int best = m_tiles;
+  long long best_cost = 2LL * ((m_tiles + sets - 1) / sets);
+  if (extra <= 0) return best;
+  for (int m_a = (m_tiles / sets) * sets; m_a >= sets; m_a -= sets) {
+    const int mb = m_tiles - m_a;
+    if (mb == 0) continue;
+    const long long u = ((long long)mb * n_tiles + extra - 1) / extra;  // per extra pair
+    const long long changes = (u + mb - 1) / mb;
+    const long long cost = std::max(2LL * (m_a / sets), 2 * u + 3 * changes);
+    if (cost < best_cost) {
+      best_cost = cost;
+      best = m_a;
+    }
+  }
+  return best;
+}
+
 sam3_status_t launch_ws(sam3_ctx_t* ctx, const CUtensorMap& ma, const WsArgs& wa) {
   sam3_status_t st = ensure_smem_attr(ctx, kSmemWs, gemm_ws_kernel, WS_SMEM_BYTES,
                                       "gemm_ws smem attribute");
   if (st != SAM3_OK) return st;
   const int max_pairs = ctx->num_sms / 2;
-  const int pairs = wa.sets > 0 ? wa.sets * wa.n_tiles
+  const int pairs = wa.sets > 0 ? (wa.m_a < wa.m_tiles ? max_pairs : wa.sets * wa.n_tiles)
                                 : (wa.units < max_pairs ? wa.units : max_pairs);
   return check_launch_ret(ctx, launch_pdl(gemm_ws_kernel, dim3(2 * pairs), dim3(WS_THREADS),
                                          WS_SMEM_BYTES, ctx->stream, ma, wa),
@@ -1350,6 +1388,7 @@ sam3_status_t gemm_palette(sam3_ctx_t* ctx, const uint16_t* x, int m, int k, con
                wa.m_tiles >= 2 * sets)
                   ? sets
                   : 0;
+    wa.m_a = wa.sets > 0 ? ws_split_m(wa.m_tiles, wa.n_tiles, wa.sets, max_pairs) : wa.m_tiles;
     CUtensorMap ma3;
     wa.a3d = make_map_a3d(&ma3, x, k, m) ? 1 : 0;
     return launch_ws(ctx, wa.a3d ? ma3 : ma, wa);

@@ -204,12 +204,13 @@ def test_linear_batch8_shapes_deterministic(ctx_full, sam3, oracle, n, k, epi):
         ctx.sync()
         outs.append(ctx.download(dy, (m, n), F16))
     assert np.array_equal(outs[0].view(np.uint16), outs[1].view(np.uint16))
-    rows = np.r_[0:256, m // 2:m // 2 + 256, m - 256:m]
-    ref = oracle.linear(x[rows], idx, pal, bias, epilogue=epi,
-                        residual=res[rows] if res is not None else None,
-                        rope=table[rows % 5184] if table is not None else None,
-                        rope_period=len(rows), heads=16, head_dim=64)
-    assert max_rel_err(outs[0][rows], ref) < 2e-3
+    # every row: the schedule splits the M tiles between the sets and the
+    # pairs left over (fc1: the last 20 of 162 tiles go to the extra pairs)
+    ref = oracle.linear(x, idx, pal, bias, epilogue=epi, residual=res, rope=table,
+                        rope_period=5184, heads=16, head_dim=64)
+    assert max_rel_err(outs[0], ref) < 2e-3
+    tiles = [max_rel_err(outs[0][r:r + 256], ref[r:r + 256]) for r in range(0, m, 256)]
+    assert max(tiles) < 2e-3
 
 
 def test_encoder_batch8_deterministic(sam3, oracle):
