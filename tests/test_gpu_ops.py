@@ -1027,6 +1027,47 @@ def test_injected_faults_propagate_and_clear(ctx, sam3, oracle):
     assert max_rel_err(ctx.download(feats, (2, 32, 256), F16), ref_f) < SPEC_TOL
 
 
+def test_encoder_submit_errors_leave_nothing_in_flight(sam3, oracle):
+    # A submission that fails (injected staging allocation failure on a fresh
+    # context; injected launch failure after its uploads were queued) returns
+    # the error with every stream drained and issues no ticket; the next
+    # submission works.
+    with sam3.Context(0, embed_dim=256, num_heads=4, mlp_hidden=512, num_blocks=2, patch=14,
+                      image_size=112, prune_after_block=1, keep_tokens=32, max_batch=2) as ctx:
+        blocks, pw, pb = _small_encoder(oracle)
+        w = _upload_encoder(ctx, sam3, blocks, pw, pb)
+        img = oracle.gen_uniform(34, 77, (3, 112, 112, 3), -1.0, 1.0)
+        hf = np.full((3, 32, 256), np.nan, F16)
+        hi = np.full((3, 32), -1, np.int32)
+        try:
+            ctx.fault = sam3.FAULT_ALLOC
+            with pytest.raises(sam3.SAM3Error) as e:
+                ctx.encoder_submit_host(img, 3, w, hf, hi)
+            assert e.value.status == sam3.ERR_OOM and "injected" in str(e.value)
+            ctx.fault = sam3.FAULT_NONE
+            t1 = ctx.encoder_submit_host(img, 3, w, hf, hi)
+            ctx.encoder_wait_host(t1)
+            ctx.fault = sam3.FAULT_LAUNCH
+            hf_bad = np.full((3, 32, 256), np.nan, F16)
+            hi_bad = np.full((3, 32), -1, np.int32)
+            with pytest.raises(sam3.SAM3Error) as e:
+                ctx.encoder_submit_host(img, 3, w, hf_bad, hi_bad)
+            assert e.value.status == sam3.ERR_CUDA and "injected launch failure" in str(e.value)
+            assert np.all(hi_bad == -1)  # nothing reached the failed call's buffers
+        finally:
+            ctx.fault = sam3.FAULT_NONE
+        ctx.sync()
+        hf2 = np.empty_like(hf)
+        hi2 = np.empty_like(hi)
+        t2 = ctx.encoder_submit_host(img, 3, w, hf2, hi2)
+        assert t2 == t1 + 1
+        ctx.encoder_wait_host(t2)
+        assert np.array_equal(hi2, hi) and np.array_equal(hf2.view(np.uint16), hf.view(np.uint16))
+        ref_f, ref_i = oracle.encoder_forward(img, blocks, pw, pb, heads=4, prune_after=1, keep=32)
+        assert np.array_equal(hi, ref_i)
+        assert max_rel_err(hf, ref_f) < SPEC_TOL
+
+
 def test_fault_environment_variable_sets_new_contexts(sam3, tmp_path):
     # SAM3_FAULT is read when a context is made (subprocess: a clean environment)
     import subprocess
