@@ -136,6 +136,29 @@ void gemm_nt(const float* A, int64_t m, const float* B, int64_t n, int64_t k, fl
   }
 }
 
+// e^x for 8 floats: x = n ln2 + r with n = round(x / ln2) and ln2 split in a
+// short high part and a low correction (Cody and Waite's reduction), e^r by
+// its Taylor series to degree 7 (|r| <= ln2 / 2, truncation under 6e-9
+// relative), 2^n added to the exponent field. x is clamped at -87 so the
+// result stays a normal float.
+inline __m256 exp8(__m256 x) {
+  x = _mm256_max_ps(x, _mm256_set1_ps(-87.0f));
+  const __m256 n = _mm256_round_ps(_mm256_mul_ps(x, _mm256_set1_ps(1.44269504088896341f)),
+                                   _MM_FROUND_TO_NEAREST_INT | _MM_FROUND_NO_EXC);
+  __m256 r = _mm256_fnmadd_ps(n, _mm256_set1_ps(0.693359375f), x);
+  r = _mm256_fnmadd_ps(n, _mm256_set1_ps(-2.12194440054690583e-4f), r);
+  __m256 p = _mm256_set1_ps(1.0f / 5040.0f);
+  p = _mm256_fmadd_ps(p, r, _mm256_set1_ps(1.0f / 720.0f));
+  p = _mm256_fmadd_ps(p, r, _mm256_set1_ps(1.0f / 120.0f));
+  p = _mm256_fmadd_ps(p, r, _mm256_set1_ps(1.0f / 24.0f));
+  p = _mm256_fmadd_ps(p, r, _mm256_set1_ps(1.0f / 6.0f));
+  p = _mm256_fmadd_ps(p, r, _mm256_set1_ps(0.5f));
+  p = _mm256_fmadd_ps(p, r, _mm256_set1_ps(1.0f));
+  p = _mm256_fmadd_ps(p, r, _mm256_set1_ps(1.0f));
+  const __m256i e = _mm256_slli_epi32(_mm256_cvtps_epi32(n), 23);
+  return _mm256_castsi256_ps(_mm256_add_epi32(_mm256_castps_si256(p), e));
+}
+
 // Rounding points (SO_ROUND_FUSED / SO_ROUND_GRAPH, see sam3_oracle.h).
 int g_rounding = SO_ROUND_FUSED;
 
@@ -438,12 +461,24 @@ void so_attention(const uint16_t* qkv, int batch, int64_t seq, int heads,
             gemm_nt_tile(qh, kh, seq, hd, S.data(), 0, rows, j0, std::min(seq, j0 + kNB),
                          pa.data(), pb.data());
           std::vector<float> l((size_t)rows);
+          const int64_t seq8 = seq / 8 * 8;
+          const __m256 vscale = _mm256_set1_ps(scale);
           for (int64_t r = 0; r < rows; ++r) {
             float* sr = S.data() + r * seq;
             float mx = -INFINITY;
             for (int64_t j = 0; j < seq; ++j) mx = std::max(mx, sr[j] * scale);
-            float sum = 0.f;
-            for (int64_t j = 0; j < seq; ++j) {
+            // exponentials 8 at a time, 8 partial sums
+            const __m256 vmx = _mm256_set1_ps(mx);
+            __m256 vsum = _mm256_setzero_ps();
+            for (int64_t j = 0; j < seq8; j += 8) {
+              const __m256 p = exp8(_mm256_fmsub_ps(_mm256_loadu_ps(sr + j), vscale, vmx));
+              _mm256_storeu_ps(sr + j, p);
+              vsum = _mm256_add_ps(vsum, p);
+            }
+            alignas(32) float ps[8];
+            _mm256_store_ps(ps, vsum);
+            float sum = ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
+            for (int64_t j = seq8; j < seq; ++j) {
               sr[j] = std::exp(sr[j] * scale - mx);
               sum += sr[j];
             }
