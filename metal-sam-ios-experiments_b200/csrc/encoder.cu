@@ -258,24 +258,29 @@ sam3_status_t sam3_encoder_submit_host(sam3_ctx_t* ctx, const uint16_t* host_ima
   const size_t idx_bytes = ((size_t)B * rows * 4 + 255) / 256 * 256;
   const size_t set_bytes = img_bytes + feat_bytes + idx_bytes;
   sam3_status_t st;
-  if (!ctx->copy_stream) {
-    if ((st = check_cuda(ctx, cudaStreamCreateWithFlags(&ctx->copy_stream, cudaStreamNonBlocking),
-                         "upload stream")) != SAM3_OK ||
-        (st = check_cuda(ctx, cudaStreamCreateWithFlags(&ctx->down_stream, cudaStreamNonBlocking),
-                         "download stream")) != SAM3_OK ||
-        (st = check_cuda(ctx, cudaHostAlloc(&ctx->pipe_err, sizeof(int) * ctx->kPipeTickets,
-                                            cudaHostAllocDefault),
-                         "pinned error words")) != SAM3_OK)
+  // streams, events and pinned words, made on first use; whatever a failed
+  // attempt made is kept (sam3_ctx_destroy frees it) and the rest retried
+  if (!ctx->copy_stream &&
+      (st = check_cuda(ctx, cudaStreamCreateWithFlags(&ctx->copy_stream, cudaStreamNonBlocking),
+                       "upload stream")) != SAM3_OK)
+    return st;
+  if (!ctx->down_stream &&
+      (st = check_cuda(ctx, cudaStreamCreateWithFlags(&ctx->down_stream, cudaStreamNonBlocking),
+                       "download stream")) != SAM3_OK)
+    return st;
+  if (!ctx->pipe_err &&
+      (st = check_cuda(ctx, cudaHostAlloc(&ctx->pipe_err, sizeof(int) * ctx->kPipeTickets,
+                                          cudaHostAllocDefault),
+                       "pinned error words")) != SAM3_OK)
+    return st;
+  for (cudaEvent_t& e : ctx->pipe_ev)
+    if (!e && (st = check_cuda(ctx, cudaEventCreateWithFlags(&e, cudaEventDisableTiming),
+                               "pipeline event")) != SAM3_OK)
       return st;
-    for (cudaEvent_t& e : ctx->pipe_ev)
-      if ((st = check_cuda(ctx, cudaEventCreateWithFlags(&e, cudaEventDisableTiming),
-                           "pipeline event")) != SAM3_OK)
-        return st;
-    for (cudaEvent_t& e : ctx->pipe_done)
-      if ((st = check_cuda(ctx, cudaEventCreateWithFlags(&e, cudaEventDisableTiming),
-                           "pipeline event")) != SAM3_OK)
-        return st;
-  }
+  for (cudaEvent_t& e : ctx->pipe_done)
+    if (!e && (st = check_cuda(ctx, cudaEventCreateWithFlags(&e, cudaEventDisableTiming),
+                               "pipeline event")) != SAM3_OK)
+      return st;
   const cudaStream_t up = ctx->copy_stream, down = ctx->down_stream;
   // on an error after the first copy, nothing may still be in flight against
   // the caller's host buffers when this returns
