@@ -1027,6 +1027,33 @@ def test_injected_faults_propagate_and_clear(ctx, sam3, oracle):
     assert max_rel_err(ctx.download(feats, (2, 32, 256), F16), ref_f) < SPEC_TOL
 
 
+def test_encoder_submissions_mixed_with_blocking_calls(ctx, sam3, oracle):
+    # blocking host calls issued while submissions are in flight, and more
+    # submissions than the tickets the context keeps events for (8): waiting
+    # for the oldest ticket still returns once it is on the host
+    blocks, pw, pb = _small_encoder(oracle)
+    w = _upload_encoder(ctx, sam3, blocks, pw, pb)
+    img = oracle.gen_uniform(35, 77, (10, 112, 112, 3), -1.0, 1.0)
+    outs = [(np.empty((1, 32, 256), F16), np.empty((1, 32), np.int32)) for _ in range(10)]
+    tickets = []
+    for i in range(10):
+        tickets.append(ctx.encoder_submit_host(np.ascontiguousarray(img[i:i + 1]), 1, w, *outs[i]))
+        if i == 4:
+            hf = np.empty((2, 32, 256), F16)
+            hi = np.empty((2, 32), np.int32)
+            ctx.encoder_forward_host(np.ascontiguousarray(img[:2]), 2, w, hf, hi)
+    ctx.encoder_wait_host(tickets[0])
+    ctx.encoder_wait_host(tickets[-1])
+    ctx.sync()
+    for i in range(10):
+        rf = np.empty((1, 32, 256), F16)
+        ri = np.empty((1, 32), np.int32)
+        ctx.encoder_forward_host(np.ascontiguousarray(img[i:i + 1]), 1, w, rf, ri)
+        assert np.array_equal(outs[i][1], ri)
+        assert np.array_equal(outs[i][0].view(np.uint16), rf.view(np.uint16))
+    assert np.array_equal(hi, np.concatenate([outs[0][1], outs[1][1]]))
+
+
 def test_encoder_submit_errors_leave_nothing_in_flight(sam3, oracle):
     # A submission that fails (injected staging allocation failure on a fresh
     # context; injected launch failure after its uploads were queued) returns
