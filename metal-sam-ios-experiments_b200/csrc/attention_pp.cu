@@ -246,28 +246,36 @@ __global__ void __launch_bounds__(THREADS, 2)
                                              args.err, kDevErrTimeoutAttn));
       if (!ok) break;
       tc_fence_after();
+      // The scores in two halves: the maximum of the first 64 runs while the
+      // second 64 are still on their way from tensor memory.
       uint32_t v[BKV];
+      const int valid = min(BKV, seq - j * BKV);  // only the last tile can be ragged
+      float mx[4];
+      auto half_max = [&](int q0) {
+        if (valid < BKV) {
 #pragma unroll
-      for (int q = 0; q < BKV / 32; ++q)
-        tmem_ld_32x32b_x32(s_col + q * 32, *reinterpret_cast<uint32_t(*)[32]>(v + 32 * q));
+          for (int e = 0; e < BKV / 2; ++e)
+            if (q0 * 32 + e >= valid) v[q0 * 32 + e] = __float_as_uint(-INFINITY);
+        }
+#pragma unroll
+        for (int q = q0; q < q0 + 2; ++q) {
+          float m = fmaxf(__uint_as_float(v[32 * q]), __uint_as_float(v[32 * q + 31]));
+#pragma unroll
+          for (int e = 1; e < 31; e += 2)
+            m = max3f(m, __uint_as_float(v[32 * q + e]), __uint_as_float(v[32 * q + e + 1]));
+          mx[q] = m;
+        }
+      };
+      tmem_ld_32x32b_x32(s_col, *reinterpret_cast<uint32_t(*)[32]>(v));
+      tmem_ld_32x32b_x32(s_col + 32, *reinterpret_cast<uint32_t(*)[32]>(v + 32));
+      tmem_wait_ld();
+      tmem_ld_32x32b_x32(s_col + 64, *reinterpret_cast<uint32_t(*)[32]>(v + 64));
+      tmem_ld_32x32b_x32(s_col + 96, *reinterpret_cast<uint32_t(*)[32]>(v + 96));
+      half_max(0);
       tmem_wait_ld();
       tc_fence_before();
       mbar_arrive(bar_s_free);  // the next Q K^T may overwrite S now
-      const int valid = min(BKV, seq - j * BKV);  // only the last tile can be ragged
-      if (valid < BKV) {
-#pragma unroll
-        for (int e = 0; e < BKV; ++e)
-          if (e >= valid) v[e] = __float_as_uint(-INFINITY);
-      }
-      float mx[4];
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        float m = fmaxf(__uint_as_float(v[32 * q]), __uint_as_float(v[32 * q + 31]));
-#pragma unroll
-        for (int e = 1; e < 31; e += 2)
-          m = max3f(m, __uint_as_float(v[32 * q + e]), __uint_as_float(v[32 * q + e + 1]));
-        mx[q] = m;
-      }
+      half_max(2);
       const float m_tile = max3f(fmaxf(mx[0], mx[1]), mx[2], mx[3]) * c;
       const bool grow = m_tile > m_run + kRescaleLog2;
       const float m_use = grow ? m_tile : m_run;
